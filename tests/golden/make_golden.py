@@ -1,0 +1,94 @@
+"""Generate the golden fixtures in this folder from the reference implementation itself.
+
+Run from the repository root in a container where the reference checkout is present:
+
+    python tests/golden/make_golden.py --reference /root/reference
+
+For every case in ``oracle/cases.py`` it runs the reference's own ``ssd_complex_chunkwise``
+(models/ssd_complex.py:58-119, ``ssd_dispatch="pytorch"``) on CPU, backpropagates
+``sum(dy * y)`` through it with torch.autograd, and stores outputs and gradients. Small cases store
+the full tensors together with their inputs; the B2 L256 H4 block-shape cases store the input checksums
+and a fixed random sample of 4096 entries per tensor (full tensors would be megabytes).
+Entries where the reference is not finite (its exp-then-mask overflow) are stored as NaN and are
+skipped by the tests.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from oracle.cases import CASES, SAMPLED_CASES, make_case  # noqa: E402
+
+N_SAMPLE = 4096
+
+
+def checksum(a):
+    a = np.asarray(a)
+    if np.iscomplexobj(a):
+        return np.array([np.abs(a.real).astype(np.float64).sum(), np.abs(a.imag).astype(np.float64).sum()])
+    return np.array([np.abs(a).astype(np.float64).sum(), 0.0])
+
+
+def run_reference(ssd_complex_chunkwise, inp, dy, chunk):
+    xs = [torch.from_numpy(np.ascontiguousarray(inp[k])).clone().requires_grad_(True)
+          for k in ("x", "A", "B_t", "C_t", "dt")]
+    y = ssd_complex_chunkwise(*xs, chunk_size=chunk, ssd_dispatch="pytorch")
+    (y * torch.from_numpy(dy)).sum().backward()
+    out = {"y": y.detach().numpy()}
+    for k, t in zip(("dx", "dA", "dB", "dC", "ddt"), xs):
+        out[k] = t.grad.detach().numpy()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", nargs="*")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from models.ssd_complex import ssd_complex_chunkwise  # the reference itself
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    for name in CASES:
+        if args.only and name not in args.only:
+            continue
+        inp, dy, chunk = make_case(name)
+        ref = run_reference(ssd_complex_chunkwise, inp, dy, chunk)
+        rec = {"chunk": np.int64(chunk)}
+        for k in ("x", "A", "B_t", "C_t", "dt"):
+            rec["sum_" + k] = checksum(inp[k])
+        rec["sum_dy"] = checksum(dy)
+        if name in SAMPLED_CASES:
+            rng = np.random.Generator(np.random.PCG64(1234))
+            for k, v in ref.items():
+                v = np.asarray(v)
+                if v.size > N_SAMPLE:
+                    idx = np.sort(rng.choice(v.size, N_SAMPLE, replace=False)).astype(np.int64)
+                else:
+                    idx = np.arange(v.size, dtype=np.int64)
+                rec["idx_" + k] = idx
+                rec[k] = v.reshape(-1)[idx]
+                rec["nonfinite_" + k] = np.float64(np.mean(~np.isfinite(v)))
+        else:
+            for k in ("x", "A", "B_t", "C_t", "dt"):
+                rec["in_" + k] = inp[k]
+            rec["in_dy"] = dy
+            for k, v in ref.items():
+                rec[k] = v
+                rec["nonfinite_" + k] = np.float64(np.mean(~np.isfinite(v)))
+        path = os.path.join(HERE, name + ".npz")
+        np.savez_compressed(path, **rec)
+        print(f"{name:16s} chunk={chunk:3d} nonfinite(y)={rec['nonfinite_y']:.3f} "
+              f"-> {os.path.getsize(path) / 1024:.1f} KiB")
+
+
+if __name__ == "__main__":
+    main()
