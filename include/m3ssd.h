@@ -1,0 +1,146 @@
+/*
+ * m3ssd - complex64 chunkwise SSD operator for NVIDIA B200 (sm_100a). Stable C ABI.
+ *
+ * The operator is the one of models/ssd_complex.py:58-119 (ssd_complex_chunkwise) in
+ * atandra2000/Mamba-3-Lite:
+ *
+ *   a[b,t,h]   = softplus(dt[b,t,h]) * A[h]                         (complex)
+ *   s_t        = exp(a_t) s_{t-1} + B_t x_t^T                        (state N x D, complex)
+ *   y[b,t,h,:] = Re( sum_n C[b,t,h,n] s_t[n,:] )                     (no conjugate on C)
+ *
+ * evaluated chunkwise with chunk length `chunk`. T need not be a multiple of `chunk` (the
+ * reference's zero padding, models/ssd_complex.py:72-80, never influences t < T).
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers on the current CUDA device, except the args structs.
+ *   - Strides are in ELEMENTS of the tensor's own element type (float for dt/dy and real x,
+ *     complex64 = two floats for A/B/C and complex x). Any strides are accepted; outputs are
+ *     written contiguous (row-major in the documented shape).
+ *   - `stream` is a cudaStream_t passed as void*; work is only enqueued, never synchronised.
+ *   - The library never allocates, frees or synchronises. Scratch is caller-provided, sized by
+ *     the *_bytes queries below. Calls are reentrant; concurrent calls need distinct scratch.
+ *   - Return value 0 is success; anything else is an m3ssd_status (see m3ssd_strerror).
+ *   - No CPU fallback exists: the only implementation is CUDA code built for sm_100a.
+ */
+#ifndef M3SSD_H_
+#define M3SSD_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M3SSD_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define M3SSD_API __attribute__((visibility("default")))
+#else
+#define M3SSD_API
+#endif
+
+typedef enum m3ssd_status {
+  M3SSD_OK = 0,
+  M3SSD_ERR_NULL = 1,          /* a required pointer is NULL */
+  M3SSD_ERR_SHAPE = 2,         /* a size is <= 0 or inconsistent */
+  M3SSD_ERR_CHUNK = 3,         /* chunk size outside [1, 256] */
+  M3SSD_ERR_DIM_LIMIT = 4,     /* head_dim or state_dim above 256 (same cap as the reference's
+                                  Triton wrapper, models/ssd_triton.py:27-28, 139-146) */
+  M3SSD_ERR_ALIGN = 5,         /* pointer not aligned to its element type */
+  M3SSD_ERR_WORKSPACE = 6,     /* scratch pointer NULL or smaller than required */
+  M3SSD_ERR_LAUNCH = 7,        /* a kernel launch failed (cudaGetLastError) */
+  M3SSD_ERR_DEVICE = 8,        /* current device is not sm_100 or cannot be queried */
+  M3SSD_ERR_FLAGS = 9,         /* unknown flag bits */
+  M3SSD_ERR_OVERFLOW = 10      /* a size product overflows the 64-bit index space */
+} m3ssd_status;
+
+/* problem flags */
+#define M3SSD_X_COMPLEX      0x1u   /* x (and dx) are complex64; otherwise float32 */
+#define M3SSD_PREC_AUTO      0x0u   /* fastest path supported for the shape */
+#define M3SSD_PREC_FP32      0x10u  /* fp32 CUDA-core arithmetic everywhere */
+#define M3SSD_PREC_TF32      0x20u  /* tf32 tensor-core tiles (tcgen05) where available */
+#define M3SSD_PREC_MASK      0x30u
+
+typedef struct m3ssd_problem {
+  int64_t batch;      /* B */
+  int64_t seqlen;     /* T */
+  int64_t nheads;     /* H */
+  int64_t headdim;    /* D */
+  int64_t dstate;     /* N */
+  int64_t chunk;      /* chunk length C */
+  uint32_t flags;     /* M3SSD_X_COMPLEX | one M3SSD_PREC_* */
+  uint32_t reserved;  /* must be 0 */
+} m3ssd_problem;
+
+typedef struct m3ssd_fwd_args {
+  m3ssd_problem prob;
+  const void* x;   int64_t x_strides[4];   /* (B,T,H,D) float32 or complex64 */
+  const void* A;                           /* (H,) complex64, contiguous */
+  const void* B;   int64_t b_strides[4];   /* (B,T,H,N) complex64 */
+  const void* C;   int64_t c_strides[4];   /* (B,T,H,N) complex64 */
+  const float* dt; int64_t dt_strides[3];  /* (B,T,H) float32, pre-softplus */
+  float* y;                                /* out: (B,T,H,D) float32 contiguous */
+  void* states;                            /* out: m3ssd_states_bytes() bytes; chunk-entry states
+                                              kept for m3ssd_bwd (layout internal) */
+  void* workspace;                         /* scratch, m3ssd_fwd_workspace_bytes() bytes */
+  size_t workspace_bytes;
+} m3ssd_fwd_args;
+
+typedef struct m3ssd_bwd_args {
+  m3ssd_problem prob;                      /* identical to the forward call */
+  const void* x;   int64_t x_strides[4];
+  const void* A;
+  const void* B;   int64_t b_strides[4];
+  const void* C;   int64_t c_strides[4];
+  const float* dt; int64_t dt_strides[3];
+  const float* dy; int64_t dy_strides[4];  /* (B,T,H,D) float32: gradient of y */
+  const void* states;                      /* from the matching m3ssd_fwd call */
+  void* dx;                                /* out: (B,T,H,D) float32 (complex64 if X_COMPLEX) */
+  void* dA;                                /* out: (H,) complex64 */
+  void* dB;                                /* out: (B,T,H,N) complex64 */
+  void* dC;                                /* out: (B,T,H,N) complex64 */
+  float* ddt;                              /* out: (B,T,H) float32 */
+  void* workspace;                         /* scratch, m3ssd_bwd_workspace_bytes() bytes */
+  size_t workspace_bytes;
+} m3ssd_bwd_args;
+
+/* ABI version of the loaded library (M3SSD_ABI_VERSION at build time). */
+M3SSD_API int m3ssd_abi_version(void);
+
+/* Human-readable text for a status code; never NULL. */
+M3SSD_API const char* m3ssd_strerror(int status);
+
+/* Validate a problem description without touching the device. Returns an m3ssd_status. */
+M3SSD_API int m3ssd_check_problem(const m3ssd_problem* prob);
+
+/* Bytes of the `states` buffer written by m3ssd_fwd and read by m3ssd_bwd (0 on bad input). */
+M3SSD_API size_t m3ssd_states_bytes(const m3ssd_problem* prob);
+/* Scratch bytes needed by m3ssd_fwd / m3ssd_bwd for this problem (0 on bad input). */
+M3SSD_API size_t m3ssd_fwd_workspace_bytes(const m3ssd_problem* prob);
+M3SSD_API size_t m3ssd_bwd_workspace_bytes(const m3ssd_problem* prob);
+
+/* Forward. Replaces the body of ssd_complex_chunkwise (models/ssd_complex.py:69-119) and the
+ * per-chunk kernel launch it dispatches to (models/ssd_triton.py:163-197). Writes y and states. */
+M3SSD_API int m3ssd_fwd(const m3ssd_fwd_args* args, void* stream);
+
+/* Backward. Replaces torch.autograd through models/ssd_complex.py:82-119 and the recompute
+ * backward of the per-chunk kernel (models/ssd_triton.py:210-225). Writes dx, dA, dB, dC, ddt in
+ * PyTorch's convention for complex tensors (grad = dL/dRe + i dL/dIm). dA is summed over
+ * batch and time. */
+M3SSD_API int m3ssd_bwd(const m3ssd_bwd_args* args, void* stream);
+
+/* Name of the implementation m3ssd_fwd would use for this problem ("tcgen05-tf32",
+ * "simt-fp32"). Host-only query, no device work. */
+M3SSD_API const char* m3ssd_fwd_path(const m3ssd_problem* prob);
+M3SSD_API const char* m3ssd_bwd_path(const m3ssd_problem* prob);
+
+/* Number of kernel launches one m3ssd_fwd (backward = 0) or m3ssd_bwd (backward = 1) call
+ * enqueues for this problem (0 on bad input). Host-only query. */
+M3SSD_API int m3ssd_launch_count(const m3ssd_problem* prob, int backward);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M3SSD_H_ */

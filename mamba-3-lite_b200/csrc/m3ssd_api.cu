@@ -1,0 +1,190 @@
+// C ABI of the m3ssd operator (declared in include/m3ssd.h): argument validation, path
+// selection and launch. No allocation, no synchronisation, no host-side compute fallback.
+#include <cuda_runtime.h>
+#include <limits.h>
+#include <stdint.h>
+
+#include "m3ssd.h"
+#include "m3ssd_common.cuh"
+#include "simt_path.h"
+
+using m3ssd::Problem;
+
+namespace {
+
+bool mul_ok(int64_t a, int64_t b, int64_t* out) {
+  if (a < 0 || b < 0) return false;
+  if (a != 0 && b > INT64_MAX / a) return false;
+  *out = a * b;
+  return true;
+}
+
+int check_problem(const m3ssd_problem* pr) {
+  if (!pr) return M3SSD_ERR_NULL;
+  if (pr->reserved != 0) return M3SSD_ERR_FLAGS;
+  const uint32_t known = M3SSD_X_COMPLEX | M3SSD_PREC_MASK;
+  if (pr->flags & ~known) return M3SSD_ERR_FLAGS;
+  if ((pr->flags & M3SSD_PREC_MASK) == M3SSD_PREC_MASK) return M3SSD_ERR_FLAGS;
+  if (pr->batch <= 0 || pr->seqlen <= 0 || pr->nheads <= 0 || pr->headdim <= 0 || pr->dstate <= 0)
+    return M3SSD_ERR_SHAPE;
+  if (pr->chunk < 1 || pr->chunk > 256) return M3SSD_ERR_CHUNK;
+  if (pr->headdim > 256 || pr->dstate > 256) return M3SSD_ERR_DIM_LIMIT;
+  const int64_t nc = (pr->seqlen + pr->chunk - 1) / pr->chunk;
+  int64_t bh, t1, t2;
+  if (!mul_ok(pr->batch, pr->nheads, &bh)) return M3SSD_ERR_OVERFLOW;
+  // grid limits of the chunk-parallel kernels (gridDim.y = chunks, gridDim.z = batch*heads)
+  if (nc > 65535 || bh > 65535) return M3SSD_ERR_SHAPE;
+  if (pr->seqlen > INT_MAX / 2) return M3SSD_ERR_SHAPE;
+  // largest buffers: states (bh*nc*N*D complex) and the per-chunk C*C workspace
+  if (!mul_ok(bh, nc, &t1) || !mul_ok(t1, pr->dstate * pr->headdim, &t2) || !mul_ok(t2, 8, &t2))
+    return M3SSD_ERR_OVERFLOW;
+  if (!mul_ok(t1, pr->chunk * pr->chunk, &t2) || !mul_ok(t2, 16, &t2)) return M3SSD_ERR_OVERFLOW;
+  return M3SSD_OK;
+}
+
+Problem make_problem(const m3ssd_problem* pr) {
+  Problem p{};
+  p.Bsz = (int)pr->batch;
+  p.T = (int)pr->seqlen;
+  p.H = (int)pr->nheads;
+  p.D = (int)pr->headdim;
+  p.N = (int)pr->dstate;
+  p.C = (int)pr->chunk;
+  p.nc = (int)((pr->seqlen + pr->chunk - 1) / pr->chunk);
+  p.x_complex = (pr->flags & M3SSD_X_COMPLEX) ? 1 : 0;
+  return p;
+}
+
+bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
+
+int check_device() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return M3SSD_ERR_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return M3SSD_ERR_DEVICE;
+  if (major != 10) return M3SSD_ERR_DEVICE;
+  return M3SSD_OK;
+}
+
+int fill_inputs(Problem& p, const void* x, const int64_t xs[4], const void* A, const void* B,
+                const int64_t bs[4], const void* C, const int64_t cs[4], const float* dt,
+                const int64_t dts[3]) {
+  if (!x || !A || !B || !C || !dt) return M3SSD_ERR_NULL;
+  const size_t xa = p.x_complex ? 8 : 4;
+  if (!aligned(x, xa) || !aligned(A, 8) || !aligned(B, 8) || !aligned(C, 8) || !aligned(dt, 4))
+    return M3SSD_ERR_ALIGN;
+  p.x = x;
+  p.A = static_cast<const float2*>(A);
+  p.Bm = static_cast<const float2*>(B);
+  p.Cm = static_cast<const float2*>(C);
+  p.dt = dt;
+  for (int i = 0; i < 4; ++i) {
+    p.xs[i] = xs[i];
+    p.bs[i] = bs[i];
+    p.cs[i] = cs[i];
+  }
+  for (int i = 0; i < 3; ++i) p.dts[i] = dts[i];
+  return M3SSD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int m3ssd_abi_version(void) { return M3SSD_ABI_VERSION; }
+
+const char* m3ssd_strerror(int status) {
+  switch (status) {
+    case M3SSD_OK: return "success";
+    case M3SSD_ERR_NULL: return "m3ssd: a required pointer is NULL";
+    case M3SSD_ERR_SHAPE: return "m3ssd: invalid or unsupported shape";
+    case M3SSD_ERR_CHUNK: return "m3ssd: chunk_size must be in [1, 256]";
+    case M3SSD_ERR_DIM_LIMIT: return "m3ssd: head_dim and state_dim must not exceed 256";
+    case M3SSD_ERR_ALIGN: return "m3ssd: pointer not aligned to its element type";
+    case M3SSD_ERR_WORKSPACE: return "m3ssd: workspace missing or too small";
+    case M3SSD_ERR_LAUNCH: return "m3ssd: CUDA kernel launch failed";
+    case M3SSD_ERR_DEVICE: return "m3ssd: current CUDA device is not an sm_100 GPU";
+    case M3SSD_ERR_FLAGS: return "m3ssd: unknown flag bits";
+    case M3SSD_ERR_OVERFLOW: return "m3ssd: problem size overflows 64-bit indexing";
+    default: return "m3ssd: unknown status";
+  }
+}
+
+int m3ssd_check_problem(const m3ssd_problem* prob) { return check_problem(prob); }
+
+size_t m3ssd_states_bytes(const m3ssd_problem* prob) {
+  if (check_problem(prob) != M3SSD_OK) return 0;
+  return m3ssd::simt::states_bytes(make_problem(prob));
+}
+
+size_t m3ssd_fwd_workspace_bytes(const m3ssd_problem* prob) {
+  if (check_problem(prob) != M3SSD_OK) return 0;
+  return m3ssd::simt::fwd_workspace_bytes(make_problem(prob));
+}
+
+size_t m3ssd_bwd_workspace_bytes(const m3ssd_problem* prob) {
+  if (check_problem(prob) != M3SSD_OK) return 0;
+  return m3ssd::simt::bwd_workspace_bytes(make_problem(prob));
+}
+
+const char* m3ssd_fwd_path(const m3ssd_problem* prob) {
+  if (check_problem(prob) != M3SSD_OK) return "invalid";
+  return "simt-fp32";
+}
+
+const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
+  if (check_problem(prob) != M3SSD_OK) return "invalid";
+  return "simt-fp32";
+}
+
+int m3ssd_launch_count(const m3ssd_problem* prob, int backward) {
+  if (check_problem(prob) != M3SSD_OK) return 0;
+  return backward ? m3ssd::simt::kBwdLaunches : m3ssd::simt::kFwdLaunches;
+}
+
+int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  Problem p = make_problem(&a->prob);
+  rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
+                   a->dt_strides);
+  if (rc) return rc;
+  if (!a->y || !a->states) return M3SSD_ERR_NULL;
+  if (!aligned(a->y, 4) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
+  const size_t need = m3ssd::simt::fwd_workspace_bytes(p);
+  if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
+  rc = check_device();
+  if (rc) return rc;
+  return m3ssd::simt::run_fwd(p, a->y, a->states, a->workspace,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  Problem p = make_problem(&a->prob);
+  rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
+                   a->dt_strides);
+  if (rc) return rc;
+  if (!a->dy || !a->states || !a->dx || !a->dA || !a->dB || !a->dC || !a->ddt)
+    return M3SSD_ERR_NULL;
+  const size_t xa = p.x_complex ? 8 : 4;
+  if (!aligned(a->dy, 4) || !aligned(a->states, 16) || !aligned(a->dx, xa) || !aligned(a->dA, 8) ||
+      !aligned(a->dB, 8) || !aligned(a->dC, 8) || !aligned(a->ddt, 4))
+    return M3SSD_ERR_ALIGN;
+  const size_t need = m3ssd::simt::bwd_workspace_bytes(p);
+  if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
+  rc = check_device();
+  if (rc) return rc;
+  long long dys[4];
+  for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
+  return m3ssd::simt::run_bwd(p, a->dy, dys, a->states, a->dx, static_cast<float2*>(a->dA),
+                              static_cast<float2*>(a->dB), static_cast<float2*>(a->dC), a->ddt,
+                              a->workspace, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,216 @@
+"""Drop-in replacement for the reference's complex chunkwise SSD operator.
+
+``ssd_complex_chunkwise(x, A, B_t, C_t, dt, chunk_size=64, ssd_dispatch=...)`` has the signature,
+shapes, dtypes and return value of models/ssd_complex.py:58-119 (atandra2000/Mamba-3-Lite):
+
+    x     (B, T, H, D) float32 (the block's real ``x_ssm``) or complex64 (the reference tests)
+    A     (H,) complex64, one complex decay rate per head (models/mamba_block.py:41)
+    B_t   (B, T, H, N) complex64
+    C_t   (B, T, H, N) complex64
+    dt    (B, T, H) float32, pre-softplus (the operator applies softplus itself)
+    ->    (B, T, H, D) float32 = Re(Y)
+
+It is differentiable with respect to all five inputs, with PyTorch's gradient convention for
+complex tensors (grad = dL/dRe + i dL/dIm; dA summed over batch and time), and runs only on CUDA
+through libm3ssd.so (include/m3ssd.h). There is no CPU fallback: CPU tensors raise.
+
+Differences from the reference, all deliberate:
+* ``exp`` is evaluated only inside the causal region, so strong decays that overflow the
+  reference's exp-then-mask (models/ssd_complex.py:52, :107) to NaN stay finite here.
+* The chunk-to-chunk carry is a sequential scan over chunks instead of the O(n_chunks^2) decay
+  matrix (models/ssd_complex.py:98-111); it is the same sum with no long-range cumsum
+  differences.
+* ``ssd_dispatch`` is accepted for call-site compatibility (models/mamba_block.py:100-121 passes
+  "triton" or nothing); every value runs the CUDA kernels here.
+* ``precision`` (extra keyword) selects "auto" (default), "fp32" (CUDA cores, fp32 everywhere) or
+  "tf32" (tensor-core tiles where the shape has them).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+ctypes_ref = ctypes.byref
+
+_PREC = {"auto": _lib.M3SSD_PREC_AUTO, "fp32": _lib.M3SSD_PREC_FP32, "tf32": _lib.M3SSD_PREC_TF32}
+
+
+def _problem(x, B_t, chunk, flags):
+    Bsz, T, H, D = x.shape
+    N = B_t.shape[-1]
+    return _lib.Problem(Bsz, T, H, D, N, int(chunk), int(flags), 0)
+
+
+def _strides(t, n):
+    s = t.stride()
+    assert len(s) == n
+    return s
+
+
+def _stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_inputs(x, A, B_t, C_t, dt, chunk_size):
+    for name, t in (("x", x), ("A", A), ("B_t", B_t), ("C_t", C_t), ("dt", dt)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"m3ssd: {name} is on {t.device}; the operator runs only on CUDA (sm_100a) "
+                "and has no CPU fallback")
+    if x.dim() != 4:
+        raise ValueError(f"x must be (B, T, H, D), got shape {tuple(x.shape)}")
+    Bsz, T, H, D = x.shape
+    if B_t.dim() != 4 or C_t.dim() != 4:
+        raise ValueError("B_t and C_t must be (B, T, H, N)")
+    N = B_t.shape[-1]
+    if tuple(B_t.shape) != (Bsz, T, H, N) or tuple(C_t.shape) != (Bsz, T, H, N):
+        raise ValueError(f"B_t/C_t shapes {tuple(B_t.shape)}, {tuple(C_t.shape)} do not match "
+                         f"x {tuple(x.shape)}")
+    if tuple(dt.shape) != (Bsz, T, H):
+        raise ValueError(f"dt must be (B, T, H) = {(Bsz, T, H)}, got {tuple(dt.shape)}")
+    if tuple(A.shape) != (H,):
+        raise ValueError(f"A must be (H,) = ({H},), got {tuple(A.shape)}")
+    if x.dtype not in (torch.float32, torch.complex64):
+        raise TypeError(f"x must be float32 or complex64, got {x.dtype}")
+    for name, t in (("A", A), ("B_t", B_t), ("C_t", C_t)):
+        if t.dtype != torch.complex64:
+            raise TypeError(f"{name} must be complex64, got {t.dtype}")
+    if dt.dtype != torch.float32:
+        raise TypeError(f"dt must be float32, got {dt.dtype}")
+    devs = {t.device for t in (x, A, B_t, C_t, dt)}
+    if len(devs) != 1:
+        raise RuntimeError(f"m3ssd: inputs are on different devices {devs}")
+    if not (1 <= int(chunk_size) <= 256):
+        raise ValueError(f"chunk_size {chunk_size} exceeds the supported range [1, 256]")
+    if D > 256 or N > 256:
+        raise ValueError(f"head_dim {D} / state_dim {N} exceeds the limit 256")
+
+
+@torch.library.custom_op("m3ssd::ssd_fwd", mutates_args=(), device_types="cuda")
+def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tensor,
+            dt: torch.Tensor, chunk: int, flags: int) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    dev = x.device
+    A = A.contiguous()
+    prob = _problem(x, B_t, chunk, flags)
+    _lib.check(lib.m3ssd_check_problem(ctypes_ref(prob)))
+    y = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
+                         device=dev)
+    ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    args = _lib.FwdArgs()
+    args.prob = prob
+    args.x, args.x_strides = x.data_ptr(), _lib.I64x4(*_strides(x, 4))
+    args.A = A.data_ptr()
+    args.B, args.b_strides = B_t.data_ptr(), _lib.I64x4(*_strides(B_t, 4))
+    args.C, args.c_strides = C_t.data_ptr(), _lib.I64x4(*_strides(C_t, 4))
+    args.dt, args.dt_strides = dt.data_ptr(), _lib.I64x3(*_strides(dt, 3))
+    args.y = y.data_ptr()
+    args.states = states.data_ptr()
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3ssd_fwd(ctypes_ref(args), _stream_ptr(dev)))
+    return y, states
+
+
+@ssd_fwd.register_fake
+def _(x, A, B_t, C_t, dt, chunk, flags):
+    lib = _lib.load()
+    prob = _problem(x, B_t, chunk, flags)
+    nbytes = int(lib.m3ssd_states_bytes(ctypes_ref(prob)))
+    return (torch.empty(x.shape, dtype=torch.float32, device=x.device),
+            torch.empty(nbytes, dtype=torch.uint8, device=x.device))
+
+
+@torch.library.custom_op("m3ssd::ssd_bwd", mutates_args=(), device_types="cuda")
+def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
+            C_t: torch.Tensor, dt: torch.Tensor, states: torch.Tensor, chunk: int,
+            flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                 torch.Tensor]:
+    lib = _lib.load()
+    dev = x.device
+    A = A.contiguous()
+    if dy.dtype != torch.float32:
+        dy = dy.float()
+    prob = _problem(x, B_t, chunk, flags)
+    dx = torch.empty(x.shape, dtype=x.dtype, device=dev)
+    dA = torch.empty(A.shape, dtype=torch.complex64, device=dev)
+    dB = torch.empty(B_t.shape, dtype=torch.complex64, device=dev)
+    dC = torch.empty(C_t.shape, dtype=torch.complex64, device=dev)
+    ddt = torch.empty(dt.shape, dtype=torch.float32, device=dev)
+    ws_bytes = int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob)))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    args = _lib.BwdArgs()
+    args.prob = prob
+    args.x, args.x_strides = x.data_ptr(), _lib.I64x4(*_strides(x, 4))
+    args.A = A.data_ptr()
+    args.B, args.b_strides = B_t.data_ptr(), _lib.I64x4(*_strides(B_t, 4))
+    args.C, args.c_strides = C_t.data_ptr(), _lib.I64x4(*_strides(C_t, 4))
+    args.dt, args.dt_strides = dt.data_ptr(), _lib.I64x3(*_strides(dt, 3))
+    args.dy, args.dy_strides = dy.data_ptr(), _lib.I64x4(*_strides(dy, 4))
+    args.states = states.data_ptr()
+    args.dx, args.dA, args.dB, args.dC, args.ddt = (dx.data_ptr(), dA.data_ptr(), dB.data_ptr(),
+                                                    dC.data_ptr(), ddt.data_ptr())
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3ssd_bwd(ctypes_ref(args), _stream_ptr(dev)))
+    return dx, dA, dB, dC, ddt
+
+
+@ssd_bwd.register_fake
+def _(dy, x, A, B_t, C_t, dt, states, chunk, flags):
+    return (torch.empty(x.shape, dtype=x.dtype, device=x.device),
+            torch.empty(A.shape, dtype=torch.complex64, device=x.device),
+            torch.empty(B_t.shape, dtype=torch.complex64, device=x.device),
+            torch.empty(C_t.shape, dtype=torch.complex64, device=x.device),
+            torch.empty(dt.shape, dtype=torch.float32, device=x.device))
+
+
+def _setup_context(ctx, inputs, output):
+    x, A, B_t, C_t, dt, chunk, flags = inputs
+    _, states = output
+    ctx.save_for_backward(x, A, B_t, C_t, dt, states)
+    ctx.chunk = chunk
+    ctx.flags = flags
+    ctx.mark_non_differentiable(states)
+
+
+def _backward(ctx, dy, _dstates):
+    x, A, B_t, C_t, dt, states = ctx.saved_tensors
+    if dy is None:
+        dy = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
+    dx, dA, dB, dC, ddt = ssd_bwd(dy, x, A, B_t, C_t, dt, states, ctx.chunk, ctx.flags)
+    return dx, dA, dB, dC, ddt, None, None
+
+
+ssd_fwd.register_autograd(_backward, setup_context=_setup_context)
+
+
+def ssd_complex_chunkwise(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
+                          C_t: torch.Tensor, dt: torch.Tensor, chunk_size: int = 64,
+                          ssd_dispatch: str = "cuda", precision: str = "auto") -> torch.Tensor:
+    """Complex chunkwise SSD, forward and backward on the GPU (see the module docstring)."""
+    del ssd_dispatch  # every dispatch value runs the CUDA kernels
+    _check_inputs(x, A, B_t, C_t, dt, chunk_size)
+    if precision not in _PREC:
+        raise ValueError(f"precision must be one of {sorted(_PREC)}, got {precision!r}")
+    flags = _PREC[precision] | (_lib.M3SSD_X_COMPLEX if x.dtype == torch.complex64 else 0)
+    with torch.autocast("cuda", enabled=False):
+        y, _ = ssd_fwd(x, A, B_t, C_t, dt, int(chunk_size), int(flags))
+    return y
+
+
+def implementation(x_shape, N, chunk_size=64, complex_x=False, precision="auto"):
+    """Names of the forward and backward implementations the library picks for a shape."""
+    lib = _lib.load()
+    Bsz, T, H, D = x_shape
+    flags = _PREC[precision] | (_lib.M3SSD_X_COMPLEX if complex_x else 0)
+    prob = _lib.Problem(Bsz, T, H, D, N, int(chunk_size), int(flags), 0)
+    return (lib.m3ssd_fwd_path(ctypes_ref(prob)).decode(),
+            lib.m3ssd_bwd_path(ctypes_ref(prob)).decode())

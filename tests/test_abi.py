@@ -1,0 +1,107 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol include/m3ssd.h
+declares, and its host-side validation returns the documented status codes."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from m3ssd import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "m3ssd.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(m3ssd_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+def prob(**kw):
+    d = dict(batch=2, seqlen=256, nheads=4, headdim=64, dstate=64, chunk=64, flags=0, reserved=0)
+    d.update(kw)
+    return _lib.Problem(**d)
+
+
+def test_header_declares_the_expected_api():
+    syms = declared_symbols()
+    assert set(syms) == set(_lib.SIGNATURES), syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.m3ssd_abi_version() == 1
+
+
+def test_strerror_covers_all_codes(lib):
+    for code in list(_lib.STATUS_NAMES) + [999]:
+        msg = lib.m3ssd_strerror(code).decode()
+        assert msg
+    assert lib.m3ssd_strerror(3).decode().startswith("m3ssd: chunk_size")
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(), 0),
+    (dict(chunk=0), 3), (dict(chunk=257), 3),
+    (dict(headdim=257), 4), (dict(dstate=300), 4),
+    (dict(batch=0), 2), (dict(seqlen=-1), 2), (dict(nheads=0), 2),
+    (dict(flags=0x100), 9), (dict(flags=0x30), 9), (dict(reserved=1), 9),
+    (dict(batch=70000, nheads=1), 2),
+    (dict(seqlen=64 * 70000, chunk=64), 2),
+    (dict(chunk=4, seqlen=20), 0), (dict(chunk=1, seqlen=3, headdim=1, dstate=1), 0),
+])
+def test_check_problem(lib, kw, code):
+    assert lib.m3ssd_check_problem(ctypes.byref(prob(**kw))) == code
+
+
+def test_sizes(lib):
+    p = prob()
+    nc = 256 // 64
+    assert lib.m3ssd_states_bytes(ctypes.byref(p)) == 8 * 2 * 4 * nc * 64 * 64
+    assert lib.m3ssd_fwd_workspace_bytes(ctypes.byref(p)) > 0
+    assert lib.m3ssd_bwd_workspace_bytes(ctypes.byref(p)) > 0
+    bad = prob(chunk=0)
+    assert lib.m3ssd_states_bytes(ctypes.byref(bad)) == 0
+    assert lib.m3ssd_fwd_path(ctypes.byref(bad)) == b"invalid"
+
+
+def test_null_arguments_rejected_before_any_device_work(lib):
+    assert lib.m3ssd_fwd(None, None) == 1
+    assert lib.m3ssd_bwd(None, None) == 1
+    a = _lib.FwdArgs()
+    a.prob = prob()
+    assert lib.m3ssd_fwd(ctypes.byref(a), None) == 1
+    a.prob = prob(chunk=0)
+    assert lib.m3ssd_fwd(ctypes.byref(a), None) == 3
+    b = _lib.BwdArgs()
+    b.prob = prob()
+    assert lib.m3ssd_bwd(ctypes.byref(b), None) == 1
+
+
+def test_error_maps_to_runtime_error():
+    with pytest.raises(RuntimeError, match="chunk_size"):
+        _lib.check(3)
+    _lib.check(0)
+
+
+def test_cpu_tensors_raise_no_fallback():
+    import torch
+    from m3ssd import ssd_complex_chunkwise
+    x = torch.randn(1, 8, 2, 4)
+    A = torch.randn(2, dtype=torch.complex64)
+    B = torch.randn(1, 8, 2, 4, dtype=torch.complex64)
+    dt = torch.randn(1, 8, 2)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ssd_complex_chunkwise(x, A, B, B, dt, chunk_size=4)
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(RuntimeError, match="not found"):
+        _lib.load(str(tmp_path / "libm3ssd.so"))
