@@ -28,8 +28,13 @@ def _chunk_local_pass(Bc, Cc, Xc, A_log, decay_states):
     return y_diag, chunk_state
 
 
-def ssd_chunkwise_torch(x, A, B_t, C_t, dt, chunk_size: int = 64):
-    """models/ssd_complex.py:58-119 on any torch device, masked before exp; returns float32."""
+def ssd_chunkwise_torch(x, A, B_t, C_t, dt, chunk_size: int = 64, cdtype=torch.complex64):
+    """models/ssd_complex.py:58-119 on any torch device, masked before exp; returns float32.
+
+    ``cdtype=torch.complex128`` (with float64/complex128 inputs) evaluates the same algorithm in
+    double precision, the ground truth for long sequences where fp32 cumsum differences lose
+    phase accuracy.
+    """
     Bsz, T, H, D = x.shape
     C = int(chunk_size)
     pad = (C - (T % C)) % C
@@ -45,7 +50,7 @@ def ssd_chunkwise_torch(x, A, B_t, C_t, dt, chunk_size: int = 64):
     def view_chunks(t):
         return t.reshape(Bsz, nc, C, *t.shape[2:])
 
-    Xc = view_chunks(x).to(torch.complex64)
+    Xc = view_chunks(x).to(cdtype)
     Bc, Cc, Ac = view_chunks(B_t), view_chunks(C_t), view_chunks(A_log)
     cs = torch.cumsum(Ac, dim=2)
     decay_states = torch.exp(cs[:, :, -1:, :] - cs)
