@@ -202,6 +202,9 @@ def main():
     ap.add_argument("--precision", default="auto")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
+    ap.add_argument("--batch", type=int, default=SHAPE["B"],
+                    help="batch per rank (a smaller batch is only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -221,6 +224,7 @@ def main():
                                 device_id=dev)
     m3ssd.load()
     B, T, H, D, N = (SHAPE[k] for k in ("B", "T", "H", "D", "N"))
+    B = args.batch
     d = make_inputs(dev, 1000 + rank, B, T, H, D, N)
     fwd_path, bwd_path = m3ssd.implementation((B, T, H, D), N, CHUNK, precision=args.precision)
     lib = m3ssd.load()
@@ -296,19 +300,21 @@ def main():
         for k, v in zip(("dx", "dA", "dB", "dC", "ddt"), xs):
             outs_h[k].copy_(v.grad, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
 
     # slowest rank
     vals = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)

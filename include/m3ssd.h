@@ -20,6 +20,9 @@
  *   - The library never allocates, frees or synchronises. Scratch is caller-provided, sized by
  *     the *_bytes queries below. Calls are reentrant; concurrent calls need distinct scratch.
  *   - Return value 0 is success; anything else is an m3ssd_status (see m3ssd_strerror).
+ *   - The first 4 bytes of each workspace receive a device status word once the enqueued work
+ *     has run: 0 = ok, otherwise bits of M3SSD_DEVERR_*. Kernels never trap or spin forever;
+ *     a wait that exceeds its bound sets a bit and the call completes with undefined outputs.
  *   - No CPU fallback exists: the only implementation is CUDA code built for sm_100a.
  */
 #ifndef M3SSD_H_
@@ -55,11 +58,17 @@ typedef enum m3ssd_status {
   M3SSD_ERR_OVERFLOW = 10      /* a size product overflows the 64-bit index space */
 } m3ssd_status;
 
+/* device status bits (first word of the workspace) */
+#define M3SSD_DEVERR_TMA_WAIT   0x1u  /* a TMA transfer did not complete within the bound */
+#define M3SSD_DEVERR_MMA_WAIT   0x2u  /* a tcgen05.mma group did not complete within the bound */
+#define M3SSD_DEVERR_FLAG_WAIT  0x4u  /* a chunk-state hand-off flag was not set within the bound */
+
 /* problem flags */
 #define M3SSD_X_COMPLEX      0x1u   /* x (and dx) are complex64; otherwise float32 */
 #define M3SSD_PREC_AUTO      0x0u   /* fastest path supported for the shape */
 #define M3SSD_PREC_FP32      0x10u  /* fp32 CUDA-core arithmetic everywhere */
-#define M3SSD_PREC_TF32      0x20u  /* tf32 tensor-core tiles (tcgen05) where available */
+#define M3SSD_PREC_TENSOR    0x20u  /* tcgen05 tensor-core tiles where the shape has them:
+                                       split-bf16 operands (hi + lo), fp32 accumulation */
 #define M3SSD_PREC_MASK      0x30u
 
 typedef struct m3ssd_problem {
@@ -68,7 +77,8 @@ typedef struct m3ssd_problem {
   int64_t nheads;     /* H */
   int64_t headdim;    /* D */
   int64_t dstate;     /* N */
-  int64_t chunk;      /* chunk length C */
+  int64_t chunk;      /* chunk length C (problems the tensor-core path can take are blocked
+                         at 64 internally; the result does not depend on the blocking) */
   uint32_t flags;     /* M3SSD_X_COMPLEX | one M3SSD_PREC_* */
   uint32_t reserved;  /* must be 0 */
 } m3ssd_problem;
@@ -130,8 +140,10 @@ M3SSD_API int m3ssd_fwd(const m3ssd_fwd_args* args, void* stream);
  * batch and time. */
 M3SSD_API int m3ssd_bwd(const m3ssd_bwd_args* args, void* stream);
 
-/* Name of the implementation m3ssd_fwd would use for this problem ("tcgen05-tf32",
- * "simt-fp32"). Host-only query, no device work. */
+/* Name of the implementation m3ssd_fwd / m3ssd_bwd use for this problem ("tcgen05-bf16x2",
+ * "simt-fp32"). The tensor-core path needs head_dim = state_dim = 64, real x, and B/C with a
+ * contiguous state dimension and 16-byte aligned strides; otherwise the fp32 path runs.
+ * Host-only query, no device work. */
 M3SSD_API const char* m3ssd_fwd_path(const m3ssd_problem* prob);
 M3SSD_API const char* m3ssd_bwd_path(const m3ssd_problem* prob);
 

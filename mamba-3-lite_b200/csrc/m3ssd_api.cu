@@ -7,6 +7,7 @@
 #include "m3ssd.h"
 #include "m3ssd_common.cuh"
 #include "simt_path.h"
+#include "tc_path.h"
 
 using m3ssd::Problem;
 
@@ -42,6 +43,15 @@ int check_problem(const m3ssd_problem* pr) {
   return M3SSD_OK;
 }
 
+// Problems the tensor-core path can take (by shape and precision) are blocked at 64 positions
+// whichever path runs, so `states` written by either forward path is read correctly by either
+// backward path. The result does not depend on the blocking.
+bool tc_shape(const m3ssd_problem* pr) {
+  const uint32_t prec = pr->flags & M3SSD_PREC_MASK;
+  return pr->headdim == 64 && pr->dstate == 64 && !(pr->flags & M3SSD_X_COMPLEX) &&
+         prec != M3SSD_PREC_FP32;
+}
+
 Problem make_problem(const m3ssd_problem* pr) {
   Problem p{};
   p.Bsz = (int)pr->batch;
@@ -52,7 +62,16 @@ Problem make_problem(const m3ssd_problem* pr) {
   p.C = (int)pr->chunk;
   p.nc = (int)((pr->seqlen + pr->chunk - 1) / pr->chunk);
   p.x_complex = (pr->flags & M3SSD_X_COMPLEX) ? 1 : 0;
+  if (tc_shape(pr)) {
+    p.C = m3ssd::tc::kChunk;
+    p.nc = (int)((pr->seqlen + p.C - 1) / p.C);
+  }
   return p;
+}
+
+size_t fwd_ws(const Problem& p) {
+  const size_t a = m3ssd::simt::fwd_workspace_bytes(p), b = m3ssd::tc::fwd_workspace_bytes(p);
+  return a > b ? a : b;
 }
 
 bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
@@ -119,7 +138,7 @@ size_t m3ssd_states_bytes(const m3ssd_problem* prob) {
 
 size_t m3ssd_fwd_workspace_bytes(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  return m3ssd::simt::fwd_workspace_bytes(make_problem(prob));
+  return fwd_ws(make_problem(prob));
 }
 
 size_t m3ssd_bwd_workspace_bytes(const m3ssd_problem* prob) {
@@ -129,7 +148,7 @@ size_t m3ssd_bwd_workspace_bytes(const m3ssd_problem* prob) {
 
 const char* m3ssd_fwd_path(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return "invalid";
-  return "simt-fp32";
+  return tc_shape(prob) ? "tcgen05-bf16x2" : "simt-fp32";
 }
 
 const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
@@ -139,7 +158,8 @@ const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
 
 int m3ssd_launch_count(const m3ssd_problem* prob, int backward) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  return backward ? m3ssd::simt::kBwdLaunches : m3ssd::simt::kFwdLaunches;
+  if (backward) return m3ssd::simt::kBwdLaunches;
+  return tc_shape(prob) ? m3ssd::tc::kFwdLaunches : m3ssd::simt::kFwdLaunches;
 }
 
 int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
@@ -152,11 +172,13 @@ int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
   if (rc) return rc;
   if (!a->y || !a->states) return M3SSD_ERR_NULL;
   if (!aligned(a->y, 4) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
-  const size_t need = m3ssd::simt::fwd_workspace_bytes(p);
+  const size_t need = fwd_ws(p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
   if (rc) return rc;
+  if (tc_shape(&a->prob) && m3ssd::tc::fwd_supported(p))
+    return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream));
   return m3ssd::simt::run_fwd(p, a->y, a->states, a->workspace,
                               static_cast<cudaStream_t>(stream));
 }

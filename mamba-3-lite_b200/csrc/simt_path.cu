@@ -16,6 +16,10 @@
 //             k_bwd_da        d(Sigma) -> reverse cumsum -> ddt and per-chunk dA partials
 //             k_bwd_dA        dA[h] = sum over batch and chunks (fixed order, deterministic)
 //
+// Chunk states (S_z, the carried H_z and the state gradients) are stored per (b*H + h, chunk)
+// as [p][n] complex64, i.e. [D][2N] floats with re/im interleaved; the tensor-core path uses the
+// same layout so forward and backward paths can be paired freely.
+//
 // Chunk-local quantities match models/ssd_complex.py:82-119: Sigma_l is the inclusive cumsum of
 // a within the chunk (:89), e^{Gamma - Sigma_s} is decay_states (:90), the causal decay
 // e^{Sigma_l - Sigma_s} is L (:50-52, evaluated only for s <= l), and the carried state H_z is
@@ -131,7 +135,7 @@ __global__ void __launch_bounds__(NT) k_fwd_state(Problem p, const float2* __res
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int n = n0 + tm0 + 8 * i, d = p0 + tn;
-    if (n < p.N && d < p.D) st[(long long)n * p.D + d] = acc[i];
+    if (n < p.N && d < p.D) st[(long long)d * p.N + n] = acc[i];
   }
 }
 
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
   };
   auto fb3 = [&](int n, int j) -> float2 {
     const int d = p0 + j;
-    return (n < p.N && d < p.D) ? hz[(long long)n * p.D + d] : cz();
+    return (n < p.N && d < p.D) ? hz[(long long)d * p.N + n] : cz();
   };
   tile_mma<true, false>(accY, p.N, fa3, fb3, sm);
 #pragma unroll
@@ -262,7 +266,7 @@ __global__ void __launch_bounds__(NT) k_bwd_q(Problem p, Grad g, const float2* _
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int n = n0 + tm0 + 8 * i, d = p0 + tn;
-    if (n < p.N && d < p.D) q[(long long)n * p.D + d] = acc[i];
+    if (n < p.N && d < p.D) q[(long long)d * p.N + n] = acc[i];
   }
 }
 
@@ -408,7 +412,7 @@ __global__ void __launch_bounds__(NT) k_bwd_dc(Problem p, Grad g, const float2* 
   };
   auto fb2 = [&](int d, int j) -> float2 {
     const int n = n0 + j;
-    return n < p.N ? cconj(hz[(long long)n * p.D + d]) : cz();
+    return n < p.N ? cconj(hz[(long long)d * p.N + n]) : cz();
   };
   tile_mma<true, true>(acc2, p.D, fa2, fb2, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
@@ -458,7 +462,7 @@ __global__ void __launch_bounds__(NT) k_bwd_db(Problem p, const float2* __restri
   };
   auto fb2 = [&](int d, int j) -> float2 {
     const int n = n0 + j;
-    return n < p.N ? dsz[(long long)n * p.D + d] : cz();
+    return n < p.N ? dsz[(long long)d * p.N + n] : cz();
   };
   tile_mma<true, true>(acc2, p.D, fa2, fb2, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
@@ -511,7 +515,7 @@ __global__ void __launch_bounds__(NT) k_bwd_dx(Problem p, Grad g, const float2* 
   };
   auto fb2 = [&](int n, int j) -> float2 {
     const int d = p0 + j;
-    return (n < p.N && d < p.D) ? dsz[(long long)n * p.D + d] : cz();
+    return (n < p.N && d < p.D) ? dsz[(long long)d * p.N + n] : cz();
   };
   tile_mma<true, false>(acc, p.N, fa2, fb2, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
@@ -582,9 +586,12 @@ struct BwdLayout {
   size_t acs, dsbuf, mbuf, dgbuf, rowpart, colpart, rowcpart, upart, gpart, dapart, total;
 };
 
+// The first 256 bytes of every workspace are the status area (device error word at offset 0).
+constexpr size_t kStatusBytes = 256;
+
 static FwdLayout fwd_layout(const Problem& p) {
   FwdLayout L;
-  size_t off = 0;
+  size_t off = kStatusBytes;
   L.acs = off; off += align256(sizeof(float2) * (size_t)p.Bsz * p.H * p.Tp());
   L.total = off;
   return L;
@@ -596,7 +603,7 @@ static BwdLayout bwd_layout(const Problem& p) {
   BwdLayout L;
   const size_t bhz = (size_t)p.Bsz * p.H * p.nc;
   const size_t tC = (size_t)tiles(p.C), tN = (size_t)tiles(p.N);
-  size_t off = 0;
+  size_t off = kStatusBytes;
   L.acs = off;      off += align256(sizeof(float2) * (size_t)p.Bsz * p.H * p.Tp());
   L.dsbuf = off;    off += align256(sizeof(float2) * bhz * p.N * p.D);
   L.mbuf = off;     off += align256(sizeof(float2) * bhz * p.C * p.C);
@@ -624,6 +631,7 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   float2* acs = reinterpret_cast<float2*>(static_cast<char*>(ws) + L.acs);
   float2* S = static_cast<float2*>(states);
   const long long nbhz = (long long)p.Bsz * p.H * p.nc;
+  if (cudaMemsetAsync(ws, 0, kStatusBytes, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   k_chunk_cumsum<<<(unsigned)((nbhz + 127) / 128), 128, 0, st>>>(p, acs);
   const dim3 g_np((unsigned)(tiles(p.N) * tiles(p.D)), (unsigned)p.nc, (unsigned)(p.Bsz * p.H));
   k_fwd_state<<<g_np, NT, 0, st>>>(p, acs, S);
@@ -655,6 +663,7 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
   const float2* S = static_cast<const float2*>(states);
   const long long nbhz = (long long)p.Bsz * p.H * p.nc;
   const unsigned bh = (unsigned)(p.Bsz * p.H), nc = (unsigned)p.nc;
+  if (cudaMemsetAsync(ws, 0, kStatusBytes, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   k_chunk_cumsum<<<(unsigned)((nbhz + 127) / 128), 128, 0, st>>>(p, acs);
   k_bwd_q<<<dim3((unsigned)(tiles(p.N) * tiles(p.D)), nc, bh), NT, 0, st>>>(p, g, acs, dsbuf);
   const int sb = scan_blocks_for(p);

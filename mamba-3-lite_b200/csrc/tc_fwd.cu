@@ -1,0 +1,601 @@
+// Tensor-core forward of the complex chunkwise SSD for head_dim = state_dim = 64, real x.
+//
+// One persistent CTA per SM takes chunk tickets (chunk-major order over all b*H sequences) from a
+// global counter. Per ticket (64 positions of one (b, h)), with Sigma_l = rho_l + i theta_l the
+// within-chunk cumsum of a = softplus(dt) A (models/ssd_complex.py:82, :89), Gamma = Sigma_63:
+//
+//   C'[l,n] = C[l,n] cis(theta_l)          B'[s,n] = B[s,n] conj(cis(theta_s))
+//   G  = Re(C' B'^T)                       (= Re(C B^T o cis(theta_l - theta_s)), K = 2N)
+//   Mr = exp(rho_l - rho_s) G  for s <= l (the causal decay L of :50-52, exp only where s <= l)
+//   Y1 = Mr x                              (intra-chunk output, :53)
+//   S~ = sum_s exp(rho_Gamma - rho_s) B'[s] x[s]^T    (chunk state, :54, before the cis(theta_Gamma))
+//   H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~       (the carry of :98-111 as a scan)
+//   y  = Y1 + exp(rho_l) Re(C' H_z)        (:115-119)
+//
+// All four contractions run on tcgen05 (kind::f16) with split-bf16 operands and fp32 TMEM
+// accumulators (tc_common.cuh). B and C tiles arrive by TMA; x and dt by 128-bit loads
+// prefetched one ticket ahead. H_z is handed from the CTA that processed chunk z-1 of the same
+// sequence through global memory (it is also the `states` output the backward reads) with a
+// release flag; waits are bounded and report kErrFlagWait instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include "m3ssd_common.cuh"
+#include "tc_common.cuh"
+#include "tc_path.h"
+
+namespace m3ssd {
+namespace tc {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr uint32_t OFF_CX = 0;          // C'x  A, K-major, stacked 128 rows x 128 k, 2 k-atoms
+constexpr uint32_t OFF_BXH = 32768;     // B'x hi (conjugate-interleaved) 64 rows x 128 k
+constexpr uint32_t OFF_BXL = 49152;     // B'x lo
+constexpr uint32_t OFF_XH = 65536;      // x hi [s][p]
+constexpr uint32_t OFF_XL = 73728;      // x lo
+constexpr uint32_t OFF_XT = 81920;      // x~ stacked [p-group][s][64]
+constexpr uint32_t OFF_MR = 98304;      // Mr stacked [128][s]
+constexpr uint32_t OFF_HH = 114688;     // Hx hi [k][p]
+constexpr uint32_t OFF_HL = 131072;     // Hx lo
+constexpr uint32_t OFF_RAWB = 147456;   // TMA tile of B (fp32, 64 x 128)
+constexpr uint32_t OFF_RAWC = 180224;   // TMA tile of C
+constexpr uint32_t OFF_MISC = 212992;
+constexpr uint32_t kSmemBytes = OFF_MISC + 2048 + 1024;
+constexpr uint32_t kTmaBytes = 2u * 64u * 128u * 4u;
+
+// TMEM columns
+constexpr uint32_t COL_G = 0, COL_S = 64, COL_Y1 = 192, COL_Y2 = 256, kTmemCols = 512;
+
+struct Misc {
+  uint64_t bar_tma, bar_mma1, bar_mma2, bar_mma3;
+  float rho[64];
+  float el[64];
+  float dec[64];
+  float2 cis[64];
+  float2 carry;
+  float2 gam;
+  float2 g;   // e^Gamma
+  float2 ct;  // cis(theta_Gamma)
+  int next_ticket;
+  uint32_t tmem_base;
+};
+static_assert(sizeof(Misc) <= 2048, "misc area");
+
+struct FwdParams {
+  int Bsz, T, H, nc, total;
+  const float* x;
+  long long xs[4];
+  int x_vec;
+  const float2* A;
+  const float* dt;
+  long long dts[3];
+  float* y;
+  float* states;
+  uint32_t* flags;
+  uint32_t* counter;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ void load_x16(const FwdParams& p, int b, int t, int h, int p0,
+                                         float (&xv)[16]) {
+  if (t >= p.T) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) xv[i] = 0.f;
+    return;
+  }
+  const float* base = p.x + b * p.xs[0] + (long long)t * p.xs[1] + h * p.xs[2];
+  if (p.x_vec) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = ldg_nc_v4(base + p0 + 4 * i);
+      xv[4 * i] = v.x;
+      xv[4 * i + 1] = v.y;
+      xv[4 * i + 2] = v.z;
+      xv[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) xv[i] = __ldg(base + (long long)(p0 + i) * p.xs[3]);
+  }
+}
+
+__device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_fwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+             const FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = smem_u32(smem);
+  Misc& m = *reinterpret_cast<Misc*>(smem + OFF_MISC);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sub = warp & 3, wg = warp >> 2, part = lane >> 4;
+  const int BH = p.Bsz * p.H;
+
+  if (tid == 0) {
+    mbar_init(&m.bar_tma, 1);
+    mbar_init(&m.bar_mma1, 1);
+    mbar_init(&m.bar_mma2, 1);
+    mbar_init(&m.bar_mma3, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+    m.next_ticket = (int)atomicAdd(p.counter, 1u);
+  }
+  if (warp == 0) {
+    tmem_alloc(&m.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = m.tmem_base;
+  const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
+
+  int ticket = m.next_ticket;
+  float xv[16];
+  float dtv = 0.f;
+  auto prefetch = [&](int tk) {
+    const int z = tk / BH, bh = tk - (tk / BH) * BH;
+    const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
+    load_x16(p, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
+    dtv = 0.f;
+    if (tid < 64 && t0 + tid < p.T) dtv = __ldg(p.dt + b * p.dts[0] + (long long)(t0 + tid) * p.dts[1] + h * p.dts[2]);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes);
+      tma_load_4d(smem + OFF_RAWB, &tmB, &m.bar_tma, 0, h, t0, b);
+      tma_load_4d(smem + OFF_RAWC, &tmC, &m.bar_tma, 0, h, t0, b);
+    }
+  };
+  if (ticket < p.total) prefetch(ticket);
+
+  uint32_t iter = 0;
+  while (ticket < p.total) {
+    const uint32_t ph = iter & 1u;
+    const int z = ticket / BH, bh = ticket - z * BH;
+    const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
+    __syncthreads();  // everyone has read m.next_ticket of the previous round
+    if (tid == 0) m.next_ticket = (int)atomicAdd(p.counter, 1u);
+
+    // ---- within-chunk cumsum of a = softplus(dt) A (warps 0-1, one position per thread)
+    if (tid < 64) {
+      const float2 A = p.A[h];
+      float2 a = make_float2(0.f, 0.f);
+      if (t0 + tid < p.T) {
+        const float sp = softplus_f(dtv);
+        a = make_float2(sp * A.x, sp * A.y);
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float ux = __shfl_up_sync(0xffffffffu, a.x, o);
+        const float uy = __shfl_up_sync(0xffffffffu, a.y, o);
+        if (lane >= o) {
+          a.x += ux;
+          a.y += uy;
+        }
+      }
+      if (tid == 31) m.carry = a;
+      // stash both components until warp 0's total (the carry) is known
+      m.rho[tid] = a.x;
+      m.el[tid] = a.y;
+    }
+    __syncthreads();
+    const int next = m.next_ticket;
+    if (tid < 64) {
+      float rx = m.rho[tid], ry = m.el[tid];
+      if (tid >= 32) {
+        rx += m.carry.x;
+        ry += m.carry.y;
+      }
+      float sn, cs;
+      sincosf(ry, &sn, &cs);
+      m.rho[tid] = rx;
+      m.cis[tid] = make_float2(cs, sn);
+      if (tid == 63) m.gam = make_float2(rx, ry);
+    }
+    __syncthreads();
+    if (tid < 64) {
+      const float rx = m.rho[tid];
+      m.el[tid] = expf(rx);
+      m.dec[tid] = expf(m.gam.x - rx);
+      if (tid == 0) {
+        const float mg = expf(m.gam.x);
+        float sn, cs;
+        sincosf(m.gam.y, &sn, &cs);
+        m.g = make_float2(mg * cs, mg * sn);
+        m.ct = make_float2(cs, sn);
+      }
+    }
+
+    // ---- TMA tiles of B and C for this ticket
+    mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);
+    __syncthreads();  // cis/el/dec visible
+
+    // ---- operand transform: C'x (stacked hi/lo), B'x (conjugate-interleaved hi, lo)
+    {
+      const float* rawB = reinterpret_cast<const float*>(smem + OFF_RAWB);
+      const float* rawC = reinterpret_cast<const float*>(smem + OFF_RAWC);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = tid + kThreads * i;
+        const int l = j >> 4, q = j & 15;
+        const float2 cs = m.cis[l];
+        const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
+        const float4 c0 = *reinterpret_cast<const float4*>(rawC + l * 128 + 8 * q);
+        const float4 c1 = *reinterpret_cast<const float4*>(rawC + l * 128 + 8 * q + 4);
+        const float cr[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {  // C * cis(theta_l)
+          v[2 * u] = cr[2 * u] * cs.x - cr[2 * u + 1] * cs.y;
+          v[2 * u + 1] = cr[2 * u] * cs.y + cr[2 * u + 1] * cs.x;
+        }
+        uint4 hi, lo;
+        split8(v, hi, lo);
+        st_shared_v4(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 0), ch), hi);
+        st_shared_v4(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 1), ch), lo);
+        const float4 b0 = *reinterpret_cast<const float4*>(rawB + l * 128 + 8 * q);
+        const float4 b1 = *reinterpret_cast<const float4*>(rawB + l * 128 + 8 * q + 4);
+        const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {  // conj(B * conj(cis(theta_s)))
+          v[2 * u] = br[2 * u] * cs.x + br[2 * u + 1] * cs.y;
+          v[2 * u + 1] = br[2 * u] * cs.y - br[2 * u + 1] * cs.x;
+        }
+        split8(v, hi, lo);
+        st_shared_v4(sb + OFF_BXH + ka * 8192u + swz(l, ch), hi);
+        st_shared_v4(sb + OFF_BXL + ka * 8192u + swz(l, ch), lo);
+      }
+      // x (hi, lo) and x~ = exp(rho_Gamma - rho_s) x, stacked over p
+      const int s = tid >> 2, pg = tid & 3;
+      float v8[8];
+      uint4 h0, l0, h1, l1;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = xv[u];
+      split8(v8, h0, l0);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = xv[8 + u];
+      split8(v8, h1, l1);
+      st_shared_v4(sb + OFF_XH + swz(s, 2 * pg), h0);
+      st_shared_v4(sb + OFF_XH + swz(s, 2 * pg + 1), h1);
+      st_shared_v4(sb + OFF_XL + swz(s, 2 * pg), l0);
+      st_shared_v4(sb + OFF_XL + swz(s, 2 * pg + 1), l1);
+      const float dd = m.dec[s];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = dd * xv[u];
+      split8(v8, h0, l0);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = dd * xv[8 + u];
+      split8(v8, h1, l1);
+      const uint32_t xt = sb + OFF_XT + (uint32_t)(pg >> 1) * 8192u;
+      const uint32_t c4 = 4u * (uint32_t)(pg & 1);
+      st_shared_v4(xt + swz(s, c4 + 0), h0);
+      st_shared_v4(xt + swz(s, c4 + 1), h1);
+      st_shared_v4(xt + swz(s, c4 + 2), l0);
+      st_shared_v4(xt + swz(s, c4 + 3), l1);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    // ---- MMA batch 1: G = C'x B'x^T (M128 N64), S~^T = x~^T B'x (M128 N128)
+    if (tid == 0) {
+      tc_fence_after_sync();
+      const uint32_t idG = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const uint32_t bofs = hl ? OFF_BXL : OFF_BXH;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint64_t a = sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024);
+          const uint64_t bd = sdesc(sb + bofs + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024);
+          mma_bf16_ss(tmem + COL_G, a, bd, idG, (hl | j) != 0);
+        }
+      }
+      const uint32_t idS = idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const uint32_t bofs = hl ? OFF_BXL : OFF_BXH;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t a = sdesc(sb + OFF_XT + j * 2048u, 8192, 1024);
+          const uint64_t bd = sdesc(sb + bofs + j * 2048u, 8192, 1024);
+          mma_bf16_ss(tmem + COL_S, a, bd, idS, (hl | j) != 0);
+        }
+      }
+      mma_commit(&m.bar_mma1);
+    }
+    // prefetch the next ticket (raw tiles are free: every thread passed the transform)
+    if (next < p.total) prefetch(next);
+
+    // ---- epilogue 1: Mr = exp(rho_l - rho_s) G (s <= l), split-bf16, stacked rows
+    mbar_wait(&m.bar_mma1, ph, p.err, kErrMmaWait);
+    tc_fence_after_sync();
+    const int r = 16 * sub + (lane & 15);  // logical row (position l, or p for S~)
+    {
+      float v[32];
+      tmem_ld32(tmem + lane_off + COL_G + 32u * wg, v);
+      tmem_ld_wait();
+      float mr[16];
+      const float rl = m.rho[r];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float send = part ? v[c] : v[16 + c];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+        const float gsum = (part ? v[16 + c] : v[c]) + recv;
+        const int s = 32 * wg + 16 * part + c;
+        mr[c] = (s <= r) ? expf(rl - m.rho[s]) * gsum : 0.f;
+      }
+      float v8[8];
+      uint4 h0, l0, h1, l1;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = mr[u];
+      split8(v8, h0, l0);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = mr[8 + u];
+      split8(v8, h1, l1);
+      const uint32_t ch = 4u * wg + 2u * part;
+      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 0), ch), h0);
+      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 0), ch + 1), h1);
+      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 1), ch), l0);
+      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 1), ch + 1), l1);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // Y1 = Mr x
+      tc_fence_after_sync();
+      const uint32_t idY = idesc_bf16(128, 64, 0, 1);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const uint32_t bofs = hl ? OFF_XL : OFF_XH;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t a = sdesc(sb + OFF_MR + j * 32u, 16, 1024);
+          const uint64_t bd = sdesc(sb + bofs + j * 2048u, 8192, 1024);
+          mma_bf16_ss(tmem + COL_Y1, a, bd, idY, (hl | j) != 0);
+        }
+      }
+      mma_commit(&m.bar_mma2);
+    }
+
+    // ---- H_z from the predecessor chunk (bounded wait on its release flag)
+    const int kb = 64 * wg + 32 * part;  // this thread's 32 interleaved state columns
+    float hz[32];
+    if (z == 0) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) hz[c] = 0.f;
+    } else {
+      if (tid == 0) {
+        const uint32_t* f = p.flags + (long long)bh * p.nc + z;
+        uint32_t i = 0;
+        for (; i < kSpinLimit; ++i) {
+          if (ld_acquire_gpu(f) != 0u) break;
+          __nanosleep(128);
+        }
+        if (i == kSpinLimit) atomicOr(p.err, kErrFlagWait);
+        __threadfence();
+      }
+      __syncthreads();
+      const float* src = p.states + (((long long)bh * p.nc + z) * 64 + r) * 128 + kb;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
+        hz[4 * i] = v.x;
+        hz[4 * i + 1] = v.y;
+        hz[4 * i + 2] = v.z;
+        hz[4 * i + 3] = v.w;
+      }
+    }
+    // Hx = (Re H, -Im H) interleaved, [k][p] MN-major, split hi/lo
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const int k = kb + c;
+      __nv_bfloat16 hh, hl;
+      split_bf16((c & 1) ? -hz[c] : hz[c], hh, hl);
+      const uint32_t off = (uint32_t)k * 128u + ((((uint32_t)r >> 3) ^ ((uint32_t)k & 7u)) << 4) +
+                           ((uint32_t)r & 7u) * 2u;
+      st_shared_u16(sb + OFF_HH + off, __bfloat16_as_ushort(hh));
+      st_shared_u16(sb + OFF_HL + off, __bfloat16_as_ushort(hl));
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {  // Y2 = Re(C' H_z) as C'x Hx
+      tc_fence_after_sync();
+      const uint32_t idY = idesc_bf16(128, 64, 0, 1);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const uint32_t bofs = hl ? OFF_HL : OFF_HH;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint64_t a = sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024);
+          const uint64_t bd = sdesc(sb + bofs + j * 2048u, 8192, 1024);
+          mma_bf16_ss(tmem + COL_Y2, a, bd, idY, (hl | j) != 0);
+        }
+      }
+      mma_commit(&m.bar_mma3);
+    }
+
+    // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~, publish for chunk z+1
+    {
+      float s0[32], s1[32];
+      tmem_ld32(tmem + lane_off + COL_S + 64u * wg, s0);
+      tmem_ld32(tmem + lane_off + COL_S + 64u * wg + 32u, s1);
+      tmem_ld_wait();
+      float hn[32];
+      const float2 g = m.g, ct = m.ct;
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        const float sa = part ? s0[c] : s1[c];
+        const float sbv = part ? s0[c + 1] : s1[c + 1];
+        const float ra = __shfl_xor_sync(0xffffffffu, sa, 16);
+        const float rbv = __shfl_xor_sync(0xffffffffu, sbv, 16);
+        const float sr = (part ? s1[c] : s0[c]) + ra;
+        const float si = -((part ? s1[c + 1] : s0[c + 1]) + rbv);  // B'x is conjugated
+        const float2 hv = cmulf(g, make_float2(hz[c], hz[c + 1]));
+        const float2 sv = cmulf(ct, make_float2(sr, si));
+        hn[c] = hv.x + sv.x;
+        hn[c + 1] = hv.y + sv.y;
+      }
+      float* row = p.states + ((long long)bh * p.nc * 64 + r) * 128 + kb;
+      if (z == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          __stcg(reinterpret_cast<float4*>(row) + i, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+      if (z + 1 < p.nc) {
+        float* dst = row + (long long)(z + 1) * 64 * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          __stcg(reinterpret_cast<float4*>(dst) + i,
+                 make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
+      }
+      __threadfence();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    if (tid == 0 && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+
+    // ---- output y = Y1 + exp(rho_l) Y2
+    mbar_wait(&m.bar_mma2, ph, p.err, kErrMmaWait);
+    mbar_wait(&m.bar_mma3, ph, p.err, kErrMmaWait);
+    tc_fence_after_sync();
+    {
+      float y1[32], y2[32];
+      tmem_ld32(tmem + lane_off + COL_Y1 + 32u * wg, y1);
+      tmem_ld32(tmem + lane_off + COL_Y2 + 32u * wg, y2);
+      tmem_ld_wait();
+      const float el = m.el[r];
+      float out[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float s1v = part ? y1[c] : y1[16 + c];
+        const float s2v = part ? y2[c] : y2[16 + c];
+        const float r1 = __shfl_xor_sync(0xffffffffu, s1v, 16);
+        const float r2 = __shfl_xor_sync(0xffffffffu, s2v, 16);
+        const float a1 = (part ? y1[16 + c] : y1[c]) + r1;
+        const float a2 = (part ? y2[16 + c] : y2[c]) + r2;
+        out[c] = a1 + el * a2;
+      }
+      const int t = t0 + r;
+      if (t < p.T) {
+        float* dst = p.y + (((long long)b * p.T + t) * p.H + h) * 64 + 32 * wg + 16 * part;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<float4*>(dst)[i] =
+              make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+      }
+    }
+    tc_fence_before_sync();
+    ticket = next;
+    ++iter;
+  }
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+// cuTensorMapEncodeTiled is a driver API; it is resolved through the runtime so the library does
+// not link libcuda (it loads on machines without a driver, where only host queries work).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+bool encode_bc_map(CUtensorMap* map, const void* ptr, const Problem& p, const long long st[4]) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (!encode) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)(2 * p.N), (cuuint64_t)p.H, (cuuint64_t)p.T,
+                        (cuuint64_t)p.Bsz};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 8u, (cuuint64_t)st[1] * 8u,
+                           (cuuint64_t)st[0] * 8u};
+  cuuint32_t box[4] = {128u, 1u, 64u, 1u};
+  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  const CUresult rc = encode(
+      map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), dims, strides, box, es,
+      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return rc == CUDA_SUCCESS;
+}
+
+bool bc_tma_ok(const void* ptr, const long long st[4]) {
+  if (st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] <= 0 || (st[i] % 2) != 0) return false;
+  return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0;
+}
+
+}  // namespace
+
+bool fwd_supported(const Problem& p) {
+  if (p.D != 64 || p.N != 64 || p.x_complex) return false;
+  if (!bc_tma_ok(p.Bm, p.bs) || !bc_tma_ok(p.Cm, p.cs)) return false;
+  const long long total = (long long)p.Bsz * p.H * ((p.T + 63) / 64);
+  return total < (1ll << 30);
+}
+
+size_t fwd_workspace_bytes(const Problem& p) {
+  const size_t nc = (size_t)((p.T + 63) / 64);
+  return 256 + 4 * (size_t)p.Bsz * p.H * nc;
+}
+
+int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st) {
+  FwdParams fp{};
+  fp.Bsz = p.Bsz;
+  fp.T = p.T;
+  fp.H = p.H;
+  fp.nc = (p.T + 63) / 64;
+  fp.total = p.Bsz * p.H * fp.nc;
+  fp.x = static_cast<const float*>(p.x);
+  for (int i = 0; i < 4; ++i) fp.xs[i] = p.xs[i];
+  fp.x_vec = (p.xs[3] == 1 && p.xs[0] % 4 == 0 && p.xs[1] % 4 == 0 && p.xs[2] % 4 == 0 &&
+              reinterpret_cast<uintptr_t>(p.x) % 16 == 0)
+                 ? 1
+                 : 0;
+  fp.A = p.A;
+  fp.dt = p.dt;
+  for (int i = 0; i < 3; ++i) fp.dts[i] = p.dts[i];
+  fp.y = y;
+  fp.states = static_cast<float*>(states);
+  uint32_t* w = static_cast<uint32_t*>(ws);
+  fp.err = w;
+  fp.counter = w + 1;
+  fp.flags = w + 64;
+  CUtensorMap tmB, tmC;
+  if (!encode_bc_map(&tmB, p.Bm, p, p.bs) || !encode_bc_map(&tmC, p.Cm, p, p.cs))
+    return M3SSD_ERR_LAUNCH;
+  if (cudaMemsetAsync(ws, 0, fwd_workspace_bytes(p), st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaFuncSetAttribute(k_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes) != cudaSuccess)
+    return M3SSD_ERR_LAUNCH;
+  const int grid = fp.total < sms ? fp.total : sms;
+  k_fwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, fp);
+  return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
+}
+
+}  // namespace tc
+}  // namespace m3ssd

@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libm3ssd.so")
 M3SSD_X_COMPLEX = 0x1
 M3SSD_PREC_AUTO = 0x0
 M3SSD_PREC_FP32 = 0x10
-M3SSD_PREC_TF32 = 0x20
+M3SSD_PREC_TENSOR = 0x20
 
 STATUS_NAMES = {
     0: "OK", 1: "ERR_NULL", 2: "ERR_SHAPE", 3: "ERR_CHUNK", 4: "ERR_DIM_LIMIT", 5: "ERR_ALIGN",

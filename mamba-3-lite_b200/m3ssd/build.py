@@ -80,7 +80,7 @@ def build(force=False, verbose=False, extra_flags=()):
             if err.strip():
                 print(err, file=sys.stderr)
     tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *[o for o, _ in outs], "-lcuda"]
+    cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *[o for o, _ in outs]]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

@@ -22,12 +22,14 @@ Differences from the reference, all deliberate:
   differences.
 * ``ssd_dispatch`` is accepted for call-site compatibility (models/mamba_block.py:100-121 passes
   "triton" or nothing); every value runs the CUDA kernels here.
-* ``precision`` (extra keyword) selects "auto" (default), "fp32" (CUDA cores, fp32 everywhere) or
-  "tf32" (tensor-core tiles where the shape has them).
+* ``precision`` (extra keyword) selects "auto" (default, same as "tensor"), "fp32" (CUDA cores,
+  fp32 everywhere) or "tensor" (tcgen05 tensor-core tiles with split-bf16 operands and fp32
+  accumulation where the shape has them: head_dim = state_dim = 64, real x).
 """
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -35,7 +37,8 @@ from . import _lib
 
 ctypes_ref = ctypes.byref
 
-_PREC = {"auto": _lib.M3SSD_PREC_AUTO, "fp32": _lib.M3SSD_PREC_FP32, "tf32": _lib.M3SSD_PREC_TF32}
+_PREC = {"auto": _lib.M3SSD_PREC_AUTO, "fp32": _lib.M3SSD_PREC_FP32,
+         "tensor": _lib.M3SSD_PREC_TENSOR}
 
 
 def _problem(x, B_t, chunk, flags):
@@ -52,6 +55,17 @@ def _strides(t, n):
 
 def _stream_ptr(device):
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_device_status(ws, what):
+    """With M3SSD_CHECK=1 in the environment, synchronise and raise if a kernel reported a
+    bounded-wait timeout in the workspace status word (a debugging aid; off by default)."""
+    if os.environ.get("M3SSD_CHECK", "0") in ("", "0"):
+        return
+    torch.cuda.synchronize(ws.device)
+    code = int(ws[:4].view(torch.int32).item())
+    if code != 0:
+        raise RuntimeError(f"m3ssd {what}: device status word {code:#x} (bounded wait expired)")
 
 
 def _check_inputs(x, A, B_t, C_t, dt, chunk_size):
@@ -103,7 +117,7 @@ def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tens
     states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
                          device=dev)
     ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
     args = _lib.FwdArgs()
     args.prob = prob
     args.x, args.x_strides = x.data_ptr(), _lib.I64x4(*_strides(x, 4))
@@ -116,6 +130,7 @@ def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tens
     args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes
     with torch.cuda.device(dev):
         _lib.check(lib.m3ssd_fwd(ctypes_ref(args), _stream_ptr(dev)))
+    _check_device_status(ws, "forward")
     return y, states
 
 
@@ -145,7 +160,7 @@ def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tenso
     dC = torch.empty(C_t.shape, dtype=torch.complex64, device=dev)
     ddt = torch.empty(dt.shape, dtype=torch.float32, device=dev)
     ws_bytes = int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
     args = _lib.BwdArgs()
     args.prob = prob
     args.x, args.x_strides = x.data_ptr(), _lib.I64x4(*_strides(x, 4))
@@ -160,6 +175,7 @@ def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tenso
     args.workspace, args.workspace_bytes = ws.data_ptr(), ws_bytes
     with torch.cuda.device(dev):
         _lib.check(lib.m3ssd_bwd(ctypes_ref(args), _stream_ptr(dev)))
+    _check_device_status(ws, "backward")
     return dx, dA, dB, dC, ddt
 
 

@@ -17,7 +17,7 @@ from tolerances import TOL
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-PRECISIONS = ["fp32"]
+PRECISIONS = ["fp32", "tensor"]
 GRAD_KEYS = ("dx", "dA", "dB", "dC", "ddt")
 
 
