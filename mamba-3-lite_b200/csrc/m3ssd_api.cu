@@ -69,6 +69,11 @@ Problem make_problem(const m3ssd_problem* pr) {
   return p;
 }
 
+size_t bwd_ws(const Problem& p) {
+  const size_t a = m3ssd::simt::bwd_workspace_bytes(p), b = m3ssd::tc::bwd_workspace_bytes(p);
+  return a > b ? a : b;
+}
+
 size_t fwd_ws(const Problem& p) {
   const size_t a = m3ssd::simt::fwd_workspace_bytes(p), b = m3ssd::tc::fwd_workspace_bytes(p);
   return a > b ? a : b;
@@ -143,7 +148,7 @@ size_t m3ssd_fwd_workspace_bytes(const m3ssd_problem* prob) {
 
 size_t m3ssd_bwd_workspace_bytes(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  return m3ssd::simt::bwd_workspace_bytes(make_problem(prob));
+  return bwd_ws(make_problem(prob));
 }
 
 const char* m3ssd_fwd_path(const m3ssd_problem* prob) {
@@ -153,12 +158,12 @@ const char* m3ssd_fwd_path(const m3ssd_problem* prob) {
 
 const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return "invalid";
-  return "simt-fp32";
+  return tc_shape(prob) ? "tcgen05-bf16x2" : "simt-fp32";
 }
 
 int m3ssd_launch_count(const m3ssd_problem* prob, int backward) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  if (backward) return m3ssd::simt::kBwdLaunches;
+  if (backward) return tc_shape(prob) ? m3ssd::tc::kBwdLaunches : m3ssd::simt::kBwdLaunches;
   return tc_shape(prob) ? m3ssd::tc::kFwdLaunches : m3ssd::simt::kFwdLaunches;
 }
 
@@ -197,13 +202,18 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   if (!aligned(a->dy, 4) || !aligned(a->states, 16) || !aligned(a->dx, xa) || !aligned(a->dA, 8) ||
       !aligned(a->dB, 8) || !aligned(a->dC, 8) || !aligned(a->ddt, 4))
     return M3SSD_ERR_ALIGN;
-  const size_t need = m3ssd::simt::bwd_workspace_bytes(p);
+  const size_t need = bwd_ws(p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
   if (rc) return rc;
   long long dys[4];
   for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
+  if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p))
+    return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, static_cast<float*>(a->dx),
+                              static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
+                              static_cast<float2*>(a->dC), a->ddt, a->workspace,
+                              static_cast<cudaStream_t>(stream));
   return m3ssd::simt::run_bwd(p, a->dy, dys, a->states, a->dx, static_cast<float2*>(a->dA),
                               static_cast<float2*>(a->dB), static_cast<float2*>(a->dC), a->ddt,
                               a->workspace, static_cast<cudaStream_t>(stream));

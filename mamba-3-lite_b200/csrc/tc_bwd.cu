@@ -1,0 +1,834 @@
+// Tensor-core backward of the complex chunkwise SSD for head_dim = state_dim = 64, real x.
+//
+// Persistent CTAs take chunk tickets in reverse chunk order. With the forward's rotated
+// operands (C' = C cis(theta_l), B' = B conj(cis(theta_s)), Mr = exp(rho_l - rho_s) Re(C'B'^T)
+// for s <= l, dec_s = exp(rho_Gamma - rho_s), e_l = exp(rho_l)) and dS_z the gradient of the
+// state leaving chunk z (the reverse scan of the decay_chunk carry, models/ssd_complex.py:98-111):
+//
+//   dM  = dy x^T,  dG' = exp(rho_l - rho_s) dM  (s <= l)                 (through :50-53)
+//   dx  = Mr^T dy + dec_s Re(conj(B') dS'),       dS' = conj(cis(theta_Gamma)) dS_z
+//   dC' = dG' conj(B') + e_l dy conj(H_z)^T,      dC = dC' conj(cis(theta_l))   (:53, :115)
+//   dB' = dG'^T conj(C') + dec_s x dS'^T,         dB = dB' cis(theta_s)          (:53, :54)
+//   dS_{z-1} = e_l-weighted conj(C')^T dy + conj(e^Gamma) dS_z                    (carry)
+//   d Sigma_l = sum_n dC conj(C) - sum_n dB conj(B) + [l = 63] <dS_z, H_{z+1}>
+//   d a_t = reverse within-chunk cumsum of d Sigma;  ddt = Re(da conj(A)) softplus'(dt),
+//   dA = sum da softplus(dt)                                                       (:82, :89)
+//
+// The d Sigma identity holds because every use of C[l] carries e^{Sigma_l}, every use of B[s]
+// carries e^{-Sigma_s}, and Gamma enters only through H_{z+1}. Nine contractions per chunk run on
+// tcgen05 (kind::f16) with split-bf16 operands stacked in groups of 8 rows (stack8) so each
+// shared buffer serves as a stacked A operand and as a plain B operand. dS_z is handed from the
+// CTA that processed chunk z+1 through a 4-slot ring in global memory (L2) with release flags.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include "m3ssd_common.cuh"
+#include "tc_common.cuh"
+#include "tc_path.h"
+
+namespace m3ssd {
+namespace tc {
+
+namespace {
+
+constexpr int kThreads = 256;
+// shared memory map
+constexpr uint32_t OFF_C = 0;        // C'x stacked [2 k-atoms][128][64]; raw C tile lands first
+constexpr uint32_t OFF_B = 32768;    // B'x (conjugate-interleaved) stacked; raw B tile lands first
+constexpr uint32_t OFF_X = 65536;    // x stacked over s [128][64 p]
+constexpr uint32_t OFF_DY = 81920;   // dy stacked over l [128][64 p]
+constexpr uint32_t OFF_DYT = 98304;  // e_l dy stacked over p, MN [2][64 l][64]; then Mr (same form)
+constexpr uint32_t OFF_DGK = 114688; // dG' stacked over l [128][64 s]
+constexpr uint32_t OFF_DGM = 131072; // dG' stacked over s, MN [2][64 l][64]
+constexpr uint32_t OFF_DS = 147456;  // dS'x hi [2][64 p][64 k], lo at +16384
+constexpr uint32_t OFF_H = 180224;   // conj(H_z) hi [2][64 p][64 k], lo at +16384
+constexpr uint32_t OFF_MISC = 212992;
+constexpr uint32_t kMiscBytes = 8192;
+constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBytes + 1024;
+constexpr uint32_t kTmaBytes = 2u * 64u * 128u * 4u;
+constexpr uint32_t kTmemCols = 512;
+// TMEM columns: batch 1, batch 2, batch 3 (reusing batch-1 columns), dBb (reusing dCa)
+constexpr uint32_t COL_G = 0, COL_DM = 64, COL_Q = 128, COL_DCA = 256, COL_DCB = 384;
+constexpr uint32_t COL_DXA = 0, COL_DXB = 64, COL_DBA = 128, COL_DBB = 256;
+
+struct Misc {
+  uint64_t bar_tma, bar1, bar2, bar3, bar4;
+  float rho[64], el[64], dec[64], sp[64], dsp[64];
+  float2 cis[64];
+  float2 rc[4][64];
+  float2 rb[4][64];
+  float2 dgw[8];
+  float2 dap[2];
+  float2 carry, gam, g, ct, sfx;
+  int first, nxt;
+  uint32_t tmem_base;
+};
+static_assert(sizeof(Misc) <= kMiscBytes, "misc area");
+
+struct BwdParams {
+  int Bsz, T, H, nc, total;
+  const float* x;
+  long long xs[4];
+  int x_vec;
+  const float* dy;
+  long long dys[4];
+  int dy_vec;
+  const float2* A;
+  const float* dt;
+  long long dts[3];
+  const float* states;
+  float* dx;
+  float2* dB;
+  float2* dC;
+  float* ddt;
+  float2* dapart;
+  float* ring;
+  uint32_t* flags;
+  uint32_t* counter;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ void load16(const float* base_ptr, const long long st[4], int vec, int T,
+                                       int b, int t, int h, int p0, float (&v)[16]) {
+  if (t >= T) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    return;
+  }
+  const float* base = base_ptr + b * st[0] + (long long)t * st[1] + h * st[2];
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 q = ldg_nc_v4(base + p0 + 4 * i);
+      v[4 * i] = q.x;
+      v[4 * i + 1] = q.y;
+      v[4 * i + 2] = q.z;
+      v[4 * i + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __ldg(base + (long long)(p0 + i) * st[3]);
+  }
+}
+
+__device__ __forceinline__ float2 cmul2(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+// x32 load of a 64-column accumulator block, hi/lo partner exchange: thread `part` keeps 16
+// columns (part 0: first 16, part 1: last 16) of the 32 its warp group owns.
+__device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)[16]) {
+  float v[32];
+  tmem_ld32(taddr, v);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const float send = part ? v[c] : v[16 + c];
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 8);
+    out[c] = (part ? v[16 + c] : v[c]) + recv;
+  }
+}
+// two x32 loads of a 128-column accumulator block (the warp group's 64 columns), exchange:
+// thread `part` keeps 32 columns.
+__device__ __forceinline__ void ld_exch32(uint32_t taddr, int part, float (&out)[32]) {
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    float v[32];
+    tmem_ld32(taddr + 32u * ch, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const float t = __shfl_xor_sync(0xffffffffu, v[c], 8);
+      if (part == ch) out[c] = v[c] + t;
+    }
+  }
+}
+
+__device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
+  float w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = v[i];
+  uint4 h, l;
+  split8(w, h, l);
+  st_shared_v4(hi_addr, h);
+  st_shared_v4(lo_addr, l);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_bwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+             const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = smem_u32(smem);
+  Misc& m = *reinterpret_cast<Misc*>(smem + OFF_MISC);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sub = warp & 3, wg = warp >> 2;
+  const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
+  const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
+  const int BH = p.Bsz * p.H;
+
+  int first = 0;
+  if (tid == 0) {
+    mbar_init(&m.bar_tma, 1);
+    mbar_init(&m.bar1, 1);
+    mbar_init(&m.bar2, 1);
+    mbar_init(&m.bar3, 1);
+    mbar_init(&m.bar4, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+    first = (int)atomicAdd(p.counter, 1u);
+    m.nxt = (int)atomicAdd(p.counter, 1u);
+    m.first = first;
+  }
+  if (warp == 0) {
+    tmem_alloc(&m.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = m.tmem_base;
+  const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
+  int ticket = m.first;
+
+  float xv[16], gv[16];
+  float dtv = 0.f;
+  auto prefetch_regs = [&](int tk) {
+    const int zr = tk / BH, bh = tk - zr * BH;
+    const int z = p.nc - 1 - zr;
+    const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
+    load16(p.x, p.xs, p.x_vec, p.T, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
+    load16(p.dy, p.dys, p.dy_vec, p.T, b, t0 + (tid >> 2), h, 16 * (tid & 3), gv);
+    dtv = 0.f;
+    if (tid < 64 && t0 + tid < p.T)
+      dtv = __ldg(p.dt + b * p.dts[0] + (long long)(t0 + tid) * p.dts[1] + h * p.dts[2]);
+  };
+  if (ticket < p.total) prefetch_regs(ticket);
+
+  uint32_t iter = 0;
+  while (ticket < p.total) {
+    const uint32_t ph = iter & 1u;
+    const int zr = ticket / BH, bh = ticket - zr * BH;
+    const int z = p.nc - 1 - zr;
+    const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
+    __syncthreads();  // previous ticket complete (including generic reads of sB / sC)
+    const int next = m.nxt;
+    int nn = 0;
+    if (tid == 0) {
+      nn = (int)atomicAdd(p.counter, 1u);
+      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes);
+      tma_load_4d(smem + OFF_B, &tmB, &m.bar_tma, 0, h, t0, b);
+      tma_load_4d(smem + OFF_C, &tmC, &m.bar_tma, 0, h, t0, b);
+    }
+
+    // ---- within-chunk cumsum of a = softplus(dt) A
+    if (tid < 64) {
+      const float2 A = p.A[h];
+      float2 a = make_float2(0.f, 0.f);
+      float spv = 0.f, dspv = 0.f;
+      if (t0 + tid < p.T) {
+        spv = softplus_f(dtv);
+        dspv = softplus_grad_f(dtv);
+        a = make_float2(spv * A.x, spv * A.y);
+      }
+      m.sp[tid] = spv;
+      m.dsp[tid] = dspv;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float ux = __shfl_up_sync(0xffffffffu, a.x, o);
+        const float uy = __shfl_up_sync(0xffffffffu, a.y, o);
+        if (lane >= o) {
+          a.x += ux;
+          a.y += uy;
+        }
+      }
+      if (tid == 31) m.carry = a;
+      m.rho[tid] = a.x;
+      m.el[tid] = a.y;
+    }
+    __syncthreads();
+    if (tid < 64) {
+      float rx = m.rho[tid], ry = m.el[tid];
+      if (tid >= 32) {
+        rx += m.carry.x;
+        ry += m.carry.y;
+      }
+      float sn, cs;
+      sincosf(ry, &sn, &cs);
+      m.rho[tid] = rx;
+      m.cis[tid] = make_float2(cs, sn);
+      if (tid == 63) m.gam = make_float2(rx, ry);
+    }
+    __syncthreads();
+    if (tid < 64) {
+      const float rx = m.rho[tid];
+      m.el[tid] = expf(rx);
+      m.dec[tid] = expf(m.gam.x - rx);
+      if (tid == 0) {
+        const float mg = expf(m.gam.x);
+        float sn, cs;
+        sincosf(m.gam.y, &sn, &cs);
+        m.g = make_float2(mg * cs, mg * sn);
+        m.ct = make_float2(cs, sn);
+      }
+    }
+    __syncthreads();
+
+    // ---- x, dy (stacked over rows, K = p) and e_l dy (stacked over p, MN) from registers
+    {
+      const int s = tid >> 2, pg = tid & 3;
+      split8_store(sb + OFF_X + swz(stack8(s, 0), 2 * pg), sb + OFF_X + swz(stack8(s, 1), 2 * pg),
+                   xv);
+      split8_store(sb + OFF_X + swz(stack8(s, 0), 2 * pg + 1),
+                   sb + OFF_X + swz(stack8(s, 1), 2 * pg + 1), xv + 8);
+      split8_store(sb + OFF_DY + swz(stack8(s, 0), 2 * pg),
+                   sb + OFF_DY + swz(stack8(s, 1), 2 * pg), gv);
+      split8_store(sb + OFF_DY + swz(stack8(s, 0), 2 * pg + 1),
+                   sb + OFF_DY + swz(stack8(s, 1), 2 * pg + 1), gv + 8);
+      const float e = m.el[s];
+      float w[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) w[u] = e * gv[u];
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        const uint32_t mh = stack8((uint32_t)(16 * pg + 8 * blk), 0u);
+        const uint32_t ml = stack8((uint32_t)(16 * pg + 8 * blk), 1u);
+        split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(s, (mh & 63u) >> 3),
+                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w + 8 * blk);
+      }
+    }
+
+    // ---- raw B, C tiles -> registers -> rotated, split, stacked operands (in place)
+    mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);
+    {
+      float4 rb4[4][2], rc4[4][2];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int j = tid + kThreads * it;
+        const int l = j >> 4, q = j & 15;
+        const float* rB = reinterpret_cast<const float*>(smem + OFF_B) + l * 128 + 8 * q;
+        const float* rC = reinterpret_cast<const float*>(smem + OFF_C) + l * 128 + 8 * q;
+        rb4[it][0] = *reinterpret_cast<const float4*>(rB);
+        rb4[it][1] = *reinterpret_cast<const float4*>(rB + 4);
+        rc4[it][0] = *reinterpret_cast<const float4*>(rC);
+        rc4[it][1] = *reinterpret_cast<const float4*>(rC + 4);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int j = tid + kThreads * it;
+        const int l = j >> 4, q = j & 15;
+        const float2 cs = m.cis[l];
+        const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
+        const float cr[8] = {rc4[it][0].x, rc4[it][0].y, rc4[it][0].z, rc4[it][0].w,
+                             rc4[it][1].x, rc4[it][1].y, rc4[it][1].z, rc4[it][1].w};
+        const float br[8] = {rb4[it][0].x, rb4[it][0].y, rb4[it][0].z, rb4[it][0].w,
+                             rb4[it][1].x, rb4[it][1].y, rb4[it][1].z, rb4[it][1].w};
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          v[2 * u] = cr[2 * u] * cs.x - cr[2 * u + 1] * cs.y;
+          v[2 * u + 1] = cr[2 * u] * cs.y + cr[2 * u + 1] * cs.x;
+        }
+        split8_store(sb + OFF_C + ka * 16384u + swz(stack8(l, 0), ch),
+                     sb + OFF_C + ka * 16384u + swz(stack8(l, 1), ch), v);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          v[2 * u] = br[2 * u] * cs.x + br[2 * u + 1] * cs.y;
+          v[2 * u + 1] = br[2 * u] * cs.y - br[2 * u + 1] * cs.x;
+        }
+        split8_store(sb + OFF_B + ka * 16384u + swz(stack8(l, 0), ch),
+                     sb + OFF_B + ka * 16384u + swz(stack8(l, 1), ch), v);
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    // ---- batch 1: G = C'x B'x^T, dM = dy x^T, Q^T = (e dy)^T C'x
+    if (tid == 0) {
+      tc_fence_after_sync();
+      const uint32_t id64 = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t ko = (j >> 2) * 16384u + (j & 3) * 32u;
+          mma_bf16_ss(tmem + COL_G, sdesc(sb + OFF_C + ko, 16, 1024),
+                      sdesc(sb + OFF_B + ko + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
+        }
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_DM, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
+                      sdesc(sb + OFF_X + j * 32u + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
+      const uint32_t idq = idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_Q, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
+                      sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idq, (hp | j) != 0);
+      mma_commit(&m.bar1);
+    }
+
+    // ---- H_z (conj) -> sH; dS_z from the next chunk; <dS_z, H_{z+1}>; dS' -> sDS
+    const int kb = 64 * wg + 32 * part;
+    float dsz[32];
+    {
+      float hz[32];
+      const float* hrow = p.states + (((long long)bh * p.nc + z) * 64 + r) * 128 + kb;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(hrow) + i);
+        hz[4 * i] = v.x;
+        hz[4 * i + 1] = -v.y;
+        hz[4 * i + 2] = v.z;
+        hz[4 * i + 3] = -v.w;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        split8_store(sb + OFF_H + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                     sb + OFF_H + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                     hz + 8 * jj);
+    }
+    if (z < p.nc - 1) {
+      if (tid == 0) {
+        const uint32_t* f = p.flags + (long long)bh * p.nc + z;
+        uint32_t i = 0;
+        for (; i < kSpinLimit; ++i) {
+          if (ld_acquire_gpu(f) != 0u) break;
+          __nanosleep(128);
+        }
+        if (i == kSpinLimit) atomicOr(p.err, kErrFlagWait);
+        __threadfence();
+      }
+      __syncthreads();
+      const float* drow = p.ring + (((long long)bh * 4 + (z & 3)) * 64 + r) * 128 + kb;
+      const float* h1row = p.states + (((long long)bh * p.nc + z + 1) * 64 + r) * 128 + kb;
+      float2 dg = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(drow) + i);
+        const float4 hv = __ldcg(reinterpret_cast<const float4*>(h1row) + i);
+        dsz[4 * i] = v.x;
+        dsz[4 * i + 1] = v.y;
+        dsz[4 * i + 2] = v.z;
+        dsz[4 * i + 3] = v.w;
+        // dS conj(H_{z+1})
+        dg.x += v.x * hv.x + v.y * hv.y + v.z * hv.z + v.w * hv.w;
+        dg.y += v.y * hv.x - v.x * hv.y + v.w * hv.z - v.z * hv.w;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
+        dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
+      }
+      if (lane == 0) m.dgw[warp] = dg;
+    } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) dsz[c] = 0.f;
+      if (lane == 0) m.dgw[warp] = make_float2(0.f, 0.f);
+    }
+    {
+      // dS'x = interleaved (Re, -Im) of conj(cis(theta_Gamma)) dS_z
+      const float2 ct = m.ct;
+      float w[32];
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        const float re = dsz[c] * ct.x + dsz[c + 1] * ct.y;
+        const float im = dsz[c + 1] * ct.x - dsz[c] * ct.y;
+        w[c] = re;
+        w[c + 1] = -im;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        split8_store(sb + OFF_DS + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                     sb + OFF_DS + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                     w + 8 * jj);
+    }
+
+    // ---- epilogue 1: Mr, dG' (two forms)
+    mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
+    tc_fence_after_sync();
+    {
+      float gs[16], ms[16];
+      ld_exch16(tmem + lane_off + COL_G + 32u * wg, part, gs);
+      ld_exch16(tmem + lane_off + COL_DM + 32u * wg, part, ms);
+      const int s0 = 32 * wg + 16 * part;
+      const float rl = m.rho[r];
+      float mrv[16], dgv[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const int s = s0 + c;
+        const float L = (s <= r) ? expf(rl - m.rho[s]) : 0.f;
+        mrv[c] = L * gs[c];
+        dgv[c] = L * ms[c];
+      }
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        const uint32_t mh = stack8((uint32_t)(s0 + 8 * blk), 0u);
+        const uint32_t ml = stack8((uint32_t)(s0 + 8 * blk), 1u);
+        split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
+                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), mrv + 8 * blk);
+        split8_store(sb + OFF_DGM + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
+                     sb + OFF_DGM + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), dgv + 8 * blk);
+        split8_store(sb + OFF_DGK + swz(stack8(r, 0), (s0 >> 3) + blk),
+                     sb + OFF_DGK + swz(stack8(r, 1), (s0 >> 3) + blk), dgv + 8 * blk);
+      }
+    }
+    // ---- state-gradient carry: dS_{z-1} = Q + conj(e^Gamma) dS_z, published for chunk z-1
+    {
+      float q[32];
+      ld_exch32(tmem + lane_off + COL_Q + 64u * wg, part, q);
+      if (z > 0) {
+        const float2 g = m.g;
+        float* drow = p.ring + (((long long)bh * 4 + ((z - 1) & 3)) * 64 + r) * 128 + kb;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float o[4];
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const int c = 4 * i + u;
+            const float qr = q[c], qi = -q[c + 1];
+            o[u] = qr + g.x * dsz[c] + g.y * dsz[c + 1];
+            o[u + 1] = qi + g.x * dsz[c + 1] - g.y * dsz[c];
+          }
+          __stcg(reinterpret_cast<float4*>(drow) + i, make_float4(o[0], o[1], o[2], o[3]));
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      if (z > 0) {
+        __threadfence();
+        st_release_gpu(p.flags + (long long)bh * p.nc + z - 1, 1u);
+      }
+      tc_fence_after_sync();
+      // batch 2: dCa = dG' B'x (MN), dCb = dy conj(H)
+      const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_DCA, sdesc(sb + OFF_DGK + j * 32u, 16, 1024),
+                      sdesc(sb + OFF_B + j * 4096u + hp * 1024u, 16384, 2048), id128,
+                      (hp | j) != 0);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_DCB, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
+                      sdesc(sb + OFF_H + hp * 16384u + j * 2048u, 8192, 1024), id128,
+                      (hp | j) != 0);
+      mma_commit(&m.bar2);
+      // batch 3: dXa = Mr^T dy, dXb = B'x dS'x, dBa = dG'^T C'x
+      const uint32_t idxa = idesc_bf16(128, 64, 1, 1);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_DXA, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
+                      sdesc(sb + OFF_DY + j * 4096u + hp * 1024u, 8192, 2048), idxa,
+                      (hp | j) != 0);
+      const uint32_t idxb = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          mma_bf16_ss(tmem + COL_DXB,
+                      sdesc(sb + OFF_B + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
+                      sdesc(sb + OFF_DS + hp * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16,
+                            1024),
+                      idxb, (hp | j) != 0);
+      const uint32_t idba = idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_DBA, sdesc(sb + OFF_DGM + j * 2048u, 8192, 1024),
+                      sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idba,
+                      (hp | j) != 0);
+      mma_commit(&m.bar3);
+    }
+    // prefetch the next ticket's x, dy, dt while the MMAs run
+    if (next < p.total) prefetch_regs(next);
+
+    // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)); row sums dC' conj(C')
+    mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
+    tc_fence_after_sync();
+    {
+      float ca[32], cb[32];
+      ld_exch32(tmem + lane_off + COL_DCA + 64u * wg, part, ca);
+      ld_exch32(tmem + lane_off + COL_DCB + 64u * wg, part, cb);
+      const float e = m.el[r];
+      const float2 cs = m.cis[r];
+      float out[32];
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const uint4 hi = ld_shared_u4(sb + OFF_C + (uint32_t)wg * 16384u + swz(stack8(r, 0), 4 * part + jj));
+        const uint4 lo = ld_shared_u4(sb + OFF_C + (uint32_t)wg * 16384u + swz(stack8(r, 1), 4 * part + jj));
+        const float2 c0 = unsplit2(hi.x, lo.x), c1 = unsplit2(hi.y, lo.y);
+        const float2 c2 = unsplit2(hi.z, lo.z), c3 = unsplit2(hi.w, lo.w);
+        const float2 cv[4] = {c0, c1, c2, c3};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = 8 * jj + 2 * u;
+          const float2 d = make_float2(ca[c] + e * cb[c], ca[c + 1] + e * cb[c + 1]);  // dC'
+          acc.x += d.x * cv[u].x + d.y * cv[u].y;  // dC' conj(C')
+          acc.y += d.y * cv[u].x - d.x * cv[u].y;
+          const float2 o = cmul2(d, make_float2(cs.x, -cs.y));
+          out[c] = o.x;
+          out[c + 1] = o.y;
+        }
+      }
+      m.rc[2 * wg + part][r] = acc;
+      const int t = t0 + r;
+      if (t < p.T) {
+        float* dst = reinterpret_cast<float*>(p.dC + (((long long)b * p.T + t) * p.H + h) * 64) + kb;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(dst)[i] =
+              make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+      }
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // dBb = x dS'x^T (MN), into the columns dCa used
+      tc_fence_after_sync();
+      const uint32_t idbb = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_DBB, sdesc(sb + OFF_X + j * 32u, 16, 1024),
+                      sdesc(sb + OFF_DS + hp * 16384u + j * 2048u, 8192, 1024), idbb,
+                      (hp | j) != 0);
+      mma_commit(&m.bar4);
+    }
+
+    // ---- epilogue 3: dx = dXa + dec_s dXb
+    mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
+    tc_fence_after_sync();
+    {
+      float xa[16], xb[16];
+      ld_exch16(tmem + lane_off + COL_DXA + 32u * wg, part, xa);
+      ld_exch16(tmem + lane_off + COL_DXB + 32u * wg, part, xb);
+      const float d = m.dec[r];
+      const int t = t0 + r;
+      if (t < p.T) {
+        float* dst = p.dx + (((long long)b * p.T + t) * p.H + h) * 64 + 32 * wg + 16 * part;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<float4*>(dst)[i] =
+              make_float4(xa[4 * i] + d * xb[4 * i], xa[4 * i + 1] + d * xb[4 * i + 1],
+                          xa[4 * i + 2] + d * xb[4 * i + 2], xa[4 * i + 3] + d * xb[4 * i + 3]);
+      }
+    }
+    // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s); row sums dB' conj(B')
+    mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
+    tc_fence_after_sync();
+    {
+      float ba[32], bbv[32];
+      ld_exch32(tmem + lane_off + COL_DBA + 64u * wg, part, ba);
+      ld_exch32(tmem + lane_off + COL_DBB + 64u * wg, part, bbv);
+      const float d = m.dec[r];
+      const float2 cs = m.cis[r];
+      float out[32];
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const uint4 hi = ld_shared_u4(sb + OFF_B + (uint32_t)wg * 16384u + swz(stack8(r, 0), 4 * part + jj));
+        const uint4 lo = ld_shared_u4(sb + OFF_B + (uint32_t)wg * 16384u + swz(stack8(r, 1), 4 * part + jj));
+        const float2 b0 = unsplit2(hi.x, lo.x), b1 = unsplit2(hi.y, lo.y);
+        const float2 b2 = unsplit2(hi.z, lo.z), b3 = unsplit2(hi.w, lo.w);
+        const float2 bv[4] = {b0, b1, b2, b3};  // conj(B') as stored
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = 8 * jj + 2 * u;
+          const float2 dbp = make_float2(ba[c] + d * bbv[c], -(ba[c + 1] + d * bbv[c + 1]));
+          acc.x += dbp.x * bv[u].x - dbp.y * bv[u].y;  // dB' conj(B')
+          acc.y += dbp.x * bv[u].y + dbp.y * bv[u].x;
+          const float2 o = cmul2(dbp, cs);
+          out[c] = o.x;
+          out[c + 1] = o.y;
+        }
+      }
+      m.rb[2 * wg + part][r] = acc;
+      const int t = t0 + r;
+      if (t < p.T) {
+        float* dst = reinterpret_cast<float*>(p.dB + (((long long)b * p.T + t) * p.H + h) * 64) + kb;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(dst)[i] =
+              make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before_sync();
+    __syncthreads();
+
+    // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial
+    float2 ds = make_float2(0.f, 0.f);
+    if (tid < 64) {
+      const int l = tid;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ds.x += m.rc[j][l].x - m.rb[j][l].x;
+        ds.y += m.rc[j][l].y - m.rb[j][l].y;
+      }
+      if (l == 63) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          ds.x += m.dgw[w].x;
+          ds.y += m.dgw[w].y;
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {  // suffix sum within the warp
+        const float ux = __shfl_down_sync(0xffffffffu, ds.x, o);
+        const float uy = __shfl_down_sync(0xffffffffu, ds.y, o);
+        if (lane + o < 32) {
+          ds.x += ux;
+          ds.y += uy;
+        }
+      }
+      if (tid == 32) m.sfx = ds;  // sum over positions 32..63
+    }
+    __syncthreads();
+    if (tid < 64) {
+      float2 da = ds;
+      if (tid < 32) {
+        da.x += m.sfx.x;
+        da.y += m.sfx.y;
+      }
+      const int t = t0 + tid;
+      const float2 A = p.A[h];
+      float2 dap = make_float2(0.f, 0.f);
+      if (t < p.T) {
+        p.ddt[((long long)b * p.T + t) * p.H + h] = (da.x * A.x + da.y * A.y) * m.dsp[tid];
+        dap = make_float2(da.x * m.sp[tid], da.y * m.sp[tid]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        dap.x += __shfl_xor_sync(0xffffffffu, dap.x, o);
+        dap.y += __shfl_xor_sync(0xffffffffu, dap.y, o);
+      }
+      if (lane == 0) m.dap[tid >> 5] = dap;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      p.dapart[(long long)bh * p.nc + z] =
+          make_float2(m.dap[0].x + m.dap[1].x, m.dap[0].y + m.dap[1].y);
+      m.nxt = nn;
+    }
+    ticket = next;
+    ++iter;
+  }
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// dA[h] = sum over batch and chunks of the per-chunk partials (fixed order)
+__global__ void k_bwd_tc_dA(const float2* __restrict__ dapart, int Bsz, int H, int nc,
+                            float2* __restrict__ dA) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= H) return;
+  float2 acc = make_float2(0.f, 0.f);
+  for (int b = 0; b < Bsz; ++b)
+    for (int z = 0; z < nc; ++z) {
+      const float2 v = dapart[((long long)b * H + h) * nc + z];
+      acc.x += v.x;
+      acc.y += v.y;
+    }
+  dA[h] = acc;
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+struct BwdLayout {
+  size_t flags, ring, dapart, total;
+};
+
+BwdLayout bwd_layout(const Problem& p) {
+  const size_t bh = (size_t)p.Bsz * p.H, nc = (size_t)((p.T + 63) / 64);
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  BwdLayout L;
+  L.flags = 256;
+  L.ring = al(L.flags + 4 * bh * nc);
+  L.dapart = al(L.ring + bh * 4 * 64 * 128 * sizeof(float));
+  L.total = al(L.dapart + bh * nc * sizeof(float2));
+  return L;
+}
+
+}  // namespace
+
+bool bwd_supported(const Problem& p) { return fwd_supported(p); }
+
+size_t bwd_workspace_bytes(const Problem& p) { return bwd_layout(p).total; }
+
+int run_bwd(const Problem& p, const float* dy, const long long dys[4], const void* states,
+            float* dx, float2* dA, float2* dB, float2* dC, float* ddt, void* ws,
+            cudaStream_t st) {
+  const BwdLayout L = bwd_layout(p);
+  BwdParams bp{};
+  bp.Bsz = p.Bsz;
+  bp.T = p.T;
+  bp.H = p.H;
+  bp.nc = (p.T + 63) / 64;
+  bp.total = p.Bsz * p.H * bp.nc;
+  bp.x = static_cast<const float*>(p.x);
+  for (int i = 0; i < 4; ++i) bp.xs[i] = p.xs[i];
+  bp.x_vec = (p.xs[3] == 1 && p.xs[0] % 4 == 0 && p.xs[1] % 4 == 0 && p.xs[2] % 4 == 0 &&
+              reinterpret_cast<uintptr_t>(p.x) % 16 == 0)
+                 ? 1
+                 : 0;
+  bp.dy = dy;
+  for (int i = 0; i < 4; ++i) bp.dys[i] = dys[i];
+  bp.dy_vec = (dys[3] == 1 && dys[0] % 4 == 0 && dys[1] % 4 == 0 && dys[2] % 4 == 0 &&
+               reinterpret_cast<uintptr_t>(dy) % 16 == 0)
+                  ? 1
+                  : 0;
+  bp.A = p.A;
+  bp.dt = p.dt;
+  for (int i = 0; i < 3; ++i) bp.dts[i] = p.dts[i];
+  bp.states = static_cast<const float*>(states);
+  bp.dx = dx;
+  bp.dB = dB;
+  bp.dC = dC;
+  bp.ddt = ddt;
+  char* base = static_cast<char*>(ws);
+  bp.err = reinterpret_cast<uint32_t*>(base);
+  bp.counter = reinterpret_cast<uint32_t*>(base) + 1;
+  bp.flags = reinterpret_cast<uint32_t*>(base + L.flags);
+  bp.ring = reinterpret_cast<float*>(base + L.ring);
+  bp.dapart = reinterpret_cast<float2*>(base + L.dapart);
+  CUtensorMap tmB, tmC;
+  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
+    return M3SSD_ERR_LAUNCH;
+  if (cudaMemsetAsync(ws, 0, L.ring, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaFuncSetAttribute(k_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes) != cudaSuccess)
+    return M3SSD_ERR_LAUNCH;
+  const int grid = bp.total < sms ? bp.total : sms;
+  k_bwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, bp);
+  k_bwd_tc_dA<<<(p.H + 127) / 128, 128, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, dA);
+  return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
+}
+
+}  // namespace tc
+}  // namespace m3ssd

@@ -216,3 +216,36 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
 
 }  // namespace tc
 }  // namespace m3ssd
+
+namespace m3ssd {
+namespace tc {
+// Stacked M = 128 row for part (0 = hi, 1 = lo) of logical row r (0..63), interleaved in groups
+// of 8: rows 16g..16g+7 hold hi of r = 8g..8g+7 and rows 16g+8..16g+15 the lo. The hi (or lo)
+// rows alone then form a regular 8-row-group layout with a 2048-byte group stride, so the same
+// buffer is also a plain 64-row operand (B role, or K rows of an MN-major operand), and the hi
+// and lo partial sums of one output row sit in TMEM lanes m and m ^ 8 of the same warp.
+__device__ __forceinline__ uint32_t stack8(uint32_t r, uint32_t part) {
+  return ((r >> 3) << 4) | (part << 3) | (r & 7u);
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t saddr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(saddr));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t saddr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(saddr));
+  return v;
+}
+// hi + lo of a packed bf16 pair -> two floats
+__device__ __forceinline__ float2 unsplit2(uint32_t hi, uint32_t lo) {
+  const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xFFFF0000u);
+  const float l0 = __uint_as_float(lo << 16), l1 = __uint_as_float(lo & 0xFFFF0000u);
+  return make_float2(h0 + l0, h1 + l1);
+}
+}  // namespace tc
+}  // namespace m3ssd

@@ -508,9 +508,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------------------------
 namespace {
 
+bool bc_tma_ok(const void* ptr, const long long st[4]) {
+  if (st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] <= 0 || (st[i] % 2) != 0) return false;
+  return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0;
+}
+
+}  // namespace
+
 // cuTensorMapEncodeTiled is a driver API; it is resolved through the runtime so the library does
 // not link libcuda (it loads on machines without a driver, where only host queries work).
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* ptr = nullptr;
@@ -523,7 +532,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool encode_bc_map(CUtensorMap* map, const void* ptr, const Problem& p, const long long st[4]) {
+static bool encode_bc_map_impl(CUtensorMap* map, const void* ptr, const Problem& p, const long long st[4]) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   if (!encode) return false;
   cuuint64_t dims[4] = {(cuuint64_t)(2 * p.N), (cuuint64_t)p.H, (cuuint64_t)p.T,
@@ -539,14 +548,10 @@ bool encode_bc_map(CUtensorMap* map, const void* ptr, const Problem& p, const lo
   return rc == CUDA_SUCCESS;
 }
 
-bool bc_tma_ok(const void* ptr, const long long st[4]) {
-  if (st[3] != 1) return false;
-  for (int i = 0; i < 3; ++i)
-    if (st[i] <= 0 || (st[i] % 2) != 0) return false;
-  return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0;
+bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
+                          const long long st[4]) {
+  return encode_bc_map_impl(map, ptr, p, st);
 }
-
-}  // namespace
 
 bool fwd_supported(const Problem& p) {
   if (p.D != 64 || p.N != 64 || p.x_complex) return false;
@@ -583,7 +588,7 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   fp.counter = w + 1;
   fp.flags = w + 64;
   CUtensorMap tmB, tmC;
-  if (!encode_bc_map(&tmB, p.Bm, p, p.bs) || !encode_bc_map(&tmC, p.Cm, p, p.cs))
+  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
     return M3SSD_ERR_LAUNCH;
   if (cudaMemsetAsync(ws, 0, fwd_workspace_bytes(p), st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   int dev = 0, sms = 0;

@@ -1,6 +1,7 @@
 // Host entry points of the tensor-core (tcgen05, split-bf16) path.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -12,13 +13,24 @@ namespace tc {
 // The tensor-core path blocks the sequence in chunks of 64 positions internally.
 constexpr int kChunk = 64;
 
-// kernels enqueued by one run_fwd call (the memset of the flag area is not a kernel)
+// kernels enqueued by one run_fwd / run_bwd call (memsets of the flag areas are not kernels)
 constexpr int kFwdLaunches = 1;
+constexpr int kBwdLaunches = 2;
+
+// TMA descriptor for a (B, T, H, N) complex64 tensor viewed as (B, T, H, 2N) fp32, box of
+// 64 time steps x 2N floats of one head (zero fill past T)
+bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
+                          const long long st[4]);
 
 // head_dim = state_dim = 64, real x, B/C with contiguous state dim and 16-byte aligned strides
 bool fwd_supported(const Problem& p);
 size_t fwd_workspace_bytes(const Problem& p);
 int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st);
+
+bool bwd_supported(const Problem& p);
+size_t bwd_workspace_bytes(const Problem& p);
+int run_bwd(const Problem& p, const float* dy, const long long dys[4], const void* states,
+            float* dx, float2* dA, float2* dB, float2* dC, float* ddt, void* ws, cudaStream_t st);
 
 }  // namespace tc
 }  // namespace m3ssd
