@@ -333,7 +333,7 @@ def main():
     dom = ("bwd", bwd_ms, bwd_gbs, BWD_BYTES_PER_TOKHEAD) if bwd_ms >= fwd_ms else \
           ("fwd", fwd_ms, fwd_gbs, FWD_BYTES_PER_TOKHEAD)
     traffic = None
-    tfile = os.path.join(ROOT, "profiles", "traffic.json")
+    tfile = os.path.join(ROOT, "profiles", "dram_traffic.json")
     if os.path.exists(tfile):
         try:
             traffic = json.load(open(tfile)).get(f"{dom[0]}:{fwd_path if dom[0] == 'fwd' else bwd_path}")
