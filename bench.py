@@ -218,10 +218,9 @@ def main():
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    from m3ssd import dist as mdist
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
+        mdist.init_process_group("nccl", timeout_s=120.0, device=dev)
     m3ssd.load()
     B, T, H, D, N = (SHAPE[k] for k in ("B", "T", "H", "D", "N"))
     B = args.batch
@@ -317,10 +316,7 @@ def main():
         e2e_ms = e0.elapsed_time(e1)
 
     # slowest rank
-    vals = torch.tensor([ms, e2e_ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, fwd_ms, bwd_ms = vals.tolist()
+    ms, e2e_ms, fwd_ms, bwd_ms = mdist.max_over_ranks([ms, e2e_ms, fwd_ms, bwd_ms], device=dev)
 
     tokens_per_rank = B * T
     value = world * tokens_per_rank * args.steps / (ms / 1e3) / 1e6
