@@ -55,7 +55,8 @@ typedef enum m3ssd_status {
   M3SSD_ERR_LAUNCH = 7,        /* a kernel launch failed (cudaGetLastError) */
   M3SSD_ERR_DEVICE = 8,        /* current device is not sm_100 or cannot be queried */
   M3SSD_ERR_FLAGS = 9,         /* unknown flag bits */
-  M3SSD_ERR_OVERFLOW = 10      /* a size product overflows the 64-bit index space */
+  M3SSD_ERR_OVERFLOW = 10,     /* a size product overflows the 64-bit index space */
+  M3SSD_ERR_SCRATCH_LIMIT = 11 /* problem too large for m3ssd_fwd_static_scratch */
 } m3ssd_status;
 
 /* device status bits (first word of the workspace) */
@@ -150,6 +151,24 @@ M3SSD_API const char* m3ssd_bwd_path(const m3ssd_problem* prob);
 /* Number of kernel launches one m3ssd_fwd (backward = 0) or m3ssd_bwd (backward = 1) call
  * enqueues for this problem (0 on bad input). Host-only query. */
 M3SSD_API int m3ssd_launch_count(const m3ssd_problem* prob, int backward);
+
+/* Forward that allocates nothing, for callers that cannot allocate device memory when they call
+ * the operator (a serving runtime that plans all device memory up front and forbids allocation
+ * on the request path, or code inside another framework's step with no allocator at hand).
+ * No counterpart in the reference. Same arguments and results as m3ssd_fwd, but
+ * `workspace`/`workspace_bytes` are ignored (may be NULL/0): the scratch this forward needs
+ * (status word, ticket counter, one hand-off flag per chunk) is a fixed device array inside the
+ * library, 131,328 bytes, held on every GPU that loads the library until exit.
+ *   - Only the tensor-core forward: head_dim = state_dim = 64, real x, B/C with a contiguous
+ *     state dimension and 16-byte aligned strides; otherwise M3SSD_ERR_SHAPE.
+ *   - batch * nheads * ceil(seqlen / 64) must be <= 32768, otherwise M3SSD_ERR_SCRATCH_LIMIT.
+ *   - The first call on a device looks up the array's device address (with that device
+ *     current); make that first call before any stream capture.
+ *   - Every call uses the same array and leaves its contents behind; each call clears what must
+ *     start at zero before its kernel runs. Calls that overlap on the GPU (other streams, other
+ *     host threads) race on the array: serialise them.
+ *   - Calls no cudaMalloc/cudaFree and no allocating library routine. */
+M3SSD_API int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* args, void* stream);
 
 #ifdef __cplusplus
 }

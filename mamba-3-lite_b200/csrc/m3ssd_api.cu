@@ -4,6 +4,8 @@
 #include <limits.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "m3ssd.h"
 #include "m3ssd_common.cuh"
 #include "simt_path.h"
@@ -111,6 +113,38 @@ int fill_inputs(Problem& p, const void* x, const int64_t xs[4], const void* A, c
   return M3SSD_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Fixed device scratch for m3ssd_fwd_static_scratch. Some callers cannot allocate device memory
+// when they call the operator: a serving runtime that plans every byte of device memory before
+// it takes requests and forbids allocation on the request path, or code running inside another
+// framework's step where no allocator is reachable. The tensor-core forward needs only a small
+// scratch area (status word, ticket counter and one hand-off flag per chunk of each sequence), so
+// that area lives in this file-scope device array instead. Every GPU that loads the library holds
+// the array until the process exits.
+constexpr int64_t kStaticMaxChunks = 32768;  // batch * heads * ceil(seqlen / 64) limit
+constexpr size_t kStaticScratchBytes = 256 + 4 * (size_t)kStaticMaxChunks;  // 131,328 bytes
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device, looked up once per device with that
+// device current (the name is only a host-side stand-in for the device array).
+int static_scratch_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return M3SSD_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_scratch_addr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr)
+      return M3SSD_ERR_DEVICE;
+    g_static_scratch_addr[dev] = ptr;
+  }
+  *out = g_static_scratch_addr[dev];
+  return M3SSD_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -130,6 +164,9 @@ const char* m3ssd_strerror(int status) {
     case M3SSD_ERR_DEVICE: return "m3ssd: current CUDA device is not an sm_100 GPU";
     case M3SSD_ERR_FLAGS: return "m3ssd: unknown flag bits";
     case M3SSD_ERR_OVERFLOW: return "m3ssd: problem size overflows 64-bit indexing";
+    case M3SSD_ERR_SCRATCH_LIMIT:
+      return "m3ssd: problem exceeds the fixed scratch of m3ssd_fwd_static_scratch "
+             "(batch * heads * ceil(seqlen / 64) must be <= 32768)";
     default: return "m3ssd: unknown status";
   }
 }
@@ -217,6 +254,30 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   return m3ssd::simt::run_bwd(p, a->dy, dys, a->states, a->dx, static_cast<float2*>(a->dA),
                               static_cast<float2*>(a->dB), static_cast<float2*>(a->dC), a->ddt,
                               a->workspace, static_cast<cudaStream_t>(stream));
+}
+
+int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* a, void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  if (!tc_shape(&a->prob)) return M3SSD_ERR_SHAPE;  // tensor-core forward shapes only
+  Problem p = make_problem(&a->prob);
+  rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
+                   a->dt_strides);
+  if (rc) return rc;
+  if (!a->y || !a->states) return M3SSD_ERR_NULL;
+  if (!aligned(a->y, 4) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
+  if (!m3ssd::tc::fwd_supported(p)) return M3SSD_ERR_SHAPE;
+  const int64_t chunks = a->prob.batch * a->prob.nheads * (int64_t)p.nc;
+  if (chunks > kStaticMaxChunks || m3ssd::tc::fwd_workspace_bytes(p) > kStaticScratchBytes)
+    return M3SSD_ERR_SCRATCH_LIMIT;
+  rc = check_device();
+  if (rc) return rc;
+  void* scratch = nullptr;
+  rc = static_scratch_address(&scratch);
+  if (rc) return rc;
+  // run_fwd clears the status word, ticket counter and flags it uses before its kernel runs
+  return m3ssd::tc::run_fwd(p, a->y, a->states, scratch, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

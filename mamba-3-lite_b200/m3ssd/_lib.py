@@ -19,6 +19,7 @@ M3SSD_PREC_TENSOR = 0x20
 STATUS_NAMES = {
     0: "OK", 1: "ERR_NULL", 2: "ERR_SHAPE", 3: "ERR_CHUNK", 4: "ERR_DIM_LIMIT", 5: "ERR_ALIGN",
     6: "ERR_WORKSPACE", 7: "ERR_LAUNCH", 8: "ERR_DEVICE", 9: "ERR_FLAGS", 10: "ERR_OVERFLOW",
+    11: "ERR_SCRATCH_LIMIT",
 }
 
 I64x3 = ctypes.c_int64 * 3
@@ -71,6 +72,7 @@ SIGNATURES = {
     "m3ssd_fwd_path": (ctypes.c_char_p, [ctypes.POINTER(Problem)]),
     "m3ssd_bwd_path": (ctypes.c_char_p, [ctypes.POINTER(Problem)]),
     "m3ssd_launch_count": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.c_int]),
+    "m3ssd_fwd_static_scratch": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
 }
 
 _lib = None
