@@ -175,7 +175,10 @@ int m3ssd_check_problem(const m3ssd_problem* prob) { return check_problem(prob);
 
 size_t m3ssd_states_bytes(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  return m3ssd::simt::states_bytes(make_problem(prob));
+  const Problem p = make_problem(prob);
+  const size_t a = m3ssd::simt::states_bytes(p);
+  const size_t b = tc_shape(prob) ? m3ssd::tc::states_bytes(p) : 0;
+  return a > b ? a : b;
 }
 
 size_t m3ssd_fwd_workspace_bytes(const m3ssd_problem* prob) {

@@ -53,14 +53,14 @@ constexpr uint32_t COL_G = 0, COL_DM = 64, COL_Q = 128, COL_DCA = 256, COL_DCB =
 constexpr uint32_t COL_DXA = 0, COL_DXB = 64, COL_DBA = 128, COL_DBB = 256;
 
 struct Misc {
+  ChunkRec rec;  // this chunk's decay quantities (bulk-copied with the B/C tiles)
   uint64_t bar_tma, bar1, bar2, bar3, bar4;
-  float rho[64], el[64], dec[64], sp[64], dsp[64];
-  float2 cis[64];
   float2 rc[4][64];
   float2 rb[4][64];
-  float2 dgw[8];
+  float2 dgp[8];   // per-warp partials of <dS_{z-1}, H_z>
+  float2 dgam;     // <dS_z, H_{z+1}> handed over by the chunk z+1 ticket
   float2 dap[2];
-  float2 carry, gam, g, ct, sfx;
+  float2 sfx;
   int first, nxt;
   uint32_t tmem_base;
 };
@@ -75,8 +75,7 @@ struct BwdParams {
   long long dys[4];
   int dy_vec;
   const float2* A;
-  const float* dt;
-  long long dts[3];
+  const ChunkRec* recs;
   const float* states;
   float* dx;
   float2* dB;
@@ -84,6 +83,7 @@ struct BwdParams {
   float* ddt;
   float2* dapart;
   float* ring;
+  float2* dgring;
   uint32_t* flags;
   uint32_t* counter;
   uint32_t* err;
@@ -182,7 +182,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmC);
     first = (int)atomicAdd(p.counter, 1u);
-    m.nxt = (int)atomicAdd(p.counter, 1u);
     m.first = first;
   }
   if (warp == 0) {
@@ -197,16 +196,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   int ticket = m.first;
 
   float xv[16], gv[16];
-  float dtv = 0.f;
   auto prefetch_regs = [&](int tk) {
     const int zr = tk / BH, bh = tk - zr * BH;
     const int z = p.nc - 1 - zr;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
     load16(p.x, p.xs, p.x_vec, p.T, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
     load16(p.dy, p.dys, p.dy_vec, p.T, b, t0 + (tid >> 2), h, 16 * (tid & 3), gv);
-    dtv = 0.f;
-    if (tid < 64 && t0 + tid < p.T)
-      dtv = __ldg(p.dt + b * p.dts[0] + (long long)(t0 + tid) * p.dts[1] + h * p.dts[2]);
   };
   if (ticket < p.total) prefetch_regs(ticket);
 
@@ -217,67 +212,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int z = p.nc - 1 - zr;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
     __syncthreads();  // previous ticket complete (including generic reads of sB / sC)
-    const int next = m.nxt;
-    int nn = 0;
+    int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
     if (tid == 0) {
-      nn = (int)atomicAdd(p.counter, 1u);
-      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes);
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec) + 32768u);
       tma_load_4d(smem + OFF_B, &tmB, &m.bar_tma, 0, h, t0, b);
       tma_load_4d(smem + OFF_C, &tmC, &m.bar_tma, 0, h, t0, b);
+      bulk_load(&m.rec, p.recs + (long long)bh * p.nc + z, (uint32_t)sizeof(ChunkRec), &m.bar_tma);
+      bulk_load(smem + OFF_H, p.states + ((long long)bh * p.nc + z) * 64 * 128, 32768u,
+                &m.bar_tma);  // H_z (fp32 [p][128]); converted in place below
     }
 
-    // ---- within-chunk cumsum of a = softplus(dt) A
-    if (tid < 64) {
-      const float2 A = p.A[h];
-      float2 a = make_float2(0.f, 0.f);
-      float spv = 0.f, dspv = 0.f;
-      if (t0 + tid < p.T) {
-        spv = softplus_f(dtv);
-        dspv = softplus_grad_f(dtv);
-        a = make_float2(spv * A.x, spv * A.y);
-      }
-      m.sp[tid] = spv;
-      m.dsp[tid] = dspv;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float ux = __shfl_up_sync(0xffffffffu, a.x, o);
-        const float uy = __shfl_up_sync(0xffffffffu, a.y, o);
-        if (lane >= o) {
-          a.x += ux;
-          a.y += uy;
-        }
-      }
-      if (tid == 31) m.carry = a;
-      m.rho[tid] = a.x;
-      m.el[tid] = a.y;
-    }
-    __syncthreads();
-    if (tid < 64) {
-      float rx = m.rho[tid], ry = m.el[tid];
-      if (tid >= 32) {
-        rx += m.carry.x;
-        ry += m.carry.y;
-      }
-      float sn, cs;
-      sincosf(ry, &sn, &cs);
-      m.rho[tid] = rx;
-      m.cis[tid] = make_float2(cs, sn);
-      if (tid == 63) m.gam = make_float2(rx, ry);
-    }
-    __syncthreads();
-    if (tid < 64) {
-      const float rx = m.rho[tid];
-      m.el[tid] = expf(rx);
-      m.dec[tid] = expf(m.gam.x - rx);
-      if (tid == 0) {
-        const float mg = expf(m.gam.x);
-        float sn, cs;
-        sincosf(m.gam.y, &sn, &cs);
-        m.g = make_float2(mg * cs, mg * sn);
-        m.ct = make_float2(cs, sn);
-      }
-    }
-    __syncthreads();
+    mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // B, C tiles, decay record, H_z
 
     // ---- x, dy (stacked over rows, K = p) and e_l dy (stacked over p, MN) from registers
     {
@@ -290,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    sb + OFF_DY + swz(stack8(s, 1), 2 * pg), gv);
       split8_store(sb + OFF_DY + swz(stack8(s, 0), 2 * pg + 1),
                    sb + OFF_DY + swz(stack8(s, 1), 2 * pg + 1), gv + 8);
-      const float e = m.el[s];
+      const float e = m.rec.el[s];
       float w[16];
 #pragma unroll
       for (int u = 0; u < 16; ++u) w[u] = e * gv[u];
@@ -304,7 +250,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---- raw B, C tiles -> registers -> rotated, split, stacked operands (in place)
-    mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);
     {
       float4 rb4[4][2], rc4[4][2];
 #pragma unroll
@@ -323,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int it = 0; it < 4; ++it) {
         const int j = tid + kThreads * it;
         const int l = j >> 4, q = j & 15;
-        const float2 cs = m.cis[l];
+        const float2 cs = m.rec.cis[l];
         const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
         const float cr[8] = {rc4[it][0].x, rc4[it][0].y, rc4[it][0].z, rc4[it][0].w,
                              rc4[it][1].x, rc4[it][1].y, rc4[it][1].z, rc4[it][1].w};
@@ -377,26 +322,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&m.bar1);
     }
 
-    // ---- H_z (conj) -> sH; dS_z from the next chunk; <dS_z, H_{z+1}>; dS' -> sDS
+    // ---- H_z (fp32 in sH) -> conj(H_z) split in place; dS_z from the next chunk; dS' -> sDS
     const int kb = 64 * wg + 32 * part;
-    float dsz[32];
     {
       float hz[32];
-      const float* hrow = p.states + (((long long)bh * p.nc + z) * 64 + r) * 128 + kb;
+      const float* hrow = reinterpret_cast<const float*>(smem + OFF_H) + r * 128 + kb;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(hrow) + i);
+        const float4 v = reinterpret_cast<const float4*>(hrow)[i];
         hz[4 * i] = v.x;
         hz[4 * i + 1] = -v.y;
         hz[4 * i + 2] = v.z;
         hz[4 * i + 3] = -v.w;
       }
+      __syncthreads();
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj)
         split8_store(sb + OFF_H + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
                      sb + OFF_H + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
                      hz + 8 * jj);
     }
+    float dsz[32];
     if (z < p.nc - 1) {
       if (tid == 0) {
         const uint32_t* f = p.flags + (long long)bh * p.nc + z;
@@ -406,38 +352,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           __nanosleep(128);
         }
         if (i == kSpinLimit) atomicOr(p.err, kErrFlagWait);
-        __threadfence();
+        m.dgam = __ldcg(p.dgring + (long long)bh * 4 + (z & 3));
       }
       __syncthreads();
       const float* drow = p.ring + (((long long)bh * 4 + (z & 3)) * 64 + r) * 128 + kb;
-      const float* h1row = p.states + (((long long)bh * p.nc + z + 1) * 64 + r) * 128 + kb;
-      float2 dg = make_float2(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 v = __ldcg(reinterpret_cast<const float4*>(drow) + i);
-        const float4 hv = __ldcg(reinterpret_cast<const float4*>(h1row) + i);
         dsz[4 * i] = v.x;
         dsz[4 * i + 1] = v.y;
         dsz[4 * i + 2] = v.z;
         dsz[4 * i + 3] = v.w;
-        // dS conj(H_{z+1})
-        dg.x += v.x * hv.x + v.y * hv.y + v.z * hv.z + v.w * hv.w;
-        dg.y += v.y * hv.x - v.x * hv.y + v.w * hv.z - v.z * hv.w;
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
-        dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
-      }
-      if (lane == 0) m.dgw[warp] = dg;
     } else {
 #pragma unroll
       for (int c = 0; c < 32; ++c) dsz[c] = 0.f;
-      if (lane == 0) m.dgw[warp] = make_float2(0.f, 0.f);
+      if (tid == 0) m.dgam = make_float2(0.f, 0.f);
     }
     {
       // dS'x = interleaved (Re, -Im) of conj(cis(theta_Gamma)) dS_z
-      const float2 ct = m.ct;
+      const float2 ct = m.rec.ct;
       float w[32];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
@@ -461,12 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ld_exch16(tmem + lane_off + COL_G + 32u * wg, part, gs);
       ld_exch16(tmem + lane_off + COL_DM + 32u * wg, part, ms);
       const int s0 = 32 * wg + 16 * part;
-      const float rl = m.rho[r];
+      const float rl = m.rec.rho[r];
       float mrv[16], dgv[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         const int s = s0 + c;
-        const float L = (s <= r) ? expf(rl - m.rho[s]) : 0.f;
+        const float L = (s <= r) ? expf(rl - m.rec.rho[s]) : 0.f;
         mrv[c] = L * gs[c];
         dgv[c] = L * ms[c];
       }
@@ -486,8 +420,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       float q[32];
       ld_exch32(tmem + lane_off + COL_Q + 64u * wg, part, q);
+      float2 dg = make_float2(0.f, 0.f);
       if (z > 0) {
-        const float2 g = m.g;
+        const float2 g = m.rec.g;
         float* drow = p.ring + (((long long)bh * 4 + ((z - 1) & 3)) * 64 + r) * 128 + kb;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -500,17 +435,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             o[u + 1] = qi + g.x * dsz[c + 1] - g.y * dsz[c];
           }
           __stcg(reinterpret_cast<float4*>(drow) + i, make_float4(o[0], o[1], o[2], o[3]));
+          // <dS_{z-1}, H_z> for chunk z-1's decay gradient; sH holds conj(H_z) as hi + lo
+          const uint32_t hoff = (uint32_t)wg * 8192u + swz(r, 4 * part + (i >> 1));
+          const uint4 hh = ld_shared_u4(sb + OFF_H + hoff), hl = ld_shared_u4(sb + OFF_H + 16384u + hoff);
+          const float2 h0 = unsplit2((i & 1) ? hh.z : hh.x, (i & 1) ? hl.z : hl.x);
+          const float2 h1 = unsplit2((i & 1) ? hh.w : hh.y, (i & 1) ? hl.w : hl.y);
+          dg.x += o[0] * h0.x - o[1] * h0.y + o[2] * h1.x - o[3] * h1.y;
+          dg.y += o[0] * h0.y + o[1] * h0.x + o[2] * h1.y + o[3] * h1.x;
         }
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
+        dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
+      }
+      if (lane == 0) m.dgp[warp] = dg;
     }
     fence_proxy_async_smem();
     tc_fence_before_sync();
     __syncthreads();
     if (tid == 0) {
+      // the barrier orders every thread's ring stores before this gpu-scope release
       if (z > 0) {
-        __threadfence();
+        float2 dg = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          dg.x += m.dgp[w].x;
+          dg.y += m.dgp[w].y;
+        }
+        __stcg(p.dgring + (long long)bh * 4 + ((z - 1) & 3), dg);
         st_release_gpu(p.flags + (long long)bh * p.nc + z - 1, 1u);
       }
+      const int nn = (int)atomicAdd(p.counter, 1u);  // result is stored after the MMA issue
       tc_fence_after_sync();
       // batch 2: dCa = dG' B'x (MN), dCb = dy conj(H)
       const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
@@ -557,8 +513,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                       sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idba,
                       (hp | j) != 0);
       mma_commit(&m.bar3);
+      m.nxt = nn;
     }
     // prefetch the next ticket's x, dy, dt while the MMAs run
+    __syncthreads();
+    next = m.nxt;
     if (next < p.total) prefetch_regs(next);
 
     // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)); row sums dC' conj(C')
@@ -568,8 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float ca[32], cb[32];
       ld_exch32(tmem + lane_off + COL_DCA + 64u * wg, part, ca);
       ld_exch32(tmem + lane_off + COL_DCB + 64u * wg, part, cb);
-      const float e = m.el[r];
-      const float2 cs = m.cis[r];
+      const float e = m.rec.el[r];
+      const float2 cs = m.rec.cis[r];
       float out[32];
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
@@ -622,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float xa[16], xb[16];
       ld_exch16(tmem + lane_off + COL_DXA + 32u * wg, part, xa);
       ld_exch16(tmem + lane_off + COL_DXB + 32u * wg, part, xb);
-      const float d = m.dec[r];
+      const float d = m.rec.dec[r];
       const int t = t0 + r;
       if (t < p.T) {
         float* dst = p.dx + (((long long)b * p.T + t) * p.H + h) * 64 + 32 * wg + 16 * part;
@@ -640,8 +599,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float ba[32], bbv[32];
       ld_exch32(tmem + lane_off + COL_DBA + 64u * wg, part, ba);
       ld_exch32(tmem + lane_off + COL_DBB + 64u * wg, part, bbv);
-      const float d = m.dec[r];
-      const float2 cs = m.cis[r];
+      const float d = m.rec.dec[r];
+      const float2 cs = m.rec.cis[r];
       float out[32];
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
@@ -686,11 +645,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ds.y += m.rc[j][l].y - m.rb[j][l].y;
       }
       if (l == 63) {
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          ds.x += m.dgw[w].x;
-          ds.y += m.dgw[w].y;
-        }
+        ds.x += m.dgam.x;
+        ds.y += m.dgam.y;
       }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {  // suffix sum within the warp
@@ -714,8 +670,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float2 A = p.A[h];
       float2 dap = make_float2(0.f, 0.f);
       if (t < p.T) {
-        p.ddt[((long long)b * p.T + t) * p.H + h] = (da.x * A.x + da.y * A.y) * m.dsp[tid];
-        dap = make_float2(da.x * m.sp[tid], da.y * m.sp[tid]);
+        p.ddt[((long long)b * p.T + t) * p.H + h] = (da.x * A.x + da.y * A.y) * m.rec.dsp[tid];
+        dap = make_float2(da.x * m.rec.sp[tid], da.y * m.rec.sp[tid]);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -728,7 +684,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
       p.dapart[(long long)bh * p.nc + z] =
           make_float2(m.dap[0].x + m.dap[1].x, m.dap[0].y + m.dap[1].y);
-      m.nxt = nn;
     }
     ticket = next;
     ++iter;
@@ -758,7 +713,7 @@ __global__ void k_bwd_tc_dA(const float2* __restrict__ dapart, int Bsz, int H, i
 namespace {
 
 struct BwdLayout {
-  size_t flags, ring, dapart, total;
+  size_t flags, ring, dgring, dapart, total;
 };
 
 BwdLayout bwd_layout(const Problem& p) {
@@ -767,7 +722,8 @@ BwdLayout bwd_layout(const Problem& p) {
   BwdLayout L;
   L.flags = 256;
   L.ring = al(L.flags + 4 * bh * nc);
-  L.dapart = al(L.ring + bh * 4 * 64 * 128 * sizeof(float));
+  L.dgring = al(L.ring + bh * 4 * 64 * 128 * sizeof(float));
+  L.dapart = al(L.dgring + bh * 4 * sizeof(float2));
   L.total = al(L.dapart + bh * nc * sizeof(float2));
   return L;
 }
@@ -801,9 +757,8 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
                   ? 1
                   : 0;
   bp.A = p.A;
-  bp.dt = p.dt;
-  for (int i = 0; i < 3; ++i) bp.dts[i] = p.dts[i];
   bp.states = static_cast<const float*>(states);
+  bp.recs = reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
   bp.dx = dx;
   bp.dB = dB;
   bp.dC = dC;
@@ -813,6 +768,7 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
   bp.counter = reinterpret_cast<uint32_t*>(base) + 1;
   bp.flags = reinterpret_cast<uint32_t*>(base + L.flags);
   bp.ring = reinterpret_cast<float*>(base + L.ring);
+  bp.dgring = reinterpret_cast<float2*>(base + L.dgring);
   bp.dapart = reinterpret_cast<float2*>(base + L.dapart);
   CUtensorMap tmB, tmC;
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))

@@ -143,6 +143,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 32 lanes x 16 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -174,16 +188,16 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bflo
   hi = __float2bfloat16_rn(v);
   lo = __float2bfloat16_rn(v - __bfloat162float(hi));
 }
-// splits 8 floats into 8 hi and 8 lo bf16 packed in two uint4
+// splits 8 floats into 8 hi and 8 lo bf16 packed in two uint4 (pairwise bf16x2 conversions)
 __device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    __nv_bfloat16 h0, l0, h1, l1;
-    split_bf16(v[2 * i], h0, l0);
-    split_bf16(v[2 * i + 1], h1, l1);
-    h[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-    l[i] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+    const __nv_bfloat162 hp = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    const float2 hf = __bfloat1622float2(hp);
+    const __nv_bfloat162 lp = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hp);
+    l[i] = *reinterpret_cast<const uint32_t*>(&lp);
   }
   hi = make_uint4(h[0], h[1], h[2], h[3]);
   lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -247,5 +261,35 @@ __device__ __forceinline__ float2 unsplit2(uint32_t hi, uint32_t lo) {
   const float l0 = __uint_as_float(lo << 16), l1 = __uint_as_float(lo & 0xFFFF0000u);
   return make_float2(h0 + l0, h1 + l1);
 }
+}  // namespace tc
+}  // namespace m3ssd
+
+namespace m3ssd {
+namespace tc {
+// Non-tensor bulk copy global -> shared (16-byte aligned, size a multiple of 16), counted on bar.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Per (sequence, chunk) decay quantities written by k_chunk_prep and bulk-copied by the forward
+// and backward kernels. Position l of chunk z is t = 64 z + l; Sigma_l = rho_l + i theta_l is the
+// within-chunk inclusive cumsum of a = softplus(dt) A (a = 0 for t >= T), Gamma = Sigma_63.
+struct ChunkRec {
+  float rho[64];   // Re Sigma_l
+  float el[64];    // exp(rho_l)
+  float dec[64];   // exp(rho_Gamma - rho_l)
+  float sp[64];    // softplus(dt_t) (0 past T)
+  float dsp[64];   // softplus'(dt_t) (0 past T)
+  float2 cis[64];  // (cos, sin)(theta_l)
+  float2 g;        // e^Gamma
+  float2 ct;       // cis(theta_Gamma)
+  float2 pad[2];
+};
+static_assert(sizeof(ChunkRec) % 16 == 0, "bulk copy granularity");
 }  // namespace tc
 }  // namespace m3ssd

@@ -1,6 +1,6 @@
 // Tensor-core forward of the complex chunkwise SSD for head_dim = state_dim = 64, real x.
 //
-// One persistent CTA per SM takes chunk tickets (chunk-major order over all b*H sequences) from a
+// Persistent CTAs (two per SM) take chunk tickets (chunk-major order over all b*H sequences) from a
 // global counter. Per ticket (64 positions of one (b, h)), with Sigma_l = rho_l + i theta_l the
 // within-chunk cumsum of a = softplus(dt) A (models/ssd_complex.py:82, :89), Gamma = Sigma_63:
 //
@@ -32,36 +32,26 @@ namespace {
 
 constexpr int kThreads = 256;
 
-// shared memory map (offsets from a 1024-aligned base)
-constexpr uint32_t OFF_CX = 0;          // C'x  A, K-major, stacked 128 rows x 128 k, 2 k-atoms
-constexpr uint32_t OFF_BXH = 32768;     // B'x hi (conjugate-interleaved) 64 rows x 128 k
-constexpr uint32_t OFF_BXL = 49152;     // B'x lo
-constexpr uint32_t OFF_XH = 65536;      // x hi [s][p]
-constexpr uint32_t OFF_XL = 73728;      // x lo
-constexpr uint32_t OFF_XT = 81920;      // x~ stacked [p-group][s][64]
-constexpr uint32_t OFF_MR = 98304;      // Mr stacked [128][s]
-constexpr uint32_t OFF_HH = 114688;     // Hx hi [k][p]
-constexpr uint32_t OFF_HL = 131072;     // Hx lo
-constexpr uint32_t OFF_RAWB = 147456;   // TMA tile of B (fp32, 64 x 128)
-constexpr uint32_t OFF_RAWC = 180224;   // TMA tile of C
-constexpr uint32_t OFF_MISC = 212992;
+// Shared memory map (offsets from a 1024-aligned base), ~100 KB so two CTAs share an SM:
+// one CTA's memory waits and barriers overlap the other's MMAs and epilogues.
+constexpr uint32_t OFF_CX = 0;       // TMA tile of C (fp32 64 x 128), then C'x stacked (A operand)
+constexpr uint32_t OFF_BX = 32768;   // TMA tile of B, then B'x hi | lo (64 x 128 each 16 KB),
+                                     // then conj(H_z) hi | lo as [k-atom][p][64] (K-major B)
+constexpr uint32_t OFF_XH = 65536;   // x hi [s][p]
+constexpr uint32_t OFF_XL = 73728;   // x lo
+constexpr uint32_t OFF_XT = 81920;   // x~ stacked [p-group][s][64], then Mr stacked [128][s]
+constexpr uint32_t OFF_MISC = 98304;
 constexpr uint32_t kSmemBytes = OFF_MISC + 2048 + 1024;
 constexpr uint32_t kTmaBytes = 2u * 64u * 128u * 4u;
 
-// TMEM columns
-constexpr uint32_t COL_G = 0, COL_S = 64, COL_Y1 = 192, COL_Y2 = 256, kTmemCols = 512;
+// TMEM columns (256 per CTA): G then Y1 share [0, 64)
+constexpr uint32_t COL_G = 0, COL_Y1 = 0, COL_S = 64, COL_Y2 = 192, kTmemCols = 256;
 
 struct Misc {
+  ChunkRec rec;  // this chunk's decay quantities (bulk-copied with the B/C tiles)
   uint64_t bar_tma, bar_mma1, bar_mma2, bar_mma3;
-  float rho[64];
-  float el[64];
-  float dec[64];
-  float2 cis[64];
-  float2 carry;
-  float2 gam;
-  float2 g;   // e^Gamma
-  float2 ct;  // cis(theta_Gamma)
-  int next_ticket;
+  int first, nxt;
+  int h_ready;
   uint32_t tmem_base;
 };
 static_assert(sizeof(Misc) <= 2048, "misc area");
@@ -71,9 +61,7 @@ struct FwdParams {
   const float* x;
   long long xs[4];
   int x_vec;
-  const float2* A;
-  const float* dt;
-  long long dts[3];
+  const ChunkRec* recs;
   float* y;
   float* states;
   uint32_t* flags;
@@ -108,9 +96,19 @@ __device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
+__device__ __forceinline__ void split_store16(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
+  float w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = v[i];
+  uint4 hi, lo;
+  split8(w, hi, lo);
+  st_shared_v4(hi_addr, hi);
+  st_shared_v4(lo_addr, lo);
+}
+
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     k_fwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -120,7 +118,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   Misc& m = *reinterpret_cast<Misc*>(smem + OFF_MISC);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sub = warp & 3, wg = warp >> 2, part = lane >> 4;
+  const int r = 16 * sub + (lane & 15);  // logical row of this TMEM lane (position l, or p)
+  const int kb = 64 * wg + 32 * part;    // this thread's 32 interleaved state columns
   const int BH = p.Bsz * p.H;
+  // ticket counter, TMA issue and hand-off flags are handled by one lane of warp 7 so warps 0-1
+  // (cumsum) and thread 0 (MMA issue) never stall on them
+  const bool ctrl = tid == kThreads - 32;
 
   if (tid == 0) {
     mbar_init(&m.bar_tma, 1);
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmC);
-    m.next_ticket = (int)atomicAdd(p.counter, 1u);
+    m.first = (int)atomicAdd(p.counter, 1u);
   }
   if (warp == 0) {
     tmem_alloc(&m.tmem_base, kTmemCols);
@@ -142,239 +145,158 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = m.tmem_base;
   const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
 
-  int ticket = m.next_ticket;
+  int ticket = m.first;
   float xv[16];
-  float dtv = 0.f;
-  auto prefetch = [&](int tk) {
+  auto prefetch_regs = [&](int tk) {
     const int z = tk / BH, bh = tk - (tk / BH) * BH;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
     load_x16(p, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
-    dtv = 0.f;
-    if (tid < 64 && t0 + tid < p.T) dtv = __ldg(p.dt + b * p.dts[0] + (long long)(t0 + tid) * p.dts[1] + h * p.dts[2]);
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes);
-      tma_load_4d(smem + OFF_RAWB, &tmB, &m.bar_tma, 0, h, t0, b);
-      tma_load_4d(smem + OFF_RAWC, &tmC, &m.bar_tma, 0, h, t0, b);
-    }
   };
-  if (ticket < p.total) prefetch(ticket);
+  if (ticket < p.total) prefetch_regs(ticket);
 
   uint32_t iter = 0;
   while (ticket < p.total) {
     const uint32_t ph = iter & 1u;
     const int z = ticket / BH, bh = ticket - z * BH;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
-    __syncthreads();  // everyone has read m.next_ticket of the previous round
-    if (tid == 0) m.next_ticket = (int)atomicAdd(p.counter, 1u);
-
-    // ---- within-chunk cumsum of a = softplus(dt) A (warps 0-1, one position per thread)
-    if (tid < 64) {
-      const float2 A = p.A[h];
-      float2 a = make_float2(0.f, 0.f);
-      if (t0 + tid < p.T) {
-        const float sp = softplus_f(dtv);
-        a = make_float2(sp * A.x, sp * A.y);
-      }
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float ux = __shfl_up_sync(0xffffffffu, a.x, o);
-        const float uy = __shfl_up_sync(0xffffffffu, a.y, o);
-        if (lane >= o) {
-          a.x += ux;
-          a.y += uy;
-        }
-      }
-      if (tid == 31) m.carry = a;
-      // stash both components until warp 0's total (the carry) is known
-      m.rho[tid] = a.x;
-      m.el[tid] = a.y;
-    }
-    __syncthreads();
-    const int next = m.next_ticket;
-    if (tid < 64) {
-      float rx = m.rho[tid], ry = m.el[tid];
-      if (tid >= 32) {
-        rx += m.carry.x;
-        ry += m.carry.y;
-      }
-      float sn, cs;
-      sincosf(ry, &sn, &cs);
-      m.rho[tid] = rx;
-      m.cis[tid] = make_float2(cs, sn);
-      if (tid == 63) m.gam = make_float2(rx, ry);
-    }
-    __syncthreads();
-    if (tid < 64) {
-      const float rx = m.rho[tid];
-      m.el[tid] = expf(rx);
-      m.dec[tid] = expf(m.gam.x - rx);
-      if (tid == 0) {
-        const float mg = expf(m.gam.x);
-        float sn, cs;
-        sincosf(m.gam.y, &sn, &cs);
-        m.g = make_float2(mg * cs, mg * sn);
-        m.ct = make_float2(cs, sn);
-      }
+    __syncthreads();  // previous ticket done: its MMAs completed
+    int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
+    if (ctrl) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec));
+      tma_load_4d(smem + OFF_BX, &tmB, &m.bar_tma, 0, h, t0, b);
+      tma_load_4d(smem + OFF_CX, &tmC, &m.bar_tma, 0, h, t0, b);
+      bulk_load(&m.rec, p.recs + (long long)bh * p.nc + z, (uint32_t)sizeof(ChunkRec), &m.bar_tma);
+      // is H_z already published? (then its loads overlap the transform and first MMAs)
+      m.h_ready = (z == 0) ? 1 : (int)ld_acquire_gpu(p.flags + (long long)bh * p.nc + z);
     }
 
-    // ---- TMA tiles of B and C for this ticket
+    // ---- TMA tiles of B and C land in the operand buffers; rotate and split them in place
     mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);
-    __syncthreads();  // cis/el/dec visible
-
-    // ---- operand transform: C'x (stacked hi/lo), B'x (conjugate-interleaved hi, lo)
     {
-      const float* rawB = reinterpret_cast<const float*>(smem + OFF_RAWB);
-      const float* rawC = reinterpret_cast<const float*>(smem + OFF_RAWC);
+      // one tile at a time: all raw values of the tile in registers, barrier, write in place
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int j = tid + kThreads * i;
-        const int l = j >> 4, q = j & 15;
-        const float2 cs = m.cis[l];
-        const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
-        const float4 c0 = *reinterpret_cast<const float4*>(rawC + l * 128 + 8 * q);
-        const float4 c1 = *reinterpret_cast<const float4*>(rawC + l * 128 + 8 * q + 4);
-        const float cr[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        float v[8];
+      for (int tile = 0; tile < 2; ++tile) {  // 0: C -> C'x (stacked), 1: B -> B'x hi | lo
+        const uint32_t base = tile ? OFF_BX : OFF_CX;
+        float4 r4[4][2];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {  // C * cis(theta_l)
-          v[2 * u] = cr[2 * u] * cs.x - cr[2 * u + 1] * cs.y;
-          v[2 * u + 1] = cr[2 * u] * cs.y + cr[2 * u + 1] * cs.x;
+        for (int it = 0; it < 4; ++it) {
+          const int j = tid + kThreads * it;
+          const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
+          r4[it][0] = *reinterpret_cast<const float4*>(src);
+          r4[it][1] = *reinterpret_cast<const float4*>(src + 4);
         }
-        uint4 hi, lo;
-        split8(v, hi, lo);
-        st_shared_v4(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 0), ch), hi);
-        st_shared_v4(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 1), ch), lo);
-        const float4 b0 = *reinterpret_cast<const float4*>(rawB + l * 128 + 8 * q);
-        const float4 b1 = *reinterpret_cast<const float4*>(rawB + l * 128 + 8 * q + 4);
-        const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        __syncthreads();
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {  // conj(B * conj(cis(theta_s)))
-          v[2 * u] = br[2 * u] * cs.x + br[2 * u + 1] * cs.y;
-          v[2 * u + 1] = br[2 * u] * cs.y - br[2 * u + 1] * cs.x;
+        for (int it = 0; it < 4; ++it) {
+          const int j = tid + kThreads * it;
+          const int l = j >> 4, q = j & 15;
+          const float2 cs = m.rec.cis[l];
+          const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
+          const float rv[8] = {r4[it][0].x, r4[it][0].y, r4[it][0].z, r4[it][0].w,
+                               r4[it][1].x, r4[it][1].y, r4[it][1].z, r4[it][1].w};
+          float v[8];
+          if (tile == 0) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // C * cis(theta_l)
+              v[2 * u] = rv[2 * u] * cs.x - rv[2 * u + 1] * cs.y;
+              v[2 * u + 1] = rv[2 * u] * cs.y + rv[2 * u + 1] * cs.x;
+            }
+            split_store16(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 0), ch),
+                          sb + OFF_CX + ka * 16384u + swz(stack_row(l, 1), ch), v);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // conj(B * conj(cis(theta_s)))
+              v[2 * u] = rv[2 * u] * cs.x + rv[2 * u + 1] * cs.y;
+              v[2 * u + 1] = rv[2 * u] * cs.y - rv[2 * u + 1] * cs.x;
+            }
+            split_store16(sb + OFF_BX + ka * 8192u + swz(l, ch),
+                          sb + OFF_BX + 16384u + ka * 8192u + swz(l, ch), v);
+          }
         }
-        split8(v, hi, lo);
-        st_shared_v4(sb + OFF_BXH + ka * 8192u + swz(l, ch), hi);
-        st_shared_v4(sb + OFF_BXL + ka * 8192u + swz(l, ch), lo);
       }
       // x (hi, lo) and x~ = exp(rho_Gamma - rho_s) x, stacked over p
       const int s = tid >> 2, pg = tid & 3;
-      float v8[8];
-      uint4 h0, l0, h1, l1;
+      split_store16(sb + OFF_XH + swz(s, 2 * pg), sb + OFF_XL + swz(s, 2 * pg), xv);
+      split_store16(sb + OFF_XH + swz(s, 2 * pg + 1), sb + OFF_XL + swz(s, 2 * pg + 1), xv + 8);
+      const float dd = m.rec.dec[s];
+      float xt[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v8[u] = xv[u];
-      split8(v8, h0, l0);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v8[u] = xv[8 + u];
-      split8(v8, h1, l1);
-      st_shared_v4(sb + OFF_XH + swz(s, 2 * pg), h0);
-      st_shared_v4(sb + OFF_XH + swz(s, 2 * pg + 1), h1);
-      st_shared_v4(sb + OFF_XL + swz(s, 2 * pg), l0);
-      st_shared_v4(sb + OFF_XL + swz(s, 2 * pg + 1), l1);
-      const float dd = m.dec[s];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v8[u] = dd * xv[u];
-      split8(v8, h0, l0);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v8[u] = dd * xv[8 + u];
-      split8(v8, h1, l1);
-      const uint32_t xt = sb + OFF_XT + (uint32_t)(pg >> 1) * 8192u;
+      for (int u = 0; u < 16; ++u) xt[u] = dd * xv[u];
+      const uint32_t xtb = sb + OFF_XT + (uint32_t)(pg >> 1) * 8192u;
       const uint32_t c4 = 4u * (uint32_t)(pg & 1);
-      st_shared_v4(xt + swz(s, c4 + 0), h0);
-      st_shared_v4(xt + swz(s, c4 + 1), h1);
-      st_shared_v4(xt + swz(s, c4 + 2), l0);
-      st_shared_v4(xt + swz(s, c4 + 3), l1);
+      split_store16(xtb + swz(s, c4 + 0), xtb + swz(s, c4 + 2), xt);
+      split_store16(xtb + swz(s, c4 + 1), xtb + swz(s, c4 + 3), xt + 8);
     }
     fence_proxy_async_smem();
     __syncthreads();
+    const bool h_early = m.h_ready != 0;
 
     // ---- MMA batch 1: G = C'x B'x^T (M128 N64), S~^T = x~^T B'x (M128 N128)
     if (tid == 0) {
       tc_fence_after_sync();
       const uint32_t idG = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        const uint32_t bofs = hl ? OFF_BXL : OFF_BXH;
+      for (int hl = 0; hl < 2; ++hl)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint64_t a = sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024);
-          const uint64_t bd = sdesc(sb + bofs + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024);
-          mma_bf16_ss(tmem + COL_G, a, bd, idG, (hl | j) != 0);
-        }
-      }
+        for (int j = 0; j < 8; ++j)
+          mma_bf16_ss(tmem + COL_G, sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
+                      sdesc(sb + OFF_BX + hl * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024),
+                      idG, (hl | j) != 0);
       const uint32_t idS = idesc_bf16(128, 128, 1, 1);
 #pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        const uint32_t bofs = hl ? OFF_BXL : OFF_BXH;
+      for (int hl = 0; hl < 2; ++hl)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t a = sdesc(sb + OFF_XT + j * 2048u, 8192, 1024);
-          const uint64_t bd = sdesc(sb + bofs + j * 2048u, 8192, 1024);
-          mma_bf16_ss(tmem + COL_S, a, bd, idS, (hl | j) != 0);
-        }
-      }
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_S, sdesc(sb + OFF_XT + j * 2048u, 8192, 1024),
+                      sdesc(sb + OFF_BX + hl * 16384u + j * 2048u, 8192, 1024), idS,
+                      (hl | j) != 0);
       mma_commit(&m.bar_mma1);
     }
-    // prefetch the next ticket (raw tiles are free: every thread passed the transform)
-    if (next < p.total) prefetch(next);
+    float hz[32];
+    if (z == 0) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) hz[c] = 0.f;
+    } else if (h_early) {  // H_z already published: load it while the MMAs run
+      const float* src = p.states + (((long long)bh * p.nc + z) * 64 + r) * 128 + kb;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
+        hz[4 * i] = v.x;
+        hz[4 * i + 1] = v.y;
+        hz[4 * i + 2] = v.z;
+        hz[4 * i + 3] = v.w;
+      }
+    }
 
-    // ---- epilogue 1: Mr = exp(rho_l - rho_s) G (s <= l), split-bf16, stacked rows
+    // ---- epilogue 1: Mr = exp(rho_l - rho_s) G (s <= l), split-bf16, stacked rows (over x~)
     mbar_wait(&m.bar_mma1, ph, p.err, kErrMmaWait);
     tc_fence_after_sync();
-    const int r = 16 * sub + (lane & 15);  // logical row (position l, or p for S~)
     {
       float v[32];
       tmem_ld32(tmem + lane_off + COL_G + 32u * wg, v);
       tmem_ld_wait();
       float mr[16];
-      const float rl = m.rho[r];
+      const float rl = m.rec.rho[r];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         const float send = part ? v[c] : v[16 + c];
         const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
         const float gsum = (part ? v[16 + c] : v[c]) + recv;
         const int s = 32 * wg + 16 * part + c;
-        mr[c] = (s <= r) ? expf(rl - m.rho[s]) * gsum : 0.f;
+        mr[c] = (s <= r) ? expf(rl - m.rec.rho[s]) * gsum : 0.f;
       }
-      float v8[8];
-      uint4 h0, l0, h1, l1;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v8[u] = mr[u];
-      split8(v8, h0, l0);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v8[u] = mr[8 + u];
-      split8(v8, h1, l1);
       const uint32_t ch = 4u * wg + 2u * part;
-      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 0), ch), h0);
-      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 0), ch + 1), h1);
-      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 1), ch), l0);
-      st_shared_v4(sb + OFF_MR + swz(stack_row(r, 1), ch + 1), l1);
-    }
-    fence_proxy_async_smem();
-    tc_fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {  // Y1 = Mr x
-      tc_fence_after_sync();
-      const uint32_t idY = idesc_bf16(128, 64, 0, 1);
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        const uint32_t bofs = hl ? OFF_XL : OFF_XH;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t a = sdesc(sb + OFF_MR + j * 32u, 16, 1024);
-          const uint64_t bd = sdesc(sb + bofs + j * 2048u, 8192, 1024);
-          mma_bf16_ss(tmem + COL_Y1, a, bd, idY, (hl | j) != 0);
-        }
-      }
-      mma_commit(&m.bar_mma2);
+      split_store16(sb + OFF_XT + swz(stack_row(r, 0), ch), sb + OFF_XT + swz(stack_row(r, 1), ch), mr);
+      split_store16(sb + OFF_XT + swz(stack_row(r, 0), ch + 1),
+                    sb + OFF_XT + swz(stack_row(r, 1), ch + 1), mr + 8);
     }
 
-    // ---- H_z from the predecessor chunk (bounded wait on its release flag)
-    const int kb = 64 * wg + 32 * part;  // this thread's 32 interleaved state columns
-    float hz[32];
-    if (z == 0) {
-#pragma unroll
-      for (int c = 0; c < 32; ++c) hz[c] = 0.f;
-    } else {
+    int nn = 0;
+    if (ctrl) nn = (int)atomicAdd(p.counter, 1u);  // next ticket; stored at the state update
+
+    // ---- H_z from the predecessor chunk (bounded wait on its release flag if not yet seen)
+    if (z > 0 && !h_early) {
       if (tid == 0) {
         const uint32_t* f = p.flags + (long long)bh * p.nc + z;
         uint32_t i = 0;
@@ -396,74 +318,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         hz[4 * i + 3] = v.w;
       }
     }
-    // Hx = (Re H, -Im H) interleaved, [k][p] MN-major, split hi/lo
+    // conj(H_z) interleaved as a K-major B operand [k-atom][p][64 k] (hi | lo), over B'x
+    {
+      float w[32];
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const int k = kb + c;
-      __nv_bfloat16 hh, hl;
-      split_bf16((c & 1) ? -hz[c] : hz[c], hh, hl);
-      const uint32_t off = (uint32_t)k * 128u + ((((uint32_t)r >> 3) ^ ((uint32_t)k & 7u)) << 4) +
-                           ((uint32_t)r & 7u) * 2u;
-      st_shared_u16(sb + OFF_HH + off, __bfloat16_as_ushort(hh));
-      st_shared_u16(sb + OFF_HL + off, __bfloat16_as_ushort(hl));
+      for (int c = 0; c < 32; ++c) w[c] = (c & 1) ? -hz[c] : hz[c];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        split_store16(sb + OFF_BX + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                      sb + OFF_BX + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                      w + 8 * jj);
     }
     fence_proxy_async_smem();
+    tc_fence_before_sync();
     __syncthreads();
-    if (tid == 0) {  // Y2 = Re(C' H_z) as C'x Hx
+    if (tid == 0) {  // Y1 = Mr x, Y2 = Re(C' H_z) as C'x conj(H)x
       tc_fence_after_sync();
-      const uint32_t idY = idesc_bf16(128, 64, 0, 1);
+      const uint32_t idY1 = idesc_bf16(128, 64, 0, 1);
 #pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        const uint32_t bofs = hl ? OFF_HL : OFF_HH;
+      for (int hl = 0; hl < 2; ++hl)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint64_t a = sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024);
-          const uint64_t bd = sdesc(sb + bofs + j * 2048u, 8192, 1024);
-          mma_bf16_ss(tmem + COL_Y2, a, bd, idY, (hl | j) != 0);
-        }
-      }
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_Y1, sdesc(sb + OFF_XT + j * 32u, 16, 1024),
+                      sdesc(sb + (hl ? OFF_XL : OFF_XH) + j * 2048u, 8192, 1024), idY1,
+                      (hl | j) != 0);
+      mma_commit(&m.bar_mma2);
+      const uint32_t idY2 = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          mma_bf16_ss(tmem + COL_Y2, sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
+                      sdesc(sb + OFF_BX + hl * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024),
+                      idY2, (hl | j) != 0);
       mma_commit(&m.bar_mma3);
     }
 
     // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~, publish for chunk z+1
     {
-      float s0[32], s1[32];
-      tmem_ld32(tmem + lane_off + COL_S + 64u * wg, s0);
-      tmem_ld32(tmem + lane_off + COL_S + 64u * wg + 32u, s1);
-      tmem_ld_wait();
-      float hn[32];
-      const float2 g = m.g, ct = m.ct;
-#pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        const float sa = part ? s0[c] : s1[c];
-        const float sbv = part ? s0[c + 1] : s1[c + 1];
-        const float ra = __shfl_xor_sync(0xffffffffu, sa, 16);
-        const float rbv = __shfl_xor_sync(0xffffffffu, sbv, 16);
-        const float sr = (part ? s1[c] : s0[c]) + ra;
-        const float si = -((part ? s1[c + 1] : s0[c + 1]) + rbv);  // B'x is conjugated
-        const float2 hv = cmulf(g, make_float2(hz[c], hz[c + 1]));
-        const float2 sv = cmulf(ct, make_float2(sr, si));
-        hn[c] = hv.x + sv.x;
-        hn[c + 1] = hv.y + sv.y;
-      }
+      if (ctrl) m.nxt = nn;
+      const float2 g = m.rec.g, ct = m.rec.ct;
       float* row = p.states + ((long long)bh * p.nc * 64 + r) * 128 + kb;
-      if (z == 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          __stcg(reinterpret_cast<float4*>(row) + i, make_float4(0.f, 0.f, 0.f, 0.f));
-      }
-      if (z + 1 < p.nc) {
-        float* dst = row + (long long)(z + 1) * 64 * 128;
+      for (int hh = 0; hh < 2; ++hh) {
+        float s0[16], s1[16];
+        tmem_ld16(tmem + lane_off + COL_S + 64u * wg + 16u * hh, s0);
+        tmem_ld16(tmem + lane_off + COL_S + 64u * wg + 32u + 16u * hh, s1);
+        tmem_ld_wait();
+        float hn[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          __stcg(reinterpret_cast<float4*>(dst) + i,
-                 make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
+        for (int c = 0; c < 16; c += 2) {
+          const float sa = part ? s0[c] : s1[c];
+          const float sbv = part ? s0[c + 1] : s1[c + 1];
+          const float ra = __shfl_xor_sync(0xffffffffu, sa, 16);
+          const float rbv = __shfl_xor_sync(0xffffffffu, sbv, 16);
+          const float sr = (part ? s1[c] : s0[c]) + ra;
+          const float si = -((part ? s1[c + 1] : s0[c + 1]) + rbv);  // B'x is conjugated
+          const int k = 16 * hh + c;
+          const float2 hv = cmulf(g, make_float2(hz[k], hz[k + 1]));
+          const float2 sv = cmulf(ct, make_float2(sr, si));
+          hn[c] = hv.x + sv.x;
+          hn[c + 1] = hv.y + sv.y;
+        }
+        if (z == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            __stcg(reinterpret_cast<float4*>(row + 16 * hh) + i, make_float4(0.f, 0.f, 0.f, 0.f));
+        }
+        if (z + 1 < p.nc) {
+          float* dst = row + (long long)(z + 1) * 64 * 128 + 16 * hh;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            __stcg(reinterpret_cast<float4*>(dst) + i,
+                   make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
+        }
       }
-      __threadfence();
     }
     tc_fence_before_sync();
     __syncthreads();
-    if (tid == 0 && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+    next = m.nxt;
+    // the barrier orders every thread's H stores before this gpu-scope release
+    if (ctrl && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+    if (next < p.total) prefetch_regs(next);
 
     // ---- output y = Y1 + exp(rho_l) Y2
     mbar_wait(&m.bar_mma2, ph, p.err, kErrMmaWait);
@@ -474,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tmem + lane_off + COL_Y1 + 32u * wg, y1);
       tmem_ld32(tmem + lane_off + COL_Y2 + 32u * wg, y2);
       tmem_ld_wait();
-      const float el = m.el[r];
+      const float el = m.rec.el[r];
       float out[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -560,6 +496,8 @@ bool fwd_supported(const Problem& p) {
   return total < (1ll << 30);
 }
 
+size_t states_bytes(const Problem& p) { return states_h_bytes(p) + chunk_prep_bytes(p); }
+
 size_t fwd_workspace_bytes(const Problem& p) {
   const size_t nc = (size_t)((p.T + 63) / 64);
   return 256 + 4 * (size_t)p.Bsz * p.H * nc;
@@ -578,11 +516,10 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
               reinterpret_cast<uintptr_t>(p.x) % 16 == 0)
                  ? 1
                  : 0;
-  fp.A = p.A;
-  fp.dt = p.dt;
-  for (int i = 0; i < 3; ++i) fp.dts[i] = p.dts[i];
   fp.y = y;
   fp.states = static_cast<float*>(states);
+  ChunkRec* recs = reinterpret_cast<ChunkRec*>(static_cast<char*>(states) + states_h_bytes(p));
+  fp.recs = recs;
   uint32_t* w = static_cast<uint32_t*>(ws);
   fp.err = w;
   fp.counter = w + 1;
@@ -591,13 +528,15 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
     return M3SSD_ERR_LAUNCH;
   if (cudaMemsetAsync(ws, 0, fwd_workspace_bytes(p), st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  const int rc = run_chunk_prep(p, recs, st);
+  if (rc != M3SSD_OK) return rc;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (cudaFuncSetAttribute(k_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kSmemBytes) != cudaSuccess)
     return M3SSD_ERR_LAUNCH;
-  const int grid = fp.total < sms ? fp.total : sms;
+  const int grid = fp.total < 2 * sms ? fp.total : 2 * sms;
   k_fwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, fp);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }

@@ -6,6 +6,7 @@
 #include <stddef.h>
 
 #include "m3ssd_common.cuh"
+#include "tc_common.cuh"
 
 namespace m3ssd {
 namespace tc {
@@ -14,8 +15,19 @@ namespace tc {
 constexpr int kChunk = 64;
 
 // kernels enqueued by one run_fwd / run_bwd call (memsets of the flag areas are not kernels)
-constexpr int kFwdLaunches = 1;
-constexpr int kBwdLaunches = 2;
+constexpr int kFwdLaunches = 2;  // k_chunk_prep, k_fwd_tc
+constexpr int kBwdLaunches = 2;  // k_bwd_tc, k_bwd_tc_dA (records come from the forward)
+
+// `states` of a tensor-core problem: the chunk-entry states H_z ([b*H+h][chunk][64 p][128] fp32)
+// followed by the per-chunk decay records written by the forward and reused by the backward
+size_t states_bytes(const Problem& p);
+inline size_t states_h_bytes(const Problem& p) {
+  return sizeof(float) * 64 * 128 * (size_t)p.Bsz * p.H * ((p.T + 63) / 64);
+}
+
+// per-chunk decay records (tc_prep.cu)
+size_t chunk_prep_bytes(const Problem& p);
+int run_chunk_prep(const Problem& p, ChunkRec* out, cudaStream_t st);
 
 // TMA descriptor for a (B, T, H, N) complex64 tensor viewed as (B, T, H, 2N) fp32, box of
 // 64 time steps x 2N floats of one head (zero fill past T)

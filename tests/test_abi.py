@@ -64,7 +64,10 @@ def test_check_problem(lib, kw, code):
 def test_sizes(lib):
     p = prob()
     nc = 256 // 64
-    assert lib.m3ssd_states_bytes(ctypes.byref(p)) == 8 * 2 * 4 * nc * 64 * 64
+    # tensor-core shape: chunk-entry states (fp32 [64][128] per chunk) + a 1824-byte decay record
+    assert lib.m3ssd_states_bytes(ctypes.byref(p)) == (8 * 64 * 64 + 1824) * 2 * 4 * nc
+    q = prob(headdim=32)  # fp32 path only: complex64 [D][N] per chunk
+    assert lib.m3ssd_states_bytes(ctypes.byref(q)) == 8 * 2 * 4 * nc * 32 * 64
     assert lib.m3ssd_fwd_workspace_bytes(ctypes.byref(p)) > 0
     assert lib.m3ssd_bwd_workspace_bytes(ctypes.byref(p)) > 0
     bad = prob(chunk=0)
