@@ -692,19 +692,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
-// dA[h] = sum over batch and chunks of the per-chunk partials (fixed order)
-__global__ void k_bwd_tc_dA(const float2* __restrict__ dapart, int Bsz, int H, int nc,
-                            float2* __restrict__ dA) {
-  const int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h >= H) return;
+// dA[h] = sum over batch and chunks of the per-chunk partials: one CTA per head, fixed-order
+// strided partial sums and a fixed tree, so the result is deterministic.
+__global__ void __launch_bounds__(256) k_bwd_tc_dA(const float2* __restrict__ dapart, int Bsz,
+                                                   int H, int nc, float2* __restrict__ dA) {
+  __shared__ float2 red[256];
+  const int h = blockIdx.x;
+  const int n = Bsz * nc;
   float2 acc = make_float2(0.f, 0.f);
-  for (int b = 0; b < Bsz; ++b)
-    for (int z = 0; z < nc; ++z) {
-      const float2 v = dapart[((long long)b * H + h) * nc + z];
-      acc.x += v.x;
-      acc.y += v.y;
+  for (int i = threadIdx.x; i < n; i += 256) {
+    const int b = i / nc, z = i - b * nc;
+    const float2 v = dapart[((long long)b * H + h) * nc + z];
+    acc.x += v.x;
+    acc.y += v.y;
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      red[threadIdx.x].x += red[threadIdx.x + o].x;
+      red[threadIdx.x].y += red[threadIdx.x + o].y;
     }
-  dA[h] = acc;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) dA[h] = red[0];
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -782,7 +793,7 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
   k_bwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, bp);
-  k_bwd_tc_dA<<<(p.H + 127) / 128, 128, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, dA);
+  k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, dA);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }
 
