@@ -143,7 +143,9 @@ M3SSD_API int m3ssd_bwd(const m3ssd_bwd_args* args, void* stream);
 
 /* Name of the implementation m3ssd_fwd / m3ssd_bwd use for this problem ("tcgen05-bf16x2",
  * "simt-fp32"). The tensor-core path needs head_dim = state_dim = 64, real x, and B/C with a
- * contiguous state dimension and 16-byte aligned strides; otherwise the fp32 path runs.
+ * contiguous state dimension and 16-byte aligned strides; otherwise the fp32 path runs. The
+ * backward additionally needs 16-byte aligned dx, dB and dC pointers (any allocator's default);
+ * m3ssd_bwd runs the fp32 path for other pointers, which this query cannot see.
  * Host-only query, no device work. */
 M3SSD_API const char* m3ssd_fwd_path(const m3ssd_problem* prob);
 M3SSD_API const char* m3ssd_bwd_path(const m3ssd_problem* prob);

@@ -249,7 +249,9 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   if (rc) return rc;
   long long dys[4];
   for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
-  if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p))
+  // the tensor-core backward writes dx, dB, dC with TMA stores: 16-byte aligned outputs
+  if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p) && aligned(a->dx, 16) &&
+      aligned(a->dB, 16) && aligned(a->dC, 16))
     return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, static_cast<float*>(a->dx),
                               static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
                               static_cast<float2*>(a->dC), a->ddt, a->workspace,

@@ -32,7 +32,8 @@ namespace tc {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kWorkers = 256;              // warps 0-7: operand transforms and epilogues
+constexpr int kThreads = kWorkers + 32;    // warp 8: tickets, TMA/bulk loads, flags, MMA issue
 // shared memory map
 constexpr uint32_t OFF_C = 0;        // C'x stacked [2 k-atoms][128][64]; raw C tile lands first
 constexpr uint32_t OFF_B = 32768;    // B'x (conjugate-interleaved) stacked; raw B tile lands first
@@ -41,27 +42,31 @@ constexpr uint32_t OFF_DY = 81920;   // dy stacked over l [128][64 p]
 constexpr uint32_t OFF_DYT = 98304;  // e_l dy stacked over p, MN [2][64 l][64]; then Mr (same form)
 constexpr uint32_t OFF_DGK = 114688; // dG' stacked over l [128][64 s]
 constexpr uint32_t OFF_DGM = 131072; // dG' stacked over s, MN [2][64 l][64]
-constexpr uint32_t OFF_DS = 147456;  // dS'x hi [2][64 p][64 k], lo at +16384
-constexpr uint32_t OFF_H = 180224;   // conj(H_z) hi [2][64 p][64 k], lo at +16384
+constexpr uint32_t OFF_DS = 147456;  // dS_z (fp32, lands by bulk copy), then dS'x hi | lo
+constexpr uint32_t OFF_H = 180224;   // H_z (fp32, lands by bulk copy), then conj(H_z) hi | lo
 constexpr uint32_t OFF_MISC = 212992;
 constexpr uint32_t kMiscBytes = 8192;
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBytes + 1024;
-constexpr uint32_t kTmaBytes = 2u * 64u * 128u * 4u;
+constexpr uint32_t kLoadBytes = 2u * 64u * 128u * 4u + (uint32_t)sizeof(ChunkRec);
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: batch 1, batch 2, batch 3 (reusing batch-1 columns), dBb (reusing dCa)
 constexpr uint32_t COL_G = 0, COL_DM = 64, COL_Q = 128, COL_DCA = 256, COL_DCB = 384;
 constexpr uint32_t COL_DXA = 0, COL_DXB = 64, COL_DBA = 128, COL_DBB = 256;
 
 struct Misc {
-  ChunkRec rec;  // this chunk's decay quantities (bulk-copied with the B/C tiles)
-  uint64_t bar_tma, bar1, bar2, bar3, bar4;
-  float2 rc[4][64];
-  float2 rb[4][64];
-  float2 dgp[8];   // per-warp partials of <dS_{z-1}, H_z>
-  float2 dgam;     // <dS_z, H_{z+1}> handed over by the chunk z+1 ticket
+  ChunkRec rec[2];  // decay records of the current and the next ticket
+  // control -> workers: B / C / record landed, H_z landed, dS landed, ticket published, MMA
+  // commits 1..4, and the staging buffers of the previous ticket's dx / dB stores read (stfree)
+  uint64_t bar_tma, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
+  // workers -> control (one arrival per worker warp)
+  uint64_t bar_ops1, bar_ops2, bar_colfree, bar_dc, bar_hfree, bar_dx, bar_db, bar_done;
+  float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
+  float2 rc[64];    // sum_n dC'_{ln} conj(C'_{ln})
+  float2 rb[64];    // sum_n dB'_{sn} conj(B'_{sn})
+  float2 dgp[8];    // per-warp partials of <dS_{z-1}, H_z>
   float2 dap[2];
   float2 sfx;
-  int first, nxt;
+  int tick[2];
   uint32_t tmem_base;
 };
 static_assert(sizeof(Misc) <= kMiscBytes, "misc area");
@@ -75,40 +80,98 @@ struct BwdParams {
   long long dys[4];
   int dy_vec;
   const float2* A;
+  const float2* Bm;
+  long long bs[4];
+  const float2* Cm;
+  long long cs[4];
   const ChunkRec* recs;
   const float* states;
-  float* dx;
-  float2* dB;
-  float2* dC;
   float* ddt;
   float2* dapart;
   float* ring;
-  float2* dgring;
+  float4* dgring;
   uint32_t* flags;
   uint32_t* counter;
   uint32_t* err;
 };
 
-__device__ __forceinline__ void load16(const float* base_ptr, const long long st[4], int vec, int T,
-                                       int b, int t, int h, int p0, float (&v)[16]) {
-  if (t >= T) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+// (sequence, chunk) of a ticket: tickets run over sequences fastest, chunks in reverse order
+struct TicketPos {
+  int bh, z, b, h;
+};
+__device__ __forceinline__ TicketPos ticket_pos(int tk, int BH, int H, int nc) {
+  TicketPos q;
+  const int zr = tk / BH;
+  q.bh = tk - zr * BH;
+  q.z = nc - 1 - zr;
+  q.b = q.bh / H;
+  q.h = q.bh - q.b * H;
+  return q;
+}
+
+// ---------------------------------------------------------------- control-warp helpers
+// (out of line: each runs once per ticket, and the kernel must stay small for the I-cache)
+static __device__ __noinline__ void ctl_load_bc(const CUtensorMap* tmB, const CUtensorMap* tmC,
+                                                uint8_t* smem, Misc* m, const ChunkRec* recs,
+                                                int nc, TicketPos q, int slot) {
+  mbar_arrive_expect_tx(&m->bar_tma, kLoadBytes);
+  tma_load_4d(smem + OFF_B, tmB, &m->bar_tma, 0, q.h, q.z * 64, q.b);
+  tma_load_4d(smem + OFF_C, tmC, &m->bar_tma, 0, q.h, q.z * 64, q.b);
+  bulk_load(&m->rec[slot], recs + (long long)q.bh * nc + q.z, (uint32_t)sizeof(ChunkRec),
+            &m->bar_tma);
+}
+static __device__ __noinline__ void ctl_load_h(uint8_t* smem, Misc* m, const float* states, int nc,
+                                               TicketPos q) {
+  mbar_arrive_expect_tx(&m->bar_h, 32768u);
+  bulk_load(smem + OFF_H, states + ((long long)q.bh * nc + q.z) * 64 * 128, 32768u, &m->bar_h);
+}
+// dS_z (and <dS_z, H_{z+1}>) from the chunk z+1 ticket once its flag is published
+static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const float* ring,
+                                                const float4* dgring, const uint32_t* flags,
+                                                uint32_t* err, int nc, TicketPos q) {
+  if (q.z == nc - 1) {
+    mbar_arrive(&m->bar_ds);
     return;
   }
-  const float* base = base_ptr + b * st[0] + (long long)t * st[1] + h * st[2];
-  if (vec) {
+  const uint32_t* f = flags + (long long)q.bh * nc + q.z;
+  uint32_t i = 0;
+  for (; i < kSpinLimit; ++i) {
+    if (ld_acquire_gpu(f) != 0u) break;
+    __nanosleep(64);
+  }
+  if (i == kSpinLimit) atomicOr(err, kErrFlagWait);
+  fence_proxy_async_global();  // the ring was written with plain stores by another CTA
+  mbar_arrive_expect_tx(&m->bar_ds, 32768u + 16u);
+  bulk_load(smem + OFF_DS, ring + ((long long)q.bh * 4 + (q.z & 3)) * 64 * 128, 32768u,
+            &m->bar_ds);
+  bulk_load(&m->dgam, dgring + (long long)q.bh * 4 + (q.z & 3), 16u, &m->bar_ds);
+}
+// TMA stores of a 64-row output tile from its 32-float staging segments (segments 0, 1 at off01,
+// 2, 3 at off23), one bulk group
+static __device__ __noinline__ void ctl_store_tile(const CUtensorMap* map, uint8_t* smem,
+                                                   uint32_t off01, uint32_t off23, int nseg,
+                                                   TicketPos q) {
+  for (int seg = 0; seg < nseg; ++seg)
+    tma_store_4d(map, smem + (seg < 2 ? off01 : off23) + (seg & 1) * 8192, 32 * seg, q.h,
+                 q.z * 64, q.b);
+  bulk_commit_group();
+}
+
+// 8 consecutive floats x[b, t, h, p0 .. p0+7] (zeros past the end of the sequence)
+__device__ __forceinline__ void load8(const float* base, long long pstride, int vec, bool valid,
+                                      int p0, float* v) {
+  if (!valid) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 q = ldg_nc_v4(base + p0 + 4 * i);
-      v[4 * i] = q.x;
-      v[4 * i + 1] = q.y;
-      v[4 * i + 2] = q.z;
-      v[4 * i + 3] = q.w;
-    }
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    return;
+  }
+  if (vec) {
+    const float4 q0 = ldg_nc_v4(base + p0), q1 = ldg_nc_v4(base + p0 + 4);
+    v[0] = q0.x; v[1] = q0.y; v[2] = q0.z; v[3] = q0.w;
+    v[4] = q1.x; v[5] = q1.y; v[6] = q1.z; v[7] = q1.w;
   } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __ldg(base + (long long)(p0 + i) * st[3]);
+    for (int i = 0; i < 8; ++i) v[i] = __ldg(base + (long long)(p0 + i) * pstride);
   }
 }
 
@@ -116,8 +179,10 @@ __device__ __forceinline__ float2 cmul2(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
-// x32 load of a 64-column accumulator block, hi/lo partner exchange: thread `part` keeps 16
-// columns (part 0: first 16, part 1: last 16) of the 32 its warp group owns.
+// Full sums of a stacked accumulator: TMEM lanes L and L ^ 8 hold the hi-row and lo-row partials
+// of one logical row. Of a 32-column block, the thread with `part` p keeps columns [16 p, 16 p + 16)
+// and sends the other half to its partner. (tcgen05.ld takes one address for the whole warp, so
+// both halves are loaded and selected per lane.)
 __device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)[16]) {
   float v[32];
   tmem_ld32(taddr, v);
@@ -125,24 +190,50 @@ __device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
     const float send = part ? v[c] : v[16 + c];
-    const float recv = __shfl_xor_sync(0xffffffffu, send, 8);
-    out[c] = (part ? v[16 + c] : v[c]) + recv;
+    out[c] = (part ? v[16 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
   }
 }
-// two x32 loads of a 128-column accumulator block (the warp group's 64 columns), exchange:
-// thread `part` keeps 32 columns.
+// the same over a 64-column block: columns [32 p, 32 p + 32)
 __device__ __forceinline__ void ld_exch32(uint32_t taddr, int part, float (&out)[32]) {
+  float v[32];
+  tmem_ld32(taddr, out);
+  tmem_ld32(taddr + 32u, v);
+  tmem_ld_wait();
 #pragma unroll
-  for (int ch = 0; ch < 2; ++ch) {
-    float v[32];
-    tmem_ld32(taddr + 32u * ch, v);
-    tmem_ld_wait();
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const float t = __shfl_xor_sync(0xffffffffu, v[c], 8);
-      if (part == ch) out[c] = v[c] + t;
-    }
+  for (int c = 0; c < 32; ++c) {
+    const float keep = part ? v[c] : out[c];
+    const float send = part ? out[c] : v[c];
+    out[c] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
   }
+}
+
+// Sum over the warp of 16 per-lane values. Lane L ends with the total of value
+// 8 bit4(L) + 4 bit3(L) + 2 bit2(L) + bit1(L) (16 shuffles instead of 80).
+__device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = (lane & 16) != 0;
+    const float send = up ? v[i] : v[8 + i];
+    v[i] = (up ? v[8 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = (lane & 8) != 0;
+    const float send = up ? v[i] : v[4 + i];
+    v[i] = (up ? v[4 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = (lane & 4) != 0;
+    const float send = up ? v[i] : v[2 + i];
+    v[i] = (up ? v[2 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool up = (lane & 2) != 0;
+    const float send = up ? v[0] : v[1];
+    v[0] = (up ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
 __device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
@@ -155,34 +246,103 @@ __device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr,
   st_shared_v4(lo_addr, l);
 }
 
+// the issuing warp's lane arrives once every lane's shared-memory writes are visible to the
+// async proxy (tensor core, TMA) and its TMEM reads are complete
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  fence_proxy_async_smem();
+  tc_fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+__device__ __forceinline__ void workers_sync() { named_sync(1, kWorkers); }
+
+// fp32 staging tile for a TMA store: 32-float column segment of a 64-row tile, 128-byte rows,
+// 16-byte chunks swizzled by row (the CU_TENSOR_MAP_SWIZZLE_128B layout)
+__device__ __forceinline__ uint32_t stage_addr(uint32_t seg_base, uint32_t row, uint32_t chunk) {
+  return seg_base + row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+// segment s of a staged tile whose segments 0, 1 sit at seg01 and 2, 3 at seg23
+__device__ __forceinline__ uint32_t stage_seg(uint32_t seg01, uint32_t seg23, uint32_t s) {
+  return (s < 2u ? seg01 : seg23) + (s & 1u) * 8192u;
+}
+
+// ---------------------------------------------------------------- worker helpers (out of line)
+// Epilogue of dC and dB: v = (a + w b) conj(rot) over this thread's 32 state columns (accumulator
+// blocks at ta, tb), conjugated if conj_out, into the staging tile. dC: w = e_l, rot = cis(theta_l);
+// dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out.
+static __device__ __noinline__ void combine_stage(uint32_t ta, uint32_t tb, int part, float w,
+                                                  float2 rot, bool conj_out, uint32_t seg,
+                                                  uint32_t row, uint64_t* colfree, int lane) {
+  float a[32], bb[32];
+  ld_exch32(ta, part, a);
+  ld_exch32(tb, part, bb);
+  if (colfree != nullptr) warp_arrive(colfree, lane);
+  const float2 nr = make_float2(rot.x, -rot.y);
+  const float cj = conj_out ? -1.f : 1.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 v0 = cmul2(make_float2(a[4 * i] + w * bb[4 * i], a[4 * i + 1] + w * bb[4 * i + 1]), nr);
+    const float2 v1 =
+        cmul2(make_float2(a[4 * i + 2] + w * bb[4 * i + 2], a[4 * i + 3] + w * bb[4 * i + 3]), nr);
+    st_shared_v4(stage_addr(seg, row, (uint32_t)i),
+                 make_uint4(__float_as_uint(v0.x), __float_as_uint(cj * v0.y),
+                            __float_as_uint(v1.x), __float_as_uint(cj * v1.y)));
+  }
+}
+// Row sums out[l] = sum_n (Y rot)_{ln} conj(round(X rot)_{ln}) for the warp's 8 rows l = row0 ..
+// row0+7 of a chunk: Y from the staging tile (dC or dB), X re-read from global memory (C or B,
+// coalesced: one 512-byte row per warp load), rounded to its split-bf16 value so the sum matches
+// the contractions. dC' conj(C'): rot = cis(theta_l); dB' conj(B'): rot = conj(cis(theta_s)).
+static __device__ __noinline__ void row_sums(const float4* Xg, long long base4, long long stride4,
+                                             int nvalid, uint32_t seg01, uint32_t seg23,
+                                             const float2* cis, bool conj_rot, int row0,
+                                             float* out, int lane) {
+  float4 xv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    xv[k] = (k < nvalid) ? __ldcg(Xg + base4 + k * stride4 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint32_t seg = stage_seg(seg01, seg23, (uint32_t)(lane >> 3));
+  float acc[16];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 cs = cis[row0 + k];
+    const float2 rot = make_float2(cs.x, conj_rot ? -cs.y : cs.y);
+    const float4 dv = ld_shared_f4(stage_addr(seg, (uint32_t)(row0 + k), (uint32_t)(lane & 7)));
+    const float2 d0 = cmul2(make_float2(dv.x, dv.y), rot), d1 = cmul2(make_float2(dv.z, dv.w), rot);
+    const float2 c0 = split_round2(cmul2(make_float2(xv[k].x, xv[k].y), rot));
+    const float2 c1 = split_round2(cmul2(make_float2(xv[k].z, xv[k].w), rot));
+    acc[2 * k] = d0.x * c0.x + d0.y * c0.y + d1.x * c1.x + d1.y * c1.y;
+    acc[2 * k + 1] = d0.y * c0.x - d0.x * c0.y + d1.y * c1.x - d1.x * c1.y;
+  }
+  const float tot = warp_sum16(acc, lane);
+  if ((lane & 1) == 0) out[2 * row0 + (lane >> 1)] = tot;
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
     k_bwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
-             const BwdParams p) {
+             const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDB,
+             const __grid_constant__ CUtensorMap tmDC, const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sb = smem_u32(smem);
   Misc& m = *reinterpret_cast<Misc*>(smem + OFF_MISC);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int sub = warp & 3, wg = warp >> 2;
-  const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
-  const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
   const int BH = p.Bsz * p.H;
 
-  int first = 0;
   if (tid == 0) {
-    mbar_init(&m.bar_tma, 1);
-    mbar_init(&m.bar1, 1);
-    mbar_init(&m.bar2, 1);
-    mbar_init(&m.bar3, 1);
-    mbar_init(&m.bar4, 1);
+    uint64_t* one[9] = {&m.bar_tma, &m.bar_h, &m.bar_ds, &m.bar_ctl, &m.bar1,
+                        &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
+    uint64_t* eight[8] = {&m.bar_ops1, &m.bar_ops2, &m.bar_colfree, &m.bar_dc,
+                          &m.bar_hfree, &m.bar_dx, &m.bar_db, &m.bar_done};
+#pragma unroll
+    for (int i = 0; i < 9; ++i) mbar_init(one[i], 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
-    prefetch_tmap(&tmB);
-    prefetch_tmap(&tmC);
-    first = (int)atomicAdd(p.counter, 1u);
-    m.first = first;
   }
   if (warp == 0) {
     tmem_alloc(&m.tmem_base, kTmemCols);
@@ -192,502 +352,472 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = m.tmem_base;
-  const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
-  int ticket = m.first;
 
-  float xv[16], gv[16];
-  auto prefetch_regs = [&](int tk) {
-    const int zr = tk / BH, bh = tk - zr * BH;
-    const int z = p.nc - 1 - zr;
-    const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
-    load16(p.x, p.xs, p.x_vec, p.T, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
-    load16(p.dy, p.dys, p.dy_vec, p.T, b, t0 + (tid >> 2), h, 16 * (tid & 3), gv);
-  };
-  if (ticket < p.total) prefetch_regs(ticket);
-
-  uint32_t iter = 0;
-  while (ticket < p.total) {
-    const uint32_t ph = iter & 1u;
-    const int zr = ticket / BH, bh = ticket - zr * BH;
-    const int z = p.nc - 1 - zr;
-    const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
-    __syncthreads();  // previous ticket complete (including generic reads of sB / sC)
-    int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
-    if (tid == 0) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec) + 32768u);
-      tma_load_4d(smem + OFF_B, &tmB, &m.bar_tma, 0, h, t0, b);
-      tma_load_4d(smem + OFF_C, &tmC, &m.bar_tma, 0, h, t0, b);
-      bulk_load(&m.rec, p.recs + (long long)bh * p.nc + z, (uint32_t)sizeof(ChunkRec), &m.bar_tma);
-      bulk_load(smem + OFF_H, p.states + ((long long)bh * p.nc + z) * 64 * 128, 32768u,
-                &m.bar_tma);  // H_z (fp32 [p][128]); converted in place below
+  if (warp == kWorkers / 32) {
+    // =============================== control warp (lane 0) ===============================
+    if (lane == 0) {
+      prefetch_tmap(&tmB);
+      prefetch_tmap(&tmC);
+      prefetch_tmap(&tmDX);
+      prefetch_tmap(&tmDB);
+      prefetch_tmap(&tmDC);
+      int cur = (int)atomicAdd(p.counter, 1u);
+      m.tick[0] = cur;
+      mbar_arrive(&m.bar_ctl);
+      TicketPos qc = ticket_pos(cur, BH, p.H, p.nc);
+      if (cur < p.total) {
+        ctl_load_bc(&tmB, &tmC, smem, &m, p.recs, p.nc, qc, 0);
+        ctl_load_h(smem, &m, p.states, p.nc, qc);
+        ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qc);
+      }
+      uint32_t it = 0;
+      while (cur < p.total) {
+        const uint32_t ph = it & 1u;
+        // batch 1: G = C'x B'x^T, dM = dy x^T, Q^T = (e dy)^T C'x
+        mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        {
+          const uint32_t id64 = idesc_bf16(128, 64, 0, 0);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t ko = (j >> 2) * 16384u + (j & 3) * 32u;
+              mma_bf16_ss(tmem + COL_G, sdesc(sb + OFF_C + ko, 16, 1024),
+                          sdesc(sb + OFF_B + ko + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
+            }
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_DM, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
+                          sdesc(sb + OFF_X + j * 32u + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
+          const uint32_t idq = idesc_bf16(128, 128, 1, 1);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_Q, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
+                          sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idq,
+                          (hp | j) != 0);
+          mma_commit(&m.bar1);
+        }
+        // publish the next ticket (workers prefetch its x and dy)
+        const int nxt = (int)atomicAdd(p.counter, 1u);
+        m.tick[(it + 1) & 1] = nxt;
+        mbar_arrive(&m.bar_ctl);
+        const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
+        // carry hand-off, then batches 2 and 3
+        mbar_wait(&m.bar_ops2, ph, p.err, kErrMmaWait);
+        if (qc.z > 0) {
+          float2 dg = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            dg.x += m.dgp[w].x;
+            dg.y += m.dgp[w].y;
+          }
+          __stcg(p.dgring + (long long)qc.bh * 4 + ((qc.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
+          // the workers' ring stores happened before their bar_ops2 arrivals
+          fence_proxy_async_global();
+          st_release_gpu(p.flags + (long long)qc.bh * p.nc + qc.z - 1, 1u);
+        }
+        tc_fence_after_sync();
+        {
+          const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_DCA, sdesc(sb + OFF_DGK + j * 32u, 16, 1024),
+                          sdesc(sb + OFF_B + j * 4096u + hp * 1024u, 16384, 2048), id128,
+                          (hp | j) != 0);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_DCB, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
+                          sdesc(sb + OFF_H + hp * 16384u + j * 2048u, 8192, 1024), id128,
+                          (hp | j) != 0);
+          mma_commit(&m.bar2);
+          const uint32_t idxa = idesc_bf16(128, 64, 1, 1);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_DXA, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
+                          sdesc(sb + OFF_DY + j * 4096u + hp * 1024u, 8192, 2048), idxa,
+                          (hp | j) != 0);
+          const uint32_t idxb = idesc_bf16(128, 64, 0, 0);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j)
+              mma_bf16_ss(tmem + COL_DXB,
+                          sdesc(sb + OFF_B + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
+                          sdesc(sb + OFF_DS + hp * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16,
+                                1024),
+                          idxb, (hp | j) != 0);
+          const uint32_t idba = idesc_bf16(128, 128, 1, 1);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_DBA, sdesc(sb + OFF_DGM + j * 2048u, 8192, 1024),
+                          sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idba,
+                          (hp | j) != 0);
+          mma_commit(&m.bar3);
+        }
+        // the next ticket's B, C tiles as soon as batch 3 has read sB / sC; its record slot once
+        // the workers finished the ticket before this one
+        if (nxt < p.total) {
+          if (it > 0) mbar_wait(&m.bar_done, ph ^ 1u, p.err, kErrMmaWait);
+          mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
+          ctl_load_bc(&tmB, &tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1));
+        }
+        // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them
+        mbar_wait(&m.bar_colfree, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        {
+          const uint32_t idbb = idesc_bf16(128, 128, 0, 1);
+#pragma unroll 1
+          for (int hp = 0; hp < 2; ++hp)
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j)
+              mma_bf16_ss(tmem + COL_DBB, sdesc(sb + OFF_X + j * 32u, 16, 1024),
+                          sdesc(sb + OFF_DS + hp * 16384u + j * 2048u, 8192, 1024), idbb,
+                          (hp | j) != 0);
+          mma_commit(&m.bar4);
+        }
+        // dC from its staging tile in sH; then the next H_z into sH once the store and the
+        // workers' row-sum pass have read it
+        mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
+        ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc);
+        mbar_wait(&m.bar_hfree, ph, p.err, kErrMmaWait);
+        bulk_wait_read_all();
+        if (nxt < p.total) ctl_load_h(smem, &m, p.states, p.nc, qn);
+        // dx from sDGK, dB from sDYT / sDGM, then the next ticket's dS once dBb has read sDS
+        mbar_wait(&m.bar_dx, ph, p.err, kErrMmaWait);
+        ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc);
+        mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
+        ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc);
+        if (nxt < p.total) {
+          mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
+          ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn);
+        }
+        bulk_wait_read_all();
+        mbar_arrive(&m.bar_stfree);
+        cur = nxt;
+        qc = qn;
+        ++it;
+      }
+      bulk_wait_all();
     }
+    __syncwarp();
+  } else {
+    // =============================== worker warps 0-7 ===============================
+    const int sub = warp & 3, wg = warp >> 2;
+    const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
+    const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
+    const int kb = 64 * wg + 32 * part;                        // this thread's state columns
+    const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
+    // x / dy staging: rows xs0 and xs0 + 32, columns 8 (tid & 7) .. + 7 (8 lanes per row)
+    const int xs0 = tid >> 3, xp0 = 8 * (tid & 7);
+    float xv[16], gv[16];
+    mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
+    int next = m.tick[0];
+    // The loop turns at the prefetch point: x and dy of ticket `next` are loaded into registers,
+    // then the epilogues of the ticket in flight run, then ticket `next` starts.
+    bool active = false;  // a ticket's epilogues are pending
+    uint32_t it = 0;      // index of that ticket
+    TicketPos q{};
+    int t0 = 0;
+    float2 dgam = make_float2(0.f, 0.f);
+    for (;;) {
+      if (next < p.total) {
+        const TicketPos qx = ticket_pos(next, BH, p.H, p.nc);
+        const int tx = qx.z * 64 + xs0;
+        const float* xr = p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2];
+        const float* gr = p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2];
+        load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
+        load8(xr + 32 * p.xs[1], p.xs[3], p.x_vec, tx + 32 < p.T, xp0, xv + 8);
+        load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
+        load8(gr + 32 * p.dys[1], p.dys[3], p.dy_vec, tx + 32 < p.T, xp0, gv + 8);
+      }
+      if (active) {
+        const uint32_t ph = it & 1u;
+        const ChunkRec& rec = m.rec[ph];
+        // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)) -> staging tile in sH
+        mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        combine_stage(tmem + lane_off + COL_DCA + 64u * wg, tmem + lane_off + COL_DCB + 64u * wg,
+                      part, rec.el[r], rec.cis[r], false,
+                      stage_seg(sb + OFF_H, sb + OFF_H + 16384u, (uint32_t)(kb >> 5)), (uint32_t)r,
+                      &m.bar_colfree, lane);
+        warp_arrive(&m.bar_dc, lane);
+        workers_sync();
+        row_sums(reinterpret_cast<const float4*>(p.Cm),
+                 (q.b * p.cs[0] + (long long)(t0 + 8 * warp) * p.cs[1] + q.h * p.cs[2]) >> 1,
+                 p.cs[1] >> 1, p.T - (t0 + 8 * warp), sb + OFF_H, sb + OFF_H + 16384u, rec.cis,
+                 false, 8 * warp, reinterpret_cast<float*>(m.rc), lane);
+        warp_arrive(&m.bar_hfree, lane);
 
-    mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // B, C tiles, decay record, H_z
+        // ---- epilogue 3: dx = dXa + dec_s dXb -> staging tile in sDGK
+        mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        {
+          float xa[16], xb[16];
+          ld_exch16(tmem + lane_off + COL_DXA + 32u * wg, part, xa);
+          ld_exch16(tmem + lane_off + COL_DXB + 32u * wg, part, xb);
+          const float d = rec.dec[r];
+          const uint32_t seg = sb + OFF_DGK + (uint32_t)wg * 8192u;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            st_shared_v4(stage_addr(seg, (uint32_t)r, (uint32_t)(4 * part + i)),
+                         make_uint4(__float_as_uint(xa[4 * i] + d * xb[4 * i]),
+                                    __float_as_uint(xa[4 * i + 1] + d * xb[4 * i + 1]),
+                                    __float_as_uint(xa[4 * i + 2] + d * xb[4 * i + 2]),
+                                    __float_as_uint(xa[4 * i + 3] + d * xb[4 * i + 3])));
+        }
+        warp_arrive(&m.bar_dx, lane);
+        // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s) -> staging tiles in sDYT, sDGM
+        mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        combine_stage(tmem + lane_off + COL_DBA + 64u * wg, tmem + lane_off + COL_DBB + 64u * wg,
+                      part, rec.dec[r], rec.cis[r], true,
+                      stage_seg(sb + OFF_DYT, sb + OFF_DGM, (uint32_t)(kb >> 5)), (uint32_t)r,
+                      nullptr, lane);
+        warp_arrive(&m.bar_db, lane);
+        workers_sync();
+        row_sums(reinterpret_cast<const float4*>(p.Bm),
+                 (q.b * p.bs[0] + (long long)(t0 + 8 * warp) * p.bs[1] + q.h * p.bs[2]) >> 1,
+                 p.bs[1] >> 1, p.T - (t0 + 8 * warp), sb + OFF_DYT, sb + OFF_DGM, rec.cis, true,
+                 8 * warp, reinterpret_cast<float*>(m.rb), lane);
+        workers_sync();
 
-    // ---- x, dy (stacked over rows, K = p) and e_l dy (stacked over p, MN) from registers
-    {
-      const int s = tid >> 2, pg = tid & 3;
-      split8_store(sb + OFF_X + swz(stack8(s, 0), 2 * pg), sb + OFF_X + swz(stack8(s, 1), 2 * pg),
-                   xv);
-      split8_store(sb + OFF_X + swz(stack8(s, 0), 2 * pg + 1),
-                   sb + OFF_X + swz(stack8(s, 1), 2 * pg + 1), xv + 8);
-      split8_store(sb + OFF_DY + swz(stack8(s, 0), 2 * pg),
-                   sb + OFF_DY + swz(stack8(s, 1), 2 * pg), gv);
-      split8_store(sb + OFF_DY + swz(stack8(s, 0), 2 * pg + 1),
-                   sb + OFF_DY + swz(stack8(s, 1), 2 * pg + 1), gv + 8);
-      const float e = m.rec.el[s];
-      float w[16];
+        // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial
+        float2 ds = make_float2(0.f, 0.f);
+        if (tid < 64) {
+          const int l = tid;
+          ds.x = m.rc[l].x - m.rb[l].x;
+          ds.y = m.rc[l].y - m.rb[l].y;
+          if (l == 63) {
+            ds.x += dgam.x;
+            ds.y += dgam.y;
+          }
 #pragma unroll
-      for (int u = 0; u < 16; ++u) w[u] = e * gv[u];
+          for (int o = 1; o < 32; o <<= 1) {  // suffix sum within the warp
+            const float ux = __shfl_down_sync(0xffffffffu, ds.x, o);
+            const float uy = __shfl_down_sync(0xffffffffu, ds.y, o);
+            if (lane + o < 32) {
+              ds.x += ux;
+              ds.y += uy;
+            }
+          }
+          if (tid == 32) m.sfx = ds;  // sum over positions 32..63
+        }
+        workers_sync();
+        if (tid < 64) {
+          float2 da = ds;
+          if (tid < 32) {
+            da.x += m.sfx.x;
+            da.y += m.sfx.y;
+          }
+          const int t = t0 + tid;
+          const float2 A = p.A[q.h];
+          float2 dap = make_float2(0.f, 0.f);
+          if (t < p.T) {
+            p.ddt[((long long)q.b * p.T + t) * p.H + q.h] = (da.x * A.x + da.y * A.y) * rec.dsp[tid];
+            dap = make_float2(da.x * rec.sp[tid], da.y * rec.sp[tid]);
+          }
 #pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
-        const uint32_t mh = stack8((uint32_t)(16 * pg + 8 * blk), 0u);
-        const uint32_t ml = stack8((uint32_t)(16 * pg + 8 * blk), 1u);
+          for (int o = 16; o > 0; o >>= 1) {
+            dap.x += __shfl_xor_sync(0xffffffffu, dap.x, o);
+            dap.y += __shfl_xor_sync(0xffffffffu, dap.y, o);
+          }
+          if (lane == 0) m.dap[tid >> 5] = dap;
+        }
+        workers_sync();
+        if (tid == 0)
+          p.dapart[(long long)q.bh * p.nc + q.z] =
+              make_float2(m.dap[0].x + m.dap[1].x, m.dap[0].y + m.dap[1].y);
+        warp_arrive(&m.bar_done, lane);
+        ++it;
+      }
+      if (next >= p.total) break;
+
+      // =================== ticket `next` starts ===================
+      active = true;
+      q = ticket_pos(next, BH, p.H, p.nc);
+      t0 = q.z * 64;
+      const uint32_t ph = it & 1u;
+      const ChunkRec& rec = m.rec[ph];
+      mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // B, C tiles, decay record
+
+      // ---- x, dy stacked over rows (K = p); e_l dy stacked over p (MN) once the previous
+      // ticket's dx / dB stores have read sDGK / sDYT / sDGM
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const uint32_t s = (uint32_t)(xs0 + 32 * hr);
+        split8_store(sb + OFF_X + swz(stack8(s, 0), tid & 7), sb + OFF_X + swz(stack8(s, 1), tid & 7),
+                     xv + 8 * hr);
+        split8_store(sb + OFF_DY + swz(stack8(s, 0), tid & 7),
+                     sb + OFF_DY + swz(stack8(s, 1), tid & 7), gv + 8 * hr);
+      }
+      if (it > 0) mbar_wait(&m.bar_stfree, ph ^ 1u, p.err, kErrMmaWait);
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const uint32_t s = (uint32_t)(xs0 + 32 * hr);
+        const float e = rec.el[s];
+        float w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) w[u] = e * gv[8 * hr + u];
+        const uint32_t mh = stack8((uint32_t)xp0, 0u), ml = stack8((uint32_t)xp0, 1u);
         split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(s, (mh & 63u) >> 3),
-                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w + 8 * blk);
+                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w);
       }
-    }
-
-    // ---- raw B, C tiles -> registers -> rotated, split, stacked operands (in place)
-    {
-      float4 rb4[4][2], rc4[4][2];
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int j = tid + kThreads * it;
-        const int l = j >> 4, q = j & 15;
-        const float* rB = reinterpret_cast<const float*>(smem + OFF_B) + l * 128 + 8 * q;
-        const float* rC = reinterpret_cast<const float*>(smem + OFF_C) + l * 128 + 8 * q;
-        rb4[it][0] = *reinterpret_cast<const float4*>(rB);
-        rb4[it][1] = *reinterpret_cast<const float4*>(rB + 4);
-        rc4[it][0] = *reinterpret_cast<const float4*>(rC);
-        rc4[it][1] = *reinterpret_cast<const float4*>(rC + 4);
-      }
-      __syncthreads();
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int j = tid + kThreads * it;
-        const int l = j >> 4, q = j & 15;
-        const float2 cs = m.rec.cis[l];
-        const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
-        const float cr[8] = {rc4[it][0].x, rc4[it][0].y, rc4[it][0].z, rc4[it][0].w,
-                             rc4[it][1].x, rc4[it][1].y, rc4[it][1].z, rc4[it][1].w};
-        const float br[8] = {rb4[it][0].x, rb4[it][0].y, rb4[it][0].z, rb4[it][0].w,
-                             rb4[it][1].x, rb4[it][1].y, rb4[it][1].z, rb4[it][1].w};
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          v[2 * u] = cr[2 * u] * cs.x - cr[2 * u + 1] * cs.y;
-          v[2 * u + 1] = cr[2 * u] * cs.y + cr[2 * u + 1] * cs.x;
+      // ---- raw tiles -> split operands, in place, 16 lanes per row: C' = C cis(theta_l) and
+      // conj(B') = conj(B conj(cis(theta_s))) stacked (then batch 1 may start), conj(H_z) hi | lo
+#pragma unroll 1
+      for (int tile = 0; tile < 3; ++tile) {
+        if (tile == 2) {
+          warp_arrive(&m.bar_ops1, lane);
+          mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
         }
-        split8_store(sb + OFF_C + ka * 16384u + swz(stack8(l, 0), ch),
-                     sb + OFF_C + ka * 16384u + swz(stack8(l, 1), ch), v);
+        const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_B : OFF_H);
+        const bool stacked = tile < 2;
+        const float sg = tile == 0 ? 1.f : -1.f;
+        float4 r4[4][2];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          v[2 * u] = br[2 * u] * cs.x + br[2 * u + 1] * cs.y;
-          v[2 * u + 1] = br[2 * u] * cs.y - br[2 * u + 1] * cs.x;
+        for (int i = 0; i < 4; ++i) {
+          const int j = tid + kWorkers * i;
+          const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
+          r4[i][0] = *reinterpret_cast<const float4*>(src);
+          r4[i][1] = *reinterpret_cast<const float4*>(src + 4);
         }
-        split8_store(sb + OFF_B + ka * 16384u + swz(stack8(l, 0), ch),
-                     sb + OFF_B + ka * 16384u + swz(stack8(l, 1), ch), v);
-      }
-    }
-    fence_proxy_async_smem();
-    __syncthreads();
-
-    // ---- batch 1: G = C'x B'x^T, dM = dy x^T, Q^T = (e dy)^T C'x
-    if (tid == 0) {
-      tc_fence_after_sync();
-      const uint32_t id64 = idesc_bf16(128, 64, 0, 0);
+        workers_sync();
 #pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
+        for (int i = 0; i < 4; ++i) {
+          const int j = tid + kWorkers * i;
+          const uint32_t l = (uint32_t)j >> 4, qq = (uint32_t)j & 15u;
+          const float2 cs = stacked ? rec.cis[l] : make_float2(1.f, 0.f);
+          const float rv[8] = {r4[i][0].x, r4[i][0].y, r4[i][0].z, r4[i][0].w,
+                               r4[i][1].x, r4[i][1].y, r4[i][1].z, r4[i][1].w};
+          float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t ko = (j >> 2) * 16384u + (j & 3) * 32u;
-          mma_bf16_ss(tmem + COL_G, sdesc(sb + OFF_C + ko, 16, 1024),
-                      sdesc(sb + OFF_B + ko + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
+          for (int u = 0; u < 4; ++u) {
+            v[2 * u] = rv[2 * u] * cs.x - sg * (rv[2 * u + 1] * cs.y);
+            v[2 * u + 1] = rv[2 * u] * cs.y + sg * (rv[2 * u + 1] * cs.x);
+          }
+          const uint32_t hi = stacked ? sb + base + (qq >> 3) * 16384u + swz(stack8(l, 0), qq & 7u)
+                                      : sb + base + (qq >> 3) * 8192u + swz(l, qq & 7u);
+          split8_store(hi, hi + (stacked ? 1024u : 16384u), v);
         }
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_DM, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
-                      sdesc(sb + OFF_X + j * 32u + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
-      const uint32_t idq = idesc_bf16(128, 128, 1, 1);
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_Q, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
-                      sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idq, (hp | j) != 0);
-      mma_commit(&m.bar1);
-    }
+      }
 
-    // ---- H_z (fp32 in sH) -> conj(H_z) split in place; dS_z from the next chunk; dS' -> sDS
-    const int kb = 64 * wg + 32 * part;
-    {
-      float hz[32];
-      const float* hrow = reinterpret_cast<const float*>(smem + OFF_H) + r * 128 + kb;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = reinterpret_cast<const float4*>(hrow)[i];
-        hz[4 * i] = v.x;
-        hz[4 * i + 1] = -v.y;
-        hz[4 * i + 2] = v.z;
-        hz[4 * i + 3] = -v.w;
-      }
-      __syncthreads();
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj)
-        split8_store(sb + OFF_H + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
-                     sb + OFF_H + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
-                     hz + 8 * jj);
-    }
-    float dsz[32];
-    if (z < p.nc - 1) {
-      if (tid == 0) {
-        const uint32_t* f = p.flags + (long long)bh * p.nc + z;
-        uint32_t i = 0;
-        for (; i < kSpinLimit; ++i) {
-          if (ld_acquire_gpu(f) != 0u) break;
-          __nanosleep(128);
-        }
-        if (i == kSpinLimit) atomicOr(p.err, kErrFlagWait);
-        m.dgam = __ldcg(p.dgring + (long long)bh * 4 + (z & 3));
-      }
-      __syncthreads();
-      const float* drow = p.ring + (((long long)bh * 4 + (z & 3)) * 64 + r) * 128 + kb;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(drow) + i);
-        dsz[4 * i] = v.x;
-        dsz[4 * i + 1] = v.y;
-        dsz[4 * i + 2] = v.z;
-        dsz[4 * i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < 32; ++c) dsz[c] = 0.f;
-      if (tid == 0) m.dgam = make_float2(0.f, 0.f);
-    }
-    {
-      // dS'x = interleaved (Re, -Im) of conj(cis(theta_Gamma)) dS_z
-      const float2 ct = m.rec.ct;
-      float w[32];
-#pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        const float re = dsz[c] * ct.x + dsz[c + 1] * ct.y;
-        const float im = dsz[c + 1] * ct.x - dsz[c] * ct.y;
-        w[c] = re;
-        w[c + 1] = -im;
-      }
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj)
-        split8_store(sb + OFF_DS + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
-                     sb + OFF_DS + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
-                     w + 8 * jj);
-    }
-
-    // ---- epilogue 1: Mr, dG' (two forms)
-    mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
-    tc_fence_after_sync();
-    {
-      float gs[16], ms[16];
-      ld_exch16(tmem + lane_off + COL_G + 32u * wg, part, gs);
-      ld_exch16(tmem + lane_off + COL_DM + 32u * wg, part, ms);
-      const int s0 = 32 * wg + 16 * part;
-      const float rl = m.rec.rho[r];
-      float mrv[16], dgv[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int s = s0 + c;
-        const float L = (s <= r) ? expf(rl - m.rec.rho[s]) : 0.f;
-        mrv[c] = L * gs[c];
-        dgv[c] = L * ms[c];
-      }
-#pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
-        const uint32_t mh = stack8((uint32_t)(s0 + 8 * blk), 0u);
-        const uint32_t ml = stack8((uint32_t)(s0 + 8 * blk), 1u);
-        split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
-                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), mrv + 8 * blk);
-        split8_store(sb + OFF_DGM + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
-                     sb + OFF_DGM + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), dgv + 8 * blk);
-        split8_store(sb + OFF_DGK + swz(stack8(r, 0), (s0 >> 3) + blk),
-                     sb + OFF_DGK + swz(stack8(r, 1), (s0 >> 3) + blk), dgv + 8 * blk);
-      }
-    }
-    // ---- state-gradient carry: dS_{z-1} = Q + conj(e^Gamma) dS_z, published for chunk z-1
-    {
-      float q[32];
-      ld_exch32(tmem + lane_off + COL_Q + 64u * wg, part, q);
-      float2 dg = make_float2(0.f, 0.f);
-      if (z > 0) {
-        const float2 g = m.rec.g;
-        float* drow = p.ring + (((long long)bh * 4 + ((z - 1) & 3)) * 64 + r) * 128 + kb;
+      // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
+      mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
+      float dsz[32];
+      dgam = make_float2(0.f, 0.f);
+      if (q.z < p.nc - 1) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float o[4];
+          const float4 v = ld_shared_f4(sb + OFF_DS + (uint32_t)(i * kWorkers + tid) * 16u);
+          dsz[4 * i] = v.x;
+          dsz[4 * i + 1] = v.y;
+          dsz[4 * i + 2] = v.z;
+          dsz[4 * i + 3] = v.w;
+        }
+        dgam = make_float2(m.dgam.x, m.dgam.y);
+      } else {
 #pragma unroll
-          for (int u = 0; u < 4; u += 2) {
-            const int c = 4 * i + u;
-            const float qr = q[c], qi = -q[c + 1];
-            o[u] = qr + g.x * dsz[c] + g.y * dsz[c + 1];
-            o[u + 1] = qi + g.x * dsz[c + 1] - g.y * dsz[c];
-          }
-          __stcg(reinterpret_cast<float4*>(drow) + i, make_float4(o[0], o[1], o[2], o[3]));
-          // <dS_{z-1}, H_z> for chunk z-1's decay gradient; sH holds conj(H_z) as hi + lo
-          const uint32_t hoff = (uint32_t)wg * 8192u + swz(r, 4 * part + (i >> 1));
-          const uint4 hh = ld_shared_u4(sb + OFF_H + hoff), hl = ld_shared_u4(sb + OFF_H + 16384u + hoff);
-          const float2 h0 = unsplit2((i & 1) ? hh.z : hh.x, (i & 1) ? hl.z : hl.x);
-          const float2 h1 = unsplit2((i & 1) ? hh.w : hh.y, (i & 1) ? hl.w : hl.y);
-          dg.x += o[0] * h0.x - o[1] * h0.y + o[2] * h1.x - o[3] * h1.y;
-          dg.y += o[0] * h0.y + o[1] * h0.x + o[2] * h1.y + o[3] * h1.x;
+        for (int c = 0; c < 32; ++c) dsz[c] = 0.f;
+      }
+      workers_sync();
+      {
+        const float2 ct = rec.ct;
+        float w[32];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {  // (Re, -Im) of conj(cis(theta_Gamma)) dS_z
+          w[c] = dsz[c] * ct.x + dsz[c + 1] * ct.y;
+          w[c + 1] = -(dsz[c + 1] * ct.x - dsz[c] * ct.y);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          split8_store(sb + OFF_DS + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                       sb + OFF_DS + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
+                       w + 8 * jj);
+      }
+
+      // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
+      mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
+      tc_fence_after_sync();
+      {
+        float gs[16], ms[16];
+        ld_exch16(tmem + lane_off + COL_G + 32u * wg, part, gs);
+        ld_exch16(tmem + lane_off + COL_DM + 32u * wg, part, ms);
+        const int s0 = 32 * wg + 16 * part;
+        const float rl = rec.rho[r];
+        float mrv[16], dgv[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int s = s0 + c;
+          const float L = (s <= r) ? expf(rl - rec.rho[s]) : 0.f;
+          mrv[c] = L * gs[c];
+          dgv[c] = L * ms[c];
+        }
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+          const uint32_t mh = stack8((uint32_t)(s0 + 8 * blk), 0u);
+          const uint32_t ml = stack8((uint32_t)(s0 + 8 * blk), 1u);
+          split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
+                       sb + OFF_DYT + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), mrv + 8 * blk);
+          split8_store(sb + OFF_DGM + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
+                       sb + OFF_DGM + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), dgv + 8 * blk);
+          split8_store(sb + OFF_DGK + swz(stack8(r, 0), (s0 >> 3) + blk),
+                       sb + OFF_DGK + swz(stack8(r, 1), (s0 >> 3) + blk), dgv + 8 * blk);
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
-        dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
-      }
-      if (lane == 0) m.dgp[warp] = dg;
-    }
-    fence_proxy_async_smem();
-    tc_fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      // the barrier orders every thread's ring stores before this gpu-scope release
-      if (z > 0) {
+      // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major), <dS_{z-1}, H_z>
+      {
+        float qv[32];
+        ld_exch32(tmem + lane_off + COL_Q + 64u * wg, part, qv);
         float2 dg = make_float2(0.f, 0.f);
+        if (q.z > 0) {
+          const float2 g = rec.g;
+          float4* slot = reinterpret_cast<float4*>(p.ring + ((long long)q.bh * 4 + ((q.z - 1) & 3)) * 64 * 128);
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          dg.x += m.dgp[w].x;
-          dg.y += m.dgp[w].y;
+          for (int i = 0; i < 8; ++i) {
+            float o[4];
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+              const int c = 4 * i + u;
+              o[u] = qv[c] + g.x * dsz[c] + g.y * dsz[c + 1];
+              o[u + 1] = -qv[c + 1] + g.x * dsz[c + 1] - g.y * dsz[c];
+            }
+            __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
+            const uint32_t hoff = (uint32_t)wg * 8192u + swz(r, 4 * part + (i >> 1));
+            const uint4 hh = ld_shared_u4(sb + OFF_H + hoff);
+            const uint4 hl = ld_shared_u4(sb + OFF_H + 16384u + hoff);
+            const float2 h0 = unsplit2((i & 1) ? hh.z : hh.x, (i & 1) ? hl.z : hl.x);
+            const float2 h1 = unsplit2((i & 1) ? hh.w : hh.y, (i & 1) ? hl.w : hl.y);
+            dg.x += o[0] * h0.x - o[1] * h0.y + o[2] * h1.x - o[3] * h1.y;
+            dg.y += o[0] * h0.y + o[1] * h0.x + o[2] * h1.y + o[3] * h1.x;
+          }
         }
-        __stcg(p.dgring + (long long)bh * 4 + ((z - 1) & 3), dg);
-        st_release_gpu(p.flags + (long long)bh * p.nc + z - 1, 1u);
-      }
-      const int nn = (int)atomicAdd(p.counter, 1u);  // result is stored after the MMA issue
-      tc_fence_after_sync();
-      // batch 2: dCa = dG' B'x (MN), dCb = dy conj(H)
-      const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
 #pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_DCA, sdesc(sb + OFF_DGK + j * 32u, 16, 1024),
-                      sdesc(sb + OFF_B + j * 4096u + hp * 1024u, 16384, 2048), id128,
-                      (hp | j) != 0);
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_DCB, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
-                      sdesc(sb + OFF_H + hp * 16384u + j * 2048u, 8192, 1024), id128,
-                      (hp | j) != 0);
-      mma_commit(&m.bar2);
-      // batch 3: dXa = Mr^T dy, dXb = B'x dS'x, dBa = dG'^T C'x
-      const uint32_t idxa = idesc_bf16(128, 64, 1, 1);
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_DXA, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
-                      sdesc(sb + OFF_DY + j * 4096u + hp * 1024u, 8192, 2048), idxa,
-                      (hp | j) != 0);
-      const uint32_t idxb = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          mma_bf16_ss(tmem + COL_DXB,
-                      sdesc(sb + OFF_B + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
-                      sdesc(sb + OFF_DS + hp * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16,
-                            1024),
-                      idxb, (hp | j) != 0);
-      const uint32_t idba = idesc_bf16(128, 128, 1, 1);
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_DBA, sdesc(sb + OFF_DGM + j * 2048u, 8192, 1024),
-                      sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idba,
-                      (hp | j) != 0);
-      mma_commit(&m.bar3);
-      m.nxt = nn;
-    }
-    // prefetch the next ticket's x, dy, dt while the MMAs run
-    __syncthreads();
-    next = m.nxt;
-    if (next < p.total) prefetch_regs(next);
-
-    // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)); row sums dC' conj(C')
-    mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
-    tc_fence_after_sync();
-    {
-      float ca[32], cb[32];
-      ld_exch32(tmem + lane_off + COL_DCA + 64u * wg, part, ca);
-      ld_exch32(tmem + lane_off + COL_DCB + 64u * wg, part, cb);
-      const float e = m.rec.el[r];
-      const float2 cs = m.rec.cis[r];
-      float out[32];
-      float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const uint4 hi = ld_shared_u4(sb + OFF_C + (uint32_t)wg * 16384u + swz(stack8(r, 0), 4 * part + jj));
-        const uint4 lo = ld_shared_u4(sb + OFF_C + (uint32_t)wg * 16384u + swz(stack8(r, 1), 4 * part + jj));
-        const float2 c0 = unsplit2(hi.x, lo.x), c1 = unsplit2(hi.y, lo.y);
-        const float2 c2 = unsplit2(hi.z, lo.z), c3 = unsplit2(hi.w, lo.w);
-        const float2 cv[4] = {c0, c1, c2, c3};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = 8 * jj + 2 * u;
-          const float2 d = make_float2(ca[c] + e * cb[c], ca[c + 1] + e * cb[c + 1]);  // dC'
-          acc.x += d.x * cv[u].x + d.y * cv[u].y;  // dC' conj(C')
-          acc.y += d.y * cv[u].x - d.x * cv[u].y;
-          const float2 o = cmul2(d, make_float2(cs.x, -cs.y));
-          out[c] = o.x;
-          out[c + 1] = o.y;
+        for (int o = 16; o > 0; o >>= 1) {
+          dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
+          dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
         }
+        if (lane == 0) m.dgp[warp] = dg;
       }
-      m.rc[2 * wg + part][r] = acc;
-      const int t = t0 + r;
-      if (t < p.T) {
-        float* dst = reinterpret_cast<float*>(p.dC + (((long long)b * p.T + t) * p.H + h) * 64) + kb;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          reinterpret_cast<float4*>(dst)[i] =
-              make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
-      }
+      warp_arrive(&m.bar_ops2, lane);
+      // the next ticket: its x and dy are prefetched at the top of the loop, during the epilogues
+      mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
+      next = m.tick[(it + 1) & 1];
     }
-    tc_fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {  // dBb = x dS'x^T (MN), into the columns dCa used
-      tc_fence_after_sync();
-      const uint32_t idbb = idesc_bf16(128, 128, 0, 1);
-#pragma unroll
-      for (int hp = 0; hp < 2; ++hp)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_DBB, sdesc(sb + OFF_X + j * 32u, 16, 1024),
-                      sdesc(sb + OFF_DS + hp * 16384u + j * 2048u, 8192, 1024), idbb,
-                      (hp | j) != 0);
-      mma_commit(&m.bar4);
-    }
-
-    // ---- epilogue 3: dx = dXa + dec_s dXb
-    mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
-    tc_fence_after_sync();
-    {
-      float xa[16], xb[16];
-      ld_exch16(tmem + lane_off + COL_DXA + 32u * wg, part, xa);
-      ld_exch16(tmem + lane_off + COL_DXB + 32u * wg, part, xb);
-      const float d = m.rec.dec[r];
-      const int t = t0 + r;
-      if (t < p.T) {
-        float* dst = p.dx + (((long long)b * p.T + t) * p.H + h) * 64 + 32 * wg + 16 * part;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          reinterpret_cast<float4*>(dst)[i] =
-              make_float4(xa[4 * i] + d * xb[4 * i], xa[4 * i + 1] + d * xb[4 * i + 1],
-                          xa[4 * i + 2] + d * xb[4 * i + 2], xa[4 * i + 3] + d * xb[4 * i + 3]);
-      }
-    }
-    // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s); row sums dB' conj(B')
-    mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
-    tc_fence_after_sync();
-    {
-      float ba[32], bbv[32];
-      ld_exch32(tmem + lane_off + COL_DBA + 64u * wg, part, ba);
-      ld_exch32(tmem + lane_off + COL_DBB + 64u * wg, part, bbv);
-      const float d = m.rec.dec[r];
-      const float2 cs = m.rec.cis[r];
-      float out[32];
-      float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const uint4 hi = ld_shared_u4(sb + OFF_B + (uint32_t)wg * 16384u + swz(stack8(r, 0), 4 * part + jj));
-        const uint4 lo = ld_shared_u4(sb + OFF_B + (uint32_t)wg * 16384u + swz(stack8(r, 1), 4 * part + jj));
-        const float2 b0 = unsplit2(hi.x, lo.x), b1 = unsplit2(hi.y, lo.y);
-        const float2 b2 = unsplit2(hi.z, lo.z), b3 = unsplit2(hi.w, lo.w);
-        const float2 bv[4] = {b0, b1, b2, b3};  // conj(B') as stored
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = 8 * jj + 2 * u;
-          const float2 dbp = make_float2(ba[c] + d * bbv[c], -(ba[c + 1] + d * bbv[c + 1]));
-          acc.x += dbp.x * bv[u].x - dbp.y * bv[u].y;  // dB' conj(B')
-          acc.y += dbp.x * bv[u].y + dbp.y * bv[u].x;
-          const float2 o = cmul2(dbp, cs);
-          out[c] = o.x;
-          out[c + 1] = o.y;
-        }
-      }
-      m.rb[2 * wg + part][r] = acc;
-      const int t = t0 + r;
-      if (t < p.T) {
-        float* dst = reinterpret_cast<float*>(p.dB + (((long long)b * p.T + t) * p.H + h) * 64) + kb;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          reinterpret_cast<float4*>(dst)[i] =
-              make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before_sync();
-    __syncthreads();
-
-    // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial
-    float2 ds = make_float2(0.f, 0.f);
-    if (tid < 64) {
-      const int l = tid;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ds.x += m.rc[j][l].x - m.rb[j][l].x;
-        ds.y += m.rc[j][l].y - m.rb[j][l].y;
-      }
-      if (l == 63) {
-        ds.x += m.dgam.x;
-        ds.y += m.dgam.y;
-      }
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {  // suffix sum within the warp
-        const float ux = __shfl_down_sync(0xffffffffu, ds.x, o);
-        const float uy = __shfl_down_sync(0xffffffffu, ds.y, o);
-        if (lane + o < 32) {
-          ds.x += ux;
-          ds.y += uy;
-        }
-      }
-      if (tid == 32) m.sfx = ds;  // sum over positions 32..63
-    }
-    __syncthreads();
-    if (tid < 64) {
-      float2 da = ds;
-      if (tid < 32) {
-        da.x += m.sfx.x;
-        da.y += m.sfx.y;
-      }
-      const int t = t0 + tid;
-      const float2 A = p.A[h];
-      float2 dap = make_float2(0.f, 0.f);
-      if (t < p.T) {
-        p.ddt[((long long)b * p.T + t) * p.H + h] = (da.x * A.x + da.y * A.y) * m.rec.dsp[tid];
-        dap = make_float2(da.x * m.rec.sp[tid], da.y * m.rec.sp[tid]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        dap.x += __shfl_xor_sync(0xffffffffu, dap.x, o);
-        dap.y += __shfl_xor_sync(0xffffffffu, dap.y, o);
-      }
-      if (lane == 0) m.dap[tid >> 5] = dap;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      p.dapart[(long long)bh * p.nc + z] =
-          make_float2(m.dap[0].x + m.dap[1].x, m.dap[0].y + m.dap[1].y);
-    }
-    ticket = next;
-    ++iter;
   }
+  tc_fence_before_sync();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
@@ -734,7 +864,7 @@ BwdLayout bwd_layout(const Problem& p) {
   L.flags = 256;
   L.ring = al(L.flags + 4 * bh * nc);
   L.dgring = al(L.ring + bh * 4 * 64 * 128 * sizeof(float));
-  L.dapart = al(L.dgring + bh * 4 * sizeof(float2));
+  L.dapart = al(L.dgring + bh * 4 * sizeof(float4));
   L.total = al(L.dapart + bh * nc * sizeof(float2));
   return L;
 }
@@ -768,21 +898,26 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
                   ? 1
                   : 0;
   bp.A = p.A;
+  bp.Bm = p.Bm;
+  bp.Cm = p.Cm;
+  for (int i = 0; i < 4; ++i) {
+    bp.bs[i] = p.bs[i];
+    bp.cs[i] = p.cs[i];
+  }
   bp.states = static_cast<const float*>(states);
   bp.recs = reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
-  bp.dx = dx;
-  bp.dB = dB;
-  bp.dC = dC;
   bp.ddt = ddt;
   char* base = static_cast<char*>(ws);
   bp.err = reinterpret_cast<uint32_t*>(base);
   bp.counter = reinterpret_cast<uint32_t*>(base) + 1;
   bp.flags = reinterpret_cast<uint32_t*>(base + L.flags);
   bp.ring = reinterpret_cast<float*>(base + L.ring);
-  bp.dgring = reinterpret_cast<float2*>(base + L.dgring);
+  bp.dgring = reinterpret_cast<float4*>(base + L.dgring);
   bp.dapart = reinterpret_cast<float2*>(base + L.dapart);
-  CUtensorMap tmB, tmC;
-  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
+  CUtensorMap tmB, tmC, tmDX, tmDB, tmDC;
+  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs) ||
+      !encode_out_tensor_map(&tmDX, dx, p, 64) || !encode_out_tensor_map(&tmDB, dB, p, 128) ||
+      !encode_out_tensor_map(&tmDC, dC, p, 128))
     return M3SSD_ERR_LAUNCH;
   if (cudaMemsetAsync(ws, 0, L.ring, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   int dev = 0, sms = 0;
@@ -792,7 +927,7 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
                            (int)kSmemBytes) != cudaSuccess)
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
-  k_bwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, bp);
+  k_bwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmDX, tmDB, tmDC, bp);
   k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, dA);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }

@@ -57,14 +57,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete. Gives up after kSpinLimit polls,
 // records `code` in *err and returns false (the kernel then finishes with garbage results
 // instead of hanging the GPU).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
-                                          uint32_t code) {
+// The polling loop is out of line: inlined at every wait site, the compiler's peeling of its first
+// iterations made the persistent kernels several times larger than the instruction cache.
+static __device__ __noinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                       uint32_t code) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 32) __nanosleep(64);
   }
   atomicOr(err, code);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                          uint32_t code) {
+  return mbar_try_wait(bar, parity) || mbar_spin(bar, parity, err, code);
 }
 
 // ----------------------------------------------------------------------------- proxies, fences
@@ -87,6 +93,26 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+// tiled TMA store from shared memory (bulk-group completion); out-of-range elements are skipped
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// the shared-memory sources of all committed bulk groups have been read
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// all committed bulk groups have completed (their global writes are done)
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -261,6 +287,13 @@ __device__ __forceinline__ float2 unsplit2(uint32_t hi, uint32_t lo) {
   const float l0 = __uint_as_float(lo << 16), l1 = __uint_as_float(lo & 0xFFFF0000u);
   return make_float2(h0 + l0, h1 + l1);
 }
+// the value a split-bf16 operand element represents (hi + lo of split8), computed from fp32
+__device__ __forceinline__ float2 split_round2(float2 v) {
+  const __nv_bfloat162 hp = __floats2bfloat162_rn(v.x, v.y);
+  const float2 hf = __bfloat1622float2(hp);
+  const float2 lf = __bfloat1622float2(__floats2bfloat162_rn(v.x - hf.x, v.y - hf.y));
+  return make_float2(hf.x + lf.x, hf.y + lf.y);
+}
 }  // namespace tc
 }  // namespace m3ssd
 
@@ -291,5 +324,22 @@ struct ChunkRec {
   float2 pad[2];
 };
 static_assert(sizeof(ChunkRec) % 16 == 0, "bulk copy granularity");
+}  // namespace tc
+}  // namespace m3ssd
+
+namespace m3ssd {
+namespace tc {
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// orders this thread's generic-proxy view of global memory with its async-proxy (bulk copy)
+// accesses: after acquiring data another CTA wrote with plain stores, before bulk-copying it
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// barrier among the first `count` threads of the CTA (ids 1..15; 0 is __syncthreads)
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 }  // namespace tc
 }  // namespace m3ssd

@@ -489,6 +489,21 @@ bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
   return encode_bc_map_impl(map, ptr, p, st);
 }
 
+bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int row_floats) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (!encode || (reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
+  const cuuint64_t rf = (cuuint64_t)row_floats;
+  cuuint64_t dims[4] = {rf, (cuuint64_t)p.H, (cuuint64_t)p.T, (cuuint64_t)p.Bsz};
+  cuuint64_t strides[3] = {rf * 4u, rf * 4u * (cuuint64_t)p.H,
+                           rf * 4u * (cuuint64_t)p.H * (cuuint64_t)p.T};
+  cuuint32_t box[4] = {32u, 1u, 64u, 1u};
+  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  const CUresult rc = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return rc == CUDA_SUCCESS;
+}
+
 bool fwd_supported(const Problem& p) {
   if (p.D != 64 || p.N != 64 || p.x_complex) return false;
   if (!bc_tma_ok(p.Bm, p.bs) || !bc_tma_ok(p.Cm, p.cs)) return false;

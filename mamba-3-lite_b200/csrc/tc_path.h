@@ -33,6 +33,10 @@ int run_chunk_prep(const Problem& p, ChunkRec* out, cudaStream_t st);
 // 64 time steps x 2N floats of one head (zero fill past T)
 bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
                           const long long st[4]);
+// 4D map over a contiguous (B, T, H, row_floats) fp32 output for TMA stores of 64-row tiles in
+// 32-float (128-byte) column segments, 128-byte swizzled in shared memory. False if the pointer
+// is not 16-byte aligned.
+bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int row_floats);
 
 // head_dim = state_dim = 64, real x, B/C with contiguous state dim and 16-byte aligned strides
 bool fwd_supported(const Problem& p);
