@@ -47,7 +47,7 @@ constexpr uint32_t OFF_H = 180224;   // H_z (fp32, lands by bulk copy), then con
 constexpr uint32_t OFF_MISC = 212992;
 constexpr uint32_t kMiscBytes = 8192;
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBytes + 1024;
-constexpr uint32_t kLoadBytes = 2u * 64u * 128u * 4u + (uint32_t)sizeof(ChunkRec);
+constexpr uint32_t kLoadBytes = 64u * 128u * 4u + (uint32_t)sizeof(ChunkRec);  // C tile + record
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: batch 1, batch 2, batch 3 (reusing batch-1 columns), dBb (reusing dCa)
 constexpr uint32_t COL_G = 0, COL_DM = 64, COL_Q = 128, COL_DCA = 256, COL_DCB = 384;
@@ -55,14 +55,15 @@ constexpr uint32_t COL_DXA = 0, COL_DXB = 64, COL_DBA = 128, COL_DBB = 256;
 
 struct Misc {
   ChunkRec rec[2];  // decay records of the current and the next ticket
-  // control -> workers: B / C / record landed, H_z landed, dS landed, ticket published, MMA
-  // commits 1..4, and the staging buffers of the previous ticket's dx / dB stores read (stfree)
-  uint64_t bar_tma, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
+  // control -> workers: C tile + record landed, B tile landed, H_z landed, dS landed, ticket
+  // published, MMA commits 1..4, and the staging buffers of the previous ticket's dx / dB stores
+  // read (stfree)
+  uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
   // workers -> control (one arrival per worker warp)
-  uint64_t bar_ops1, bar_ops2, bar_colfree, bar_dc, bar_hfree, bar_dx, bar_db, bar_done;
+  uint64_t bar_ops1, bar_ops2, bar_colfree, bar_dc, bar_dx, bar_db, bar_done;
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
-  float2 rc[64];    // sum_n dC'_{ln} conj(C'_{ln})
-  float2 rb[64];    // sum_n dB'_{sn} conj(B'_{sn})
+  float2 rc[2][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the two 32-state halves
+  float2 rb[2][64];  // sum_n dB'_{sn} conj(B'_{sn})
   float2 dgp[8];    // per-warp partials of <dS_{z-1}, H_z>
   float2 dap[2];
   float2 sfx;
@@ -111,14 +112,19 @@ __device__ __forceinline__ TicketPos ticket_pos(int tk, int BH, int H, int nc) {
 
 // ---------------------------------------------------------------- control-warp helpers
 // (out of line: each runs once per ticket, and the kernel must stay small for the I-cache)
-static __device__ __noinline__ void ctl_load_bc(const CUtensorMap* tmB, const CUtensorMap* tmC,
-                                                uint8_t* smem, Misc* m, const ChunkRec* recs,
-                                                int nc, TicketPos q, int slot) {
+// C tile and decay record (bar_tma), once the epilogue of dC has read sC; B tile (bar_tmb) once the
+// epilogue of dB has read sB
+static __device__ __noinline__ void ctl_load_c(const CUtensorMap* tmC, uint8_t* smem, Misc* m,
+                                               const ChunkRec* recs, int nc, TicketPos q, int slot) {
   mbar_arrive_expect_tx(&m->bar_tma, kLoadBytes);
-  tma_load_4d(smem + OFF_B, tmB, &m->bar_tma, 0, q.h, q.z * 64, q.b);
   tma_load_4d(smem + OFF_C, tmC, &m->bar_tma, 0, q.h, q.z * 64, q.b);
   bulk_load(&m->rec[slot], recs + (long long)q.bh * nc + q.z, (uint32_t)sizeof(ChunkRec),
             &m->bar_tma);
+}
+static __device__ __noinline__ void ctl_load_b(const CUtensorMap* tmB, uint8_t* smem, Misc* m,
+                                               TicketPos q) {
+  mbar_arrive_expect_tx(&m->bar_tmb, 64u * 128u * 4u);
+  tma_load_4d(smem + OFF_B, tmB, &m->bar_tmb, 0, q.h, q.z * 64, q.b);
 }
 static __device__ __noinline__ void ctl_load_h(uint8_t* smem, Misc* m, const float* states, int nc,
                                                TicketPos q) {
@@ -207,35 +213,6 @@ __device__ __forceinline__ void ld_exch32(uint32_t taddr, int part, float (&out)
   }
 }
 
-// Sum over the warp of 16 per-lane values. Lane L ends with the total of value
-// 8 bit4(L) + 4 bit3(L) + 2 bit2(L) + bit1(L) (16 shuffles instead of 80).
-__device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool up = (lane & 16) != 0;
-    const float send = up ? v[i] : v[8 + i];
-    v[i] = (up ? v[8 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool up = (lane & 8) != 0;
-    const float send = up ? v[i] : v[4 + i];
-    v[i] = (up ? v[4 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const bool up = (lane & 4) != 0;
-    const float send = up ? v[i] : v[2 + i];
-    v[i] = (up ? v[2 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  {
-    const bool up = (lane & 2) != 0;
-    const float send = up ? v[0] : v[1];
-    v[0] = (up ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
-}
-
 __device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
   float w[8];
 #pragma unroll
@@ -268,55 +245,49 @@ __device__ __forceinline__ uint32_t stage_seg(uint32_t seg01, uint32_t seg23, ui
 }
 
 // ---------------------------------------------------------------- worker helpers (out of line)
-// Epilogue of dC and dB: v = (a + w b) conj(rot) over this thread's 32 state columns (accumulator
-// blocks at ta, tb), conjugated if conj_out, into the staging tile. dC: w = e_l, rot = cis(theta_l);
-// dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out.
-static __device__ __noinline__ void combine_stage(uint32_t ta, uint32_t tb, int part, float w,
-                                                  float2 rot, bool conj_out, uint32_t seg,
-                                                  uint32_t row, uint64_t* colfree, int lane) {
+// Epilogue of dC and dB over this thread's 32 state columns of row `row` (accumulator blocks at
+// ta, tb): v = a + w b, staged as v conj(rot) (conjugated if conj_out), and the partial row sum
+// sum v conj(X) with X the split-bf16 operand row as the tensor core saw it (hi part in stacked row
+// xrow of the k-atom at xop, lo part 8 rows further). dC: w = e_l, rot = cis(theta_l), X = C', sum = dC' conj(C').
+// dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out, X = conj(B'),
+// sum = conj(dB' conj(B')).
+static __device__ __noinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int part, float w,
+                                                    float2 rot, bool conj_out, uint32_t seg,
+                                                    uint32_t row, uint32_t xop, uint32_t xrow,
+                                                    uint64_t* colfree, int lane) {
   float a[32], bb[32];
   ld_exch32(ta, part, a);
   ld_exch32(tb, part, bb);
   if (colfree != nullptr) warp_arrive(colfree, lane);
   const float2 nr = make_float2(rot.x, -rot.y);
   const float cj = conj_out ? -1.f : 1.f;
+  float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float2 v0 = cmul2(make_float2(a[4 * i] + w * bb[4 * i], a[4 * i + 1] + w * bb[4 * i + 1]), nr);
-    const float2 v1 =
-        cmul2(make_float2(a[4 * i + 2] + w * bb[4 * i + 2], a[4 * i + 3] + w * bb[4 * i + 3]), nr);
-    st_shared_v4(stage_addr(seg, row, (uint32_t)i),
-                 make_uint4(__float_as_uint(v0.x), __float_as_uint(cj * v0.y),
-                            __float_as_uint(v1.x), __float_as_uint(cj * v1.y)));
+  for (int jj = 0; jj < 4; ++jj) {
+    const uint32_t xa = xop + swz(xrow, 4u * (uint32_t)part + (uint32_t)jj);
+    const uint4 hi = ld_shared_u4(xa);
+    const uint4 lo = ld_shared_u4(xa + 1024u);
+    const float2 xv[4] = {unsplit2(hi.x, lo.x), unsplit2(hi.y, lo.y), unsplit2(hi.z, lo.z),
+                          unsplit2(hi.w, lo.w)};
+    float o[8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = 8 * jj + 2 * u;
+      const float2 v = make_float2(a[c] + w * bb[c], a[c + 1] + w * bb[c + 1]);
+      acc.x += v.x * xv[u].x + v.y * xv[u].y;
+      acc.y += v.y * xv[u].x - v.x * xv[u].y;
+      const float2 r2 = cmul2(v, nr);
+      o[2 * u] = r2.x;
+      o[2 * u + 1] = cj * r2.y;
+    }
+    st_shared_v4(stage_addr(seg, row, 2u * jj),
+                 make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
+                            __float_as_uint(o[3])));
+    st_shared_v4(stage_addr(seg, row, 2u * jj + 1u),
+                 make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]),
+                            __float_as_uint(o[7])));
   }
-}
-// Row sums out[l] = sum_n (Y rot)_{ln} conj(round(X rot)_{ln}) for the warp's 8 rows l = row0 ..
-// row0+7 of a chunk: Y from the staging tile (dC or dB), X re-read from global memory (C or B,
-// coalesced: one 512-byte row per warp load), rounded to its split-bf16 value so the sum matches
-// the contractions. dC' conj(C'): rot = cis(theta_l); dB' conj(B'): rot = conj(cis(theta_s)).
-static __device__ __noinline__ void row_sums(const float4* Xg, long long base4, long long stride4,
-                                             int nvalid, uint32_t seg01, uint32_t seg23,
-                                             const float2* cis, bool conj_rot, int row0,
-                                             float* out, int lane) {
-  float4 xv[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    xv[k] = (k < nvalid) ? __ldcg(Xg + base4 + k * stride4 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-  const uint32_t seg = stage_seg(seg01, seg23, (uint32_t)(lane >> 3));
-  float acc[16];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float2 cs = cis[row0 + k];
-    const float2 rot = make_float2(cs.x, conj_rot ? -cs.y : cs.y);
-    const float4 dv = ld_shared_f4(stage_addr(seg, (uint32_t)(row0 + k), (uint32_t)(lane & 7)));
-    const float2 d0 = cmul2(make_float2(dv.x, dv.y), rot), d1 = cmul2(make_float2(dv.z, dv.w), rot);
-    const float2 c0 = split_round2(cmul2(make_float2(xv[k].x, xv[k].y), rot));
-    const float2 c1 = split_round2(cmul2(make_float2(xv[k].z, xv[k].w), rot));
-    acc[2 * k] = d0.x * c0.x + d0.y * c0.y + d1.x * c1.x + d1.y * c1.y;
-    acc[2 * k + 1] = d0.y * c0.x - d0.x * c0.y + d1.y * c1.x - d1.x * c1.y;
-  }
-  const float tot = warp_sum16(acc, lane);
-  if ((lane & 1) == 0) out[2 * row0 + (lane >> 1)] = tot;
+  return acc;
 }
 
 }  // namespace
@@ -334,14 +305,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int BH = p.Bsz * p.H;
 
   if (tid == 0) {
-    uint64_t* one[9] = {&m.bar_tma, &m.bar_h, &m.bar_ds, &m.bar_ctl, &m.bar1,
-                        &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
-    uint64_t* eight[8] = {&m.bar_ops1, &m.bar_ops2, &m.bar_colfree, &m.bar_dc,
-                          &m.bar_hfree, &m.bar_dx, &m.bar_db, &m.bar_done};
+    uint64_t* one[10] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds, &m.bar_ctl,
+                         &m.bar1,    &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
+    uint64_t* eight[7] = {&m.bar_ops1, &m.bar_ops2, &m.bar_colfree, &m.bar_dc,
+                          &m.bar_dx,   &m.bar_db,   &m.bar_done};
 #pragma unroll
-    for (int i = 0; i < 9; ++i) mbar_init(one[i], 1);
+    for (int i = 0; i < 10; ++i) mbar_init(one[i], 1);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mbar_init(eight[i], kWorkers / 32);
+    for (int i = 0; i < 7; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -366,7 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&m.bar_ctl);
       TicketPos qc = ticket_pos(cur, BH, p.H, p.nc);
       if (cur < p.total) {
-        ctl_load_bc(&tmB, &tmC, smem, &m, p.recs, p.nc, qc, 0);
+        ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qc, 0);
+        ctl_load_b(&tmB, smem, &m, qc);
         ctl_load_h(smem, &m, p.states, p.nc, qc);
         ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qc);
       }
@@ -467,13 +439,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                           (hp | j) != 0);
           mma_commit(&m.bar3);
         }
-        // the next ticket's B, C tiles as soon as batch 3 has read sB / sC; its record slot once
-        // the workers finished the ticket before this one
-        if (nxt < p.total) {
-          if (it > 0) mbar_wait(&m.bar_done, ph ^ 1u, p.err, kErrMmaWait);
-          mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
-          ctl_load_bc(&tmB, &tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1));
-        }
         // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them
         mbar_wait(&m.bar_colfree, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
@@ -488,20 +453,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                           (hp | j) != 0);
           mma_commit(&m.bar4);
         }
-        // dC from its staging tile in sH; then the next H_z into sH once the store and the
-        // workers' row-sum pass have read it
+        // dC from its staging tile in sH; the epilogue of dC has read sC, and once batch 3 has
+        // too, the next C tile and record (its slot: the workers finished the ticket before this
+        // one); the next H_z into sH once the store has read it
         mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc);
-        mbar_wait(&m.bar_hfree, ph, p.err, kErrMmaWait);
+        if (nxt < p.total) {
+          if (it > 0) mbar_wait(&m.bar_done, ph ^ 1u, p.err, kErrMmaWait);
+          mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
+          ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1));
+        }
         bulk_wait_read_all();
         if (nxt < p.total) ctl_load_h(smem, &m, p.states, p.nc, qn);
-        // dx from sDGK, dB from sDYT / sDGM, then the next ticket's dS once dBb has read sDS
+        // dx from sDGK, dB from sDYT / sDGM; the next B tile (the epilogue of dB has read sB) and
+        // the next dS (dBb has read sDS)
         mbar_wait(&m.bar_dx, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc);
         mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc);
         if (nxt < p.total) {
-          mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
+          ctl_load_b(&tmB, smem, &m, qn);
           ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn);
         }
         bulk_wait_read_all();
@@ -549,17 +520,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)) -> staging tile in sH
         mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
-        combine_stage(tmem + lane_off + COL_DCA + 64u * wg, tmem + lane_off + COL_DCB + 64u * wg,
-                      part, rec.el[r], rec.cis[r], false,
-                      stage_seg(sb + OFF_H, sb + OFF_H + 16384u, (uint32_t)(kb >> 5)), (uint32_t)r,
-                      &m.bar_colfree, lane);
+        {
+          float2 acc = combine_stage(
+              tmem + lane_off + COL_DCA + 64u * wg, tmem + lane_off + COL_DCB + 64u * wg, part,
+              rec.el[r], rec.cis[r], false,
+              stage_seg(sb + OFF_H, sb + OFF_H + 16384u, (uint32_t)(kb >> 5)), (uint32_t)r,
+              sb + OFF_C + (uint32_t)wg * 16384u, stack8((uint32_t)r, 0u), &m.bar_colfree, lane);
+          acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
+          acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
+          if (part == 0) m.rc[wg][r] = acc;
+        }
         warp_arrive(&m.bar_dc, lane);
-        workers_sync();
-        row_sums(reinterpret_cast<const float4*>(p.Cm),
-                 (q.b * p.cs[0] + (long long)(t0 + 8 * warp) * p.cs[1] + q.h * p.cs[2]) >> 1,
-                 p.cs[1] >> 1, p.T - (t0 + 8 * warp), sb + OFF_H, sb + OFF_H + 16384u, rec.cis,
-                 false, 8 * warp, reinterpret_cast<float*>(m.rc), lane);
-        warp_arrive(&m.bar_hfree, lane);
 
         // ---- epilogue 3: dx = dXa + dec_s dXb -> staging tile in sDGK
         mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
@@ -582,24 +553,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s) -> staging tiles in sDYT, sDGM
         mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
-        combine_stage(tmem + lane_off + COL_DBA + 64u * wg, tmem + lane_off + COL_DBB + 64u * wg,
-                      part, rec.dec[r], rec.cis[r], true,
-                      stage_seg(sb + OFF_DYT, sb + OFF_DGM, (uint32_t)(kb >> 5)), (uint32_t)r,
-                      nullptr, lane);
+        {
+          float2 acc = combine_stage(
+              tmem + lane_off + COL_DBA + 64u * wg, tmem + lane_off + COL_DBB + 64u * wg, part,
+              rec.dec[r], rec.cis[r], true,
+              stage_seg(sb + OFF_DYT, sb + OFF_DGM, (uint32_t)(kb >> 5)), (uint32_t)r,
+              sb + OFF_B + (uint32_t)wg * 16384u, stack8((uint32_t)r, 0u), nullptr, lane);
+          acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
+          acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
+          if (part == 0) m.rb[wg][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
+        }
         warp_arrive(&m.bar_db, lane);
-        workers_sync();
-        row_sums(reinterpret_cast<const float4*>(p.Bm),
-                 (q.b * p.bs[0] + (long long)(t0 + 8 * warp) * p.bs[1] + q.h * p.bs[2]) >> 1,
-                 p.bs[1] >> 1, p.T - (t0 + 8 * warp), sb + OFF_DYT, sb + OFF_DGM, rec.cis, true,
-                 8 * warp, reinterpret_cast<float*>(m.rb), lane);
         workers_sync();
 
         // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial
         float2 ds = make_float2(0.f, 0.f);
         if (tid < 64) {
           const int l = tid;
-          ds.x = m.rc[l].x - m.rb[l].x;
-          ds.y = m.rc[l].y - m.rb[l].y;
+          ds.x = m.rc[0][l].x + m.rc[1][l].x - m.rb[0][l].x - m.rb[1][l].x;
+          ds.y = m.rc[0][l].y + m.rc[1][l].y - m.rb[0][l].y - m.rb[1][l].y;
           if (l == 63) {
             ds.x += dgam.x;
             ds.y += dgam.y;
@@ -651,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       t0 = q.z * 64;
       const uint32_t ph = it & 1u;
       const ChunkRec& rec = m.rec[ph];
-      mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // B, C tiles, decay record
+      mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // C tile, decay record
 
       // ---- x, dy stacked over rows (K = p); e_l dy stacked over p (MN) once the previous
       // ticket's dx / dB stores have read sDGK / sDYT / sDGM
@@ -679,6 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // conj(B') = conj(B conj(cis(theta_s))) stacked (then batch 1 may start), conj(H_z) hi | lo
 #pragma unroll 1
       for (int tile = 0; tile < 3; ++tile) {
+        if (tile == 1) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
         if (tile == 2) {
           warp_arrive(&m.bar_ops1, lane);
           mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
