@@ -60,7 +60,9 @@ struct Misc {
   // read (stfree)
   uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
   // workers -> control (one arrival per worker warp)
-  uint64_t bar_ops1, bar_ops2, bar_colfree, bar_dc, bar_dx, bar_db, bar_done;
+  // (ops1: x, dy, e dy, C', B' written; ops1b: conj(H), dS' written; ops2: epilogue 1 done;
+  // ops3: carry done)
+  uint64_t bar_ops1, bar_ops1b, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db, bar_done;
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
   float2 rc[2][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the two 32-state halves
   float2 rb[2][64];  // sum_n dB'_{sn} conj(B'_{sn})
@@ -108,6 +110,23 @@ __device__ __forceinline__ TicketPos ticket_pos(int tk, int BH, int H, int nc) {
   q.b = q.bh / H;
   q.h = q.bh - q.b * H;
   return q;
+}
+
+// Four K-steps of one accumulation: operand descriptors advance by `as` / `bs` bytes per step
+// (the descriptor's address field holds address >> 4 in its low word, so a step is one add).
+// Starts the accumulator over when `fresh`.
+__device__ __forceinline__ void mma_run4(uint32_t d, uint64_t a, uint64_t b, uint32_t as,
+                                         uint32_t bs, uint32_t idesc, bool fresh) {
+  uint32_t alo = (uint32_t)a, blo = (uint32_t)b;
+  const uint32_t ahi = (uint32_t)(a >> 32), bhi = (uint32_t)(b >> 32);
+  uint32_t acc = fresh ? 0u : 1u;
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j) {
+    mma_bf16_ss_w(d, alo, ahi, blo, bhi, idesc, acc);
+    alo += as >> 4;
+    blo += bs >> 4;
+    acc = 1u;
+  }
 }
 
 // ---------------------------------------------------------------- control-warp helpers
@@ -307,12 +326,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     uint64_t* one[10] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds, &m.bar_ctl,
                          &m.bar1,    &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
-    uint64_t* eight[7] = {&m.bar_ops1, &m.bar_ops2, &m.bar_colfree, &m.bar_dc,
-                          &m.bar_dx,   &m.bar_db,   &m.bar_done};
+    uint64_t* eight[9] = {&m.bar_ops1, &m.bar_ops1b, &m.bar_ops2, &m.bar_ops3, &m.bar_colfree,
+                          &m.bar_dc,   &m.bar_dx,    &m.bar_db,   &m.bar_done};
 #pragma unroll
     for (int i = 0; i < 10; ++i) mbar_init(one[i], 1);
 #pragma unroll
-    for (int i = 0; i < 7; ++i) mbar_init(eight[i], kWorkers / 32);
+    for (int i = 0; i < 9; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -349,29 +368,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
         {
-          const uint32_t id64 = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 8; ++j) {
-              const uint32_t ko = (j >> 2) * 16384u + (j & 3) * 32u;
-              mma_bf16_ss(tmem + COL_G, sdesc(sb + OFF_C + ko, 16, 1024),
-                          sdesc(sb + OFF_B + ko + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
-            }
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_DM, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
-                          sdesc(sb + OFF_X + j * 32u + hp * 1024u, 16, 2048), id64, (hp | j) != 0);
-          const uint32_t idq = idesc_bf16(128, 128, 1, 1);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_Q, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
-                          sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idq,
-                          (hp | j) != 0);
+          const uint32_t id64 = idesc_bf16(128, 64, 0, 0), idq = idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+#pragma unroll
+            for (int ka = 0; ka < 2; ++ka)
+              mma_run4(tmem + COL_G, sdesc(sb + OFF_C + ka * 16384u, 16, 1024),
+                       sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), 32, 32, id64,
+                       hp == 0 && ka == 0);
+            mma_run4(tmem + COL_DM, sdesc(sb + OFF_DY, 16, 1024), sdesc(sb + OFF_X + hp * 1024u, 16, 2048),
+                     32, 32, id64, hp == 0);
+            mma_run4(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
+                     sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idq, hp == 0);
+          }
           mma_commit(&m.bar1);
         }
         // publish the next ticket (workers prefetch its x and dy)
@@ -379,8 +388,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         m.tick[(it + 1) & 1] = nxt;
         mbar_arrive(&m.bar_ctl);
         const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
-        // carry hand-off, then batches 2 and 3
+        // Each remaining contraction as soon as its operands are written and its TMEM columns
+        // read: dCb = dy conj(H)^T (columns nobody else uses) once conj(H) is in sH
+        const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
+        mbar_wait(&m.bar_ops1b, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+          mma_run4(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
+                   sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), 32, 2048, id128, hp == 0);
+        // after epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
+        // dXb = conj(B') dS' into the columns of G and dM
         mbar_wait(&m.bar_ops2, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        {
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp)
+            mma_run4(tmem + COL_DCA, sdesc(sb + OFF_DGK, 16, 1024),
+                     sdesc(sb + OFF_B + hp * 1024u, 16384, 2048), 32, 4096, id128, hp == 0);
+          mma_commit(&m.bar2);
+          const uint32_t idxa = idesc_bf16(128, 64, 1, 1), idxb = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+            mma_run4(tmem + COL_DXA, sdesc(sb + OFF_DYT, 8192, 1024),
+                     sdesc(sb + OFF_DY + hp * 1024u, 8192, 2048), 2048, 4096, idxa, hp == 0);
+#pragma unroll
+            for (int ka = 0; ka < 2; ++ka)
+              mma_run4(tmem + COL_DXB, sdesc(sb + OFF_B + ka * 16384u, 16, 1024),
+                       sdesc(sb + OFF_DS + hp * 16384u + ka * 8192u, 16, 1024), 32, 32, idxb,
+                       hp == 0 && ka == 0);
+          }
+          mma_commit(&m.bar3);
+        }
+        // after the carry (Q read): dBa = dG'^T conj(C') into the columns of Q; then hand dS_{z-1}
+        // and <dS_{z-1}, H_z> to the chunk z-1 ticket
+        mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+        {
+          const uint32_t idba = idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp)
+            mma_run4(tmem + COL_DBA, sdesc(sb + OFF_DGM, 8192, 1024),
+                     sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idba, hp == 0);
+        }
         if (qc.z > 0) {
           float2 dg = make_float2(0.f, 0.f);
 #pragma unroll
@@ -389,78 +439,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             dg.y += m.dgp[w].y;
           }
           __stcg(p.dgring + (long long)qc.bh * 4 + ((qc.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
-          // the workers' ring stores happened before their bar_ops2 arrivals
+          // the workers' ring stores happened before their bar_ops3 arrivals
           fence_proxy_async_global();
           st_release_gpu(p.flags + (long long)qc.bh * p.nc + qc.z - 1, 1u);
         }
-        tc_fence_after_sync();
-        {
-          const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_DCA, sdesc(sb + OFF_DGK + j * 32u, 16, 1024),
-                          sdesc(sb + OFF_B + j * 4096u + hp * 1024u, 16384, 2048), id128,
-                          (hp | j) != 0);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_DCB, sdesc(sb + OFF_DY + j * 32u, 16, 1024),
-                          sdesc(sb + OFF_H + hp * 16384u + j * 2048u, 8192, 1024), id128,
-                          (hp | j) != 0);
-          mma_commit(&m.bar2);
-          const uint32_t idxa = idesc_bf16(128, 64, 1, 1);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_DXA, sdesc(sb + OFF_DYT + j * 2048u, 8192, 1024),
-                          sdesc(sb + OFF_DY + j * 4096u + hp * 1024u, 8192, 2048), idxa,
-                          (hp | j) != 0);
-          const uint32_t idxb = idesc_bf16(128, 64, 0, 0);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 8; ++j)
-              mma_bf16_ss(tmem + COL_DXB,
-                          sdesc(sb + OFF_B + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
-                          sdesc(sb + OFF_DS + hp * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16,
-                                1024),
-                          idxb, (hp | j) != 0);
-          const uint32_t idba = idesc_bf16(128, 128, 1, 1);
-#pragma unroll 1
-          for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_DBA, sdesc(sb + OFF_DGM + j * 2048u, 8192, 1024),
-                          sdesc(sb + OFF_C + j * 4096u + hp * 1024u, 16384, 2048), idba,
-                          (hp | j) != 0);
-          mma_commit(&m.bar3);
-        }
-        // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them
+        // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them; its
+        // commit also covers dBa
         mbar_wait(&m.bar_colfree, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
         {
           const uint32_t idbb = idesc_bf16(128, 128, 0, 1);
-#pragma unroll 1
+#pragma unroll
           for (int hp = 0; hp < 2; ++hp)
-#pragma unroll 1
-            for (int j = 0; j < 4; ++j)
-              mma_bf16_ss(tmem + COL_DBB, sdesc(sb + OFF_X + j * 32u, 16, 1024),
-                          sdesc(sb + OFF_DS + hp * 16384u + j * 2048u, 8192, 1024), idbb,
-                          (hp | j) != 0);
+            mma_run4(tmem + COL_DBB, sdesc(sb + OFF_X, 16, 1024),
+                     sdesc(sb + OFF_DS + hp * 16384u, 8192, 1024), 32, 2048, idbb, hp == 0);
           mma_commit(&m.bar4);
         }
-        // dC from its staging tile in sH; the epilogue of dC has read sC, and once batch 3 has
-        // too, the next C tile and record (its slot: the workers finished the ticket before this
-        // one); the next H_z into sH once the store has read it
+        // dC from its staging tile in sH; the epilogue of dC has read sC, and once dBa has too,
+        // the next C tile and record (its slot: the workers finished the ticket before this one);
+        // the next H_z into sH once the store has read it
         mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc);
         if (nxt < p.total) {
           if (it > 0) mbar_wait(&m.bar_done, ph ^ 1u, p.err, kErrMmaWait);
-          mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
+          mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
           ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1));
         }
         bulk_wait_read_all();
@@ -721,6 +723,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                        w + 8 * jj);
       }
 
+      warp_arrive(&m.bar_ops1b, lane);
+
       // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
       mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
       tc_fence_after_sync();
@@ -750,6 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        sb + OFF_DGK + swz(stack8(r, 1), (s0 >> 3) + blk), dgv + 8 * blk);
         }
       }
+      warp_arrive(&m.bar_ops2, lane);
       // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major), <dS_{z-1}, H_z>
       {
         float qv[32];
@@ -784,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) m.dgp[warp] = dg;
       }
-      warp_arrive(&m.bar_ops2, lane);
+      warp_arrive(&m.bar_ops3, lane);
       // the next ticket: its x and dy are prefetched at the top of the loop, during the epilogues
       mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
       next = m.tick[(it + 1) & 1];
