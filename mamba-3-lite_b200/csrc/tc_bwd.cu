@@ -67,8 +67,6 @@ struct Misc {
   float2 rc[2][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the two 32-state halves
   float2 rb[2][64];  // sum_n dB'_{sn} conj(B'_{sn})
   float2 dgp[8];    // per-warp partials of <dS_{z-1}, H_z>
-  float2 dap[2];
-  float2 sfx;
   int tick[2];
   uint32_t tmem_base;
 };
@@ -505,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     TicketPos q{};
     int t0 = 0;
     float2 dgam = make_float2(0.f, 0.f);
+    float2 Ah = make_float2(0.f, 0.f);  // A[h] of the ticket in flight
     for (;;) {
       if (next < p.total) {
         const TicketPos qx = ticket_pos(next, BH, p.H, p.nc);
@@ -568,52 +567,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         warp_arrive(&m.bar_db, lane);
         workers_sync();
 
-        // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial
-        float2 ds = make_float2(0.f, 0.f);
-        if (tid < 64) {
-          const int l = tid;
-          ds.x = m.rc[0][l].x + m.rc[1][l].x - m.rb[0][l].x - m.rb[1][l].x;
-          ds.y = m.rc[0][l].y + m.rc[1][l].y - m.rb[0][l].y - m.rb[1][l].y;
-          if (l == 63) {
-            ds.x += dgam.x;
-            ds.y += dgam.y;
+        // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial (warp 0; lane L takes
+        // positions L and L + 32: each half is scanned within the warp, then the upper half's total
+        // is added to the lower half)
+        if (warp == 0) {
+          float2 dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int l = lane + 32 * u;
+            dv[u] = make_float2(m.rc[0][l].x + m.rc[1][l].x - m.rb[0][l].x - m.rb[1][l].x,
+                                m.rc[0][l].y + m.rc[1][l].y - m.rb[0][l].y - m.rb[1][l].y);
+          }
+          if (lane == 31) {
+            dv[1].x += dgam.x;
+            dv[1].y += dgam.y;
           }
 #pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {  // suffix sum within the warp
-            const float ux = __shfl_down_sync(0xffffffffu, ds.x, o);
-            const float uy = __shfl_down_sync(0xffffffffu, ds.y, o);
-            if (lane + o < 32) {
-              ds.x += ux;
-              ds.y += uy;
+          for (int o = 1; o < 32; o <<= 1) {  // suffix sums within each half
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float ux = __shfl_down_sync(0xffffffffu, dv[u].x, o);
+              const float uy = __shfl_down_sync(0xffffffffu, dv[u].y, o);
+              if (lane + o < 32) {
+                dv[u].x += ux;
+                dv[u].y += uy;
+              }
             }
           }
-          if (tid == 32) m.sfx = ds;  // sum over positions 32..63
-        }
-        workers_sync();
-        if (tid < 64) {
-          float2 da = ds;
-          if (tid < 32) {
-            da.x += m.sfx.x;
-            da.y += m.sfx.y;
-          }
-          const int t = t0 + tid;
-          const float2 A = p.A[q.h];
-          float2 dap = make_float2(0.f, 0.f);
-          if (t < p.T) {
-            p.ddt[((long long)q.b * p.T + t) * p.H + q.h] = (da.x * A.x + da.y * A.y) * rec.dsp[tid];
-            dap = make_float2(da.x * rec.sp[tid], da.y * rec.sp[tid]);
-          }
+          const float2 hi_total = make_float2(__shfl_sync(0xffffffffu, dv[1].x, 0),
+                                              __shfl_sync(0xffffffffu, dv[1].y, 0));
+          const float2 s0 = make_float2(dv[0].x + hi_total.x, dv[0].y + hi_total.y);
+          const float2 s1 = dv[1];
+          float2 dap[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            dap.x += __shfl_xor_sync(0xffffffffu, dap.x, o);
-            dap.y += __shfl_xor_sync(0xffffffffu, dap.y, o);
+          for (int u = 0; u < 2; ++u) {
+            const int l = lane + 32 * u, t = t0 + l;
+            const float2 da = u ? s1 : s0;
+            if (t < p.T) {
+              p.ddt[((long long)q.b * p.T + t) * p.H + q.h] =
+                  (da.x * Ah.x + da.y * Ah.y) * rec.dsp[l];
+              dap[u] = make_float2(da.x * rec.sp[l], da.y * rec.sp[l]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              dap[u].x += __shfl_xor_sync(0xffffffffu, dap[u].x, o);
+              dap[u].y += __shfl_xor_sync(0xffffffffu, dap[u].y, o);
+            }
           }
-          if (lane == 0) m.dap[tid >> 5] = dap;
+          if (lane == 0)
+            p.dapart[(long long)q.bh * p.nc + q.z] =
+                make_float2(dap[0].x + dap[1].x, dap[0].y + dap[1].y);
         }
-        workers_sync();
-        if (tid == 0)
-          p.dapart[(long long)q.bh * p.nc + q.z] =
-              make_float2(m.dap[0].x + m.dap[1].x, m.dap[0].y + m.dap[1].y);
         warp_arrive(&m.bar_done, lane);
         ++it;
       }
@@ -623,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       active = true;
       q = ticket_pos(next, BH, p.H, p.nc);
       t0 = q.z * 64;
+      Ah = p.A[q.h];
       const uint32_t ph = it & 1u;
       const ChunkRec& rec = m.rec[ph];
       mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // C tile, decay record
