@@ -143,10 +143,10 @@ M3SSD_API int m3ssd_bwd(const m3ssd_bwd_args* args, void* stream);
 
 /* Name of the implementation m3ssd_fwd / m3ssd_bwd use for this problem ("tcgen05-bf16x2",
  * "simt-fp32"). The tensor-core path needs head_dim = state_dim = 64, real x, and B/C with a
- * contiguous state dimension and 16-byte aligned strides; otherwise the fp32 path runs. The
- * backward additionally needs 16-byte aligned dx, dB and dC pointers (any allocator's default);
- * m3ssd_bwd runs the fp32 path for other pointers, which this query cannot see.
- * Host-only query, no device work. */
+ * contiguous state dimension and 16-byte aligned strides; otherwise the fp32 path runs. On the
+ * tensor-core path y (forward) and dx, dB, dC (backward) must be 16-byte aligned (any allocator's
+ * default), else the call returns M3SSD_ERR_ALIGN: its outputs leave through TMA stores and its
+ * `states` layout is its own, so it has no fallback for them. Host-only query, no device work. */
 M3SSD_API const char* m3ssd_fwd_path(const m3ssd_problem* prob);
 M3SSD_API const char* m3ssd_bwd_path(const m3ssd_problem* prob);
 
@@ -162,7 +162,8 @@ M3SSD_API int m3ssd_launch_count(const m3ssd_problem* prob, int backward);
  * (status word, ticket counter, one hand-off flag per chunk) is a fixed device array inside the
  * library, 131,328 bytes, held on every GPU that loads the library until exit.
  *   - Only the tensor-core forward: head_dim = state_dim = 64, real x, B/C with a contiguous
- *     state dimension and 16-byte aligned strides; otherwise M3SSD_ERR_SHAPE.
+ *     state dimension and 16-byte aligned strides; otherwise M3SSD_ERR_SHAPE. y and states must
+ *     be 16-byte aligned (M3SSD_ERR_ALIGN).
  *   - batch * nheads * ceil(seqlen / 64) must be <= 32768, otherwise M3SSD_ERR_SCRATCH_LIMIT.
  *   - The first call on a device looks up the array's device address (with that device
  *     current); make that first call before any stream capture.

@@ -222,8 +222,11 @@ int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
   if (rc) return rc;
-  if (tc_shape(&a->prob) && m3ssd::tc::fwd_supported(p))
+  if (tc_shape(&a->prob) && m3ssd::tc::fwd_supported(p)) {
+    // y leaves the tensor-core forward through TMA stores
+    if (!aligned(a->y, 16)) return M3SSD_ERR_ALIGN;
     return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream));
+  }
   return m3ssd::simt::run_fwd(p, a->y, a->states, a->workspace,
                               static_cast<cudaStream_t>(stream));
 }
@@ -249,13 +252,16 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   if (rc) return rc;
   long long dys[4];
   for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
-  // the tensor-core backward writes dx, dB, dC with TMA stores: 16-byte aligned outputs
-  if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p) && aligned(a->dx, 16) &&
-      aligned(a->dB, 16) && aligned(a->dC, 16))
+  // the tensor-core backward reads the forward's private state layout and writes dx, dB, dC
+  // with TMA stores: 16-byte aligned outputs
+  if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p)) {
+    if (!aligned(a->dx, 16) || !aligned(a->dB, 16) || !aligned(a->dC, 16))
+      return M3SSD_ERR_ALIGN;
     return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, static_cast<float*>(a->dx),
                               static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
                               static_cast<float2*>(a->dC), a->ddt, a->workspace,
                               static_cast<cudaStream_t>(stream));
+  }
   return m3ssd::simt::run_bwd(p, a->dy, dys, a->states, a->dx, static_cast<float2*>(a->dA),
                               static_cast<float2*>(a->dB), static_cast<float2*>(a->dC), a->ddt,
                               a->workspace, static_cast<cudaStream_t>(stream));
@@ -271,7 +277,7 @@ int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* a, void* stream) {
                    a->dt_strides);
   if (rc) return rc;
   if (!a->y || !a->states) return M3SSD_ERR_NULL;
-  if (!aligned(a->y, 4) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
+  if (!aligned(a->y, 16) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
   if (!m3ssd::tc::fwd_supported(p)) return M3SSD_ERR_SHAPE;
   const int64_t chunks = a->prob.batch * a->prob.nheads * (int64_t)p.nc;
   if (chunks > kStaticMaxChunks || m3ssd::tc::fwd_workspace_bytes(p) > kStaticScratchBytes)

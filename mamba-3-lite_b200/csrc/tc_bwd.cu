@@ -518,7 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (active) {
         const uint32_t ph = it & 1u;
         const ChunkRec& rec = m.rec[ph];
-        // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)) -> staging tile in sH
+        // ---- epilogue 2: dC = (dCa + e_l dCb) conj(cis(theta_l)) -> staging tile in sH, once
+        // every warp's carry has read conj(H_z) there (bar2 can complete before that)
+        mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
         mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
         {
@@ -654,8 +656,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(s, (mh & 63u) >> 3),
                      sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w);
       }
-      // ---- raw tiles -> split operands, in place, 16 lanes per row: C' = C cis(theta_l) and
-      // conj(B') = conj(B conj(cis(theta_s))) stacked (then batch 1 may start), conj(H_z) hi | lo
+      // ---- raw tiles -> split operands, in place: C' = C cis(theta_l) and
+      // conj(B') = conj(B conj(cis(theta_s))) stacked (16 lanes per row; then batch 1 may start),
+      // conj(H_z) hi | lo from the forward's thread-major state tile (float4 i of forward thread
+      // f at [i][f]; f holds row 16 (f/32 mod 4) + f mod 16, columns 64 (f/128) + 32 (f/16 mod 2))
 #pragma unroll 1
       for (int tile = 0; tile < 3; ++tile) {
         if (tile == 1) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
@@ -670,15 +674,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int j = tid + kWorkers * i;
-          const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
-          r4[i][0] = *reinterpret_cast<const float4*>(src);
-          r4[i][1] = *reinterpret_cast<const float4*>(src + 4);
+          const float4* src = reinterpret_cast<const float4*>(smem + base) +
+                              (stacked ? (j >> 4) * 32 + 2 * (j & 15) : 2 * i * kWorkers + tid);
+          r4[i][0] = src[0];
+          r4[i][1] = src[stacked ? 1 : kWorkers];
         }
         workers_sync();
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int j = tid + kWorkers * i;
-          const uint32_t l = (uint32_t)j >> 4, qq = (uint32_t)j & 15u;
+          const uint32_t l = stacked ? (uint32_t)j >> 4 : 16u * ((uint32_t)warp & 3u) + ((uint32_t)lane & 15u);
+          const uint32_t qq = stacked ? (uint32_t)j & 15u
+                                      : 8u * ((uint32_t)warp >> 2) + 4u * ((uint32_t)lane >> 4) + (uint32_t)i;
           const float2 cs = stacked ? rec.cis[l] : make_float2(1.f, 0.f);
           const float rv[8] = {r4[i][0].x, r4[i][0].y, r4[i][0].z, r4[i][0].w,
                                r4[i][1].x, r4[i][1].y, r4[i][1].z, r4[i][1].w};

@@ -16,7 +16,9 @@
 // accumulators (tc_common.cuh). B and C tiles arrive by TMA; x and dt by 128-bit loads
 // prefetched one ticket ahead. H_z is handed from the CTA that processed chunk z-1 of the same
 // sequence through global memory (it is also the `states` output the backward reads) with a
-// release flag; waits are bounded and report kErrFlagWait instead of hanging.
+// release flag; waits are bounded and report kErrFlagWait instead of hanging. A state tile is
+// stored thread-major (float4 i of thread t at [i][t]) so each warp access is 512 contiguous bytes;
+// y leaves through a swizzled staging tile and TMA stores.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -39,7 +41,8 @@ constexpr uint32_t OFF_BX = 32768;   // TMA tile of B, then B'x hi | lo (64 x 12
                                      // then conj(H_z) hi | lo as [k-atom][p][64] (K-major B)
 constexpr uint32_t OFF_XH = 65536;   // x hi [s][p]
 constexpr uint32_t OFF_XL = 73728;   // x lo
-constexpr uint32_t OFF_XT = 81920;   // x~ stacked [p-group][s][64], then Mr stacked [128][s]
+constexpr uint32_t OFF_XT = 81920;   // x~ stacked [p-group][s][64], then Mr stacked [128][s],
+                                     // then the y staging tile (two 32-float segments)
 constexpr uint32_t OFF_MISC = 98304;
 constexpr uint32_t kSmemBytes = OFF_MISC + 2048 + 1024;
 constexpr uint32_t kTmaBytes = 2u * 64u * 128u * 4u;
@@ -62,7 +65,6 @@ struct FwdParams {
   long long xs[4];
   int x_vec;
   const ChunkRec* recs;
-  float* y;
   float* states;
   uint32_t* flags;
   uint32_t* counter;
@@ -96,6 +98,12 @@ __device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
+// fp32 staging tile for a TMA store: 32-float column segment of a 64-row tile, 128-byte rows,
+// 16-byte chunks swizzled by row (the CU_TENSOR_MAP_SWIZZLE_128B layout)
+__device__ __forceinline__ uint32_t stage_addr(uint32_t seg_base, uint32_t row, uint32_t chunk) {
+  return seg_base + row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+
 __device__ __forceinline__ void split_store16(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
   float w[8];
 #pragma unroll
@@ -110,7 +118,7 @@ __device__ __forceinline__ void split_store16(uint32_t hi_addr, uint32_t lo_addr
 
 __global__ void __launch_bounds__(kThreads, 2)
     k_fwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
-             const FwdParams p) {
+             const __grid_constant__ CUtensorMap tmY, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -133,6 +141,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_barrier_init();
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmC);
+    prefetch_tmap(&tmY);
     m.first = (int)atomicAdd(p.counter, 1u);
   }
   if (warp == 0) {
@@ -153,20 +162,34 @@ __global__ void __launch_bounds__(kThreads, 2)
     load_x16(p, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
   };
   if (ticket < p.total) prefetch_regs(ticket);
+  // B, C tiles and the decay record of a ticket (issued once the previous ticket's MMAs are done)
+  auto issue_tma = [&](int tk) {
+    const int z = tk / BH, bh = tk - z * BH;
+    const int b = bh / p.H, h = bh - b * p.H;
+    mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec));
+    tma_load_4d(smem + OFF_BX, &tmB, &m.bar_tma, 0, h, z * 64, b);
+    tma_load_4d(smem + OFF_CX, &tmC, &m.bar_tma, 0, h, z * 64, b);
+    bulk_load(&m.rec, p.recs + (long long)bh * p.nc + z, (uint32_t)sizeof(ChunkRec), &m.bar_tma);
+  };
+  if (ctrl && ticket < p.total) issue_tma(ticket);
+  int yb = 0, yh = 0, yt0 = 0;  // (ctrl) output tile staged by the previous ticket
 
   uint32_t iter = 0;
   while (ticket < p.total) {
     const uint32_t ph = iter & 1u;
     const int z = ticket / BH, bh = ticket - z * BH;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
-    __syncthreads();  // previous ticket done: its MMAs completed
+    __syncthreads();  // previous ticket done: its MMAs completed, its y tile staged
     int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
     if (ctrl) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec));
-      tma_load_4d(smem + OFF_BX, &tmB, &m.bar_tma, 0, h, t0, b);
-      tma_load_4d(smem + OFF_CX, &tmC, &m.bar_tma, 0, h, t0, b);
-      bulk_load(&m.rec, p.recs + (long long)bh * p.nc + z, (uint32_t)sizeof(ChunkRec), &m.bar_tma);
+      if (iter > 0) {  // the previous ticket's y: two 32-column segments from sXT
+        tma_store_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb);
+        tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
+        bulk_commit_group();
+      }
+      yb = b;
+      yh = h;
+      yt0 = t0;
       // is H_z already published? (then its loads overlap the transform and first MMAs)
       m.h_ready = (z == 0) ? 1 : (int)ld_acquire_gpu(p.flags + (long long)bh * p.nc + z);
     }
@@ -186,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           r4[it][0] = *reinterpret_cast<const float4*>(src);
           r4[it][1] = *reinterpret_cast<const float4*>(src + 4);
         }
+        if (ctrl && tile == 0) bulk_wait_read_all();  // sXT (y staging) is rewritten below
         __syncthreads();
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
@@ -258,10 +282,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int c = 0; c < 32; ++c) hz[c] = 0.f;
     } else if (h_early) {  // H_z already published: load it while the MMAs run
-      const float* src = p.states + (((long long)bh * p.nc + z) * 64 + r) * 128 + kb;
+      const float4* src =
+          reinterpret_cast<const float4*>(p.states + ((long long)bh * p.nc + z) * 64 * 128) + tid;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
+        const float4 v = __ldcg(src + i * kThreads);
         hz[4 * i] = v.x;
         hz[4 * i + 1] = v.y;
         hz[4 * i + 2] = v.z;
@@ -270,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---- epilogue 1: Mr = exp(rho_l - rho_s) G (s <= l), split-bf16, stacked rows (over x~)
+    float el_r;  // exp(rho_r), kept for the output (the record slot is refilled before it)
     mbar_wait(&m.bar_mma1, ph, p.err, kErrMmaWait);
     tc_fence_after_sync();
     {
@@ -278,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_ld_wait();
       float mr[16];
       const float rl = m.rec.rho[r];
+      el_r = m.rec.el[r];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         const float send = part ? v[c] : v[16 + c];
@@ -308,10 +335,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         __threadfence();
       }
       __syncthreads();
-      const float* src = p.states + (((long long)bh * p.nc + z) * 64 + r) * 128 + kb;
+      const float4* src =
+          reinterpret_cast<const float4*>(p.states + ((long long)bh * p.nc + z) * 64 * 128) + tid;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
+        const float4 v = __ldcg(src + i * kThreads);
         hz[4 * i] = v.x;
         hz[4 * i + 1] = v.y;
         hz[4 * i + 2] = v.z;
@@ -358,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     {
       if (ctrl) m.nxt = nn;
       const float2 g = m.rec.g, ct = m.rec.ct;
-      float* row = p.states + ((long long)bh * p.nc * 64 + r) * 128 + kb;
+      float4* tile0 = reinterpret_cast<float4*>(p.states + (long long)bh * p.nc * 64 * 128) + tid;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float s0[16], s1[16];
@@ -383,13 +411,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (z == 0) {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            __stcg(reinterpret_cast<float4*>(row + 16 * hh) + i, make_float4(0.f, 0.f, 0.f, 0.f));
+            __stcg(tile0 + (4 * hh + i) * kThreads, make_float4(0.f, 0.f, 0.f, 0.f));
         }
         if (z + 1 < p.nc) {
-          float* dst = row + (long long)(z + 1) * 64 * 128 + 16 * hh;
+          float4* dst = tile0 + (long long)(z + 1) * 64 * 32;
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            __stcg(reinterpret_cast<float4*>(dst) + i,
+            __stcg(dst + (4 * hh + i) * kThreads,
                    make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
         }
       }
@@ -401,16 +429,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (ctrl && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
     if (next < p.total) prefetch_regs(next);
 
-    // ---- output y = Y1 + exp(rho_l) Y2
+    // ---- output y = Y1 + exp(rho_l) Y2 into the staging tile in sXT; the next ticket's B, C
+    // tiles and record load as soon as the last MMA has read sCX / sBX
     mbar_wait(&m.bar_mma2, ph, p.err, kErrMmaWait);
     mbar_wait(&m.bar_mma3, ph, p.err, kErrMmaWait);
     tc_fence_after_sync();
+    if (ctrl && next < p.total) issue_tma(next);
     {
       float y1[32], y2[32];
       tmem_ld32(tmem + lane_off + COL_Y1 + 32u * wg, y1);
       tmem_ld32(tmem + lane_off + COL_Y2 + 32u * wg, y2);
       tmem_ld_wait();
-      const float el = m.rec.el[r];
       float out[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -420,22 +449,29 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float r2 = __shfl_xor_sync(0xffffffffu, s2v, 16);
         const float a1 = (part ? y1[16 + c] : y1[c]) + r1;
         const float a2 = (part ? y2[16 + c] : y2[c]) + r2;
-        out[c] = a1 + el * a2;
+        out[c] = a1 + el_r * a2;
       }
-      const int t = t0 + r;
-      if (t < p.T) {
-        float* dst = p.y + (((long long)b * p.T + t) * p.H + h) * 64 + 32 * wg + 16 * part;
+      const uint32_t seg = sb + OFF_XT + (uint32_t)wg * 8192u;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          reinterpret_cast<float4*>(dst)[i] =
-              make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
-      }
+      for (int i = 0; i < 4; ++i)
+        st_shared_v4(stage_addr(seg, (uint32_t)r, (uint32_t)(4 * part + i)),
+                     make_uint4(__float_as_uint(out[4 * i]), __float_as_uint(out[4 * i + 1]),
+                                __float_as_uint(out[4 * i + 2]), __float_as_uint(out[4 * i + 3])));
+      fence_proxy_async_smem();
     }
     tc_fence_before_sync();
     ticket = next;
     ++iter;
   }
   __syncthreads();
+  if (ctrl) {
+    if (iter > 0) {  // the last ticket's y
+      tma_store_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb);
+      tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
+      bulk_commit_group();
+    }
+    bulk_wait_all();
+  }
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
@@ -531,7 +567,6 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
               reinterpret_cast<uintptr_t>(p.x) % 16 == 0)
                  ? 1
                  : 0;
-  fp.y = y;
   fp.states = static_cast<float*>(states);
   ChunkRec* recs = reinterpret_cast<ChunkRec*>(static_cast<char*>(states) + states_h_bytes(p));
   fp.recs = recs;
@@ -539,8 +574,9 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   fp.err = w;
   fp.counter = w + 1;
   fp.flags = w + 64;
-  CUtensorMap tmB, tmC;
-  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
+  CUtensorMap tmB, tmC, tmY;
+  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs) ||
+      !encode_out_tensor_map(&tmY, y, p, 64))
     return M3SSD_ERR_LAUNCH;
   if (cudaMemsetAsync(ws, 0, fwd_workspace_bytes(p), st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   const int rc = run_chunk_prep(p, recs, st);
@@ -552,7 +588,7 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
                            (int)kSmemBytes) != cudaSuccess)
     return M3SSD_ERR_LAUNCH;
   const int grid = fp.total < 2 * sms ? fp.total : 2 * sms;
-  k_fwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, fp);
+  k_fwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmY, fp);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }
 
