@@ -276,6 +276,12 @@ def main():
     ms = t_start.elapsed_time(t_end)
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
     bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_ev)
+    # one more step with the device status words checked: a kernel whose bounded wait gave up
+    # (a hand-off that never came) makes the run fail instead of reporting its time
+    os.environ["M3SSD_CHECK"] = "1"
+    step()
+    torch.cuda.synchronize()
+    os.environ["M3SSD_CHECK"] = "0"
 
     # e2e: pinned host inputs in, all outputs back, through the public API
     h = make_inputs("cpu", 2000 + rank, B, T, H, D, N, pin=True)

@@ -61,8 +61,9 @@ struct Misc {
   uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
   // workers -> control (one arrival per worker warp)
   // (ops1: x, dy, e dy, C', B' written; ops1b: conj(H), dS' written; ops2: epilogue 1 done;
-  // ops3: carry done)
-  uint64_t bar_ops1, bar_ops1b, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db, bar_done;
+  // ops3: carry done). Every wait is on the phase of the current ticket: no barrier can complete
+  // twice before its waiter looks, so a parity never repeats under a waiter.
+  uint64_t bar_ops1, bar_ops1b, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db;
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
   float2 rc[2][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the two 32-state halves
   float2 rb[2][64];  // sum_n dB'_{sn} conj(B'_{sn})
@@ -324,12 +325,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     uint64_t* one[10] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds, &m.bar_ctl,
                          &m.bar1,    &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
-    uint64_t* eight[9] = {&m.bar_ops1, &m.bar_ops1b, &m.bar_ops2, &m.bar_ops3, &m.bar_colfree,
-                          &m.bar_dc,   &m.bar_dx,    &m.bar_db,   &m.bar_done};
+    uint64_t* eight[8] = {&m.bar_ops1, &m.bar_ops1b, &m.bar_ops2, &m.bar_ops3,
+                          &m.bar_colfree, &m.bar_dc, &m.bar_dx, &m.bar_db};
 #pragma unroll
     for (int i = 0; i < 10; ++i) mbar_init(one[i], 1);
 #pragma unroll
-    for (int i = 0; i < 9; ++i) mbar_init(eight[i], kWorkers / 32);
+    for (int i = 0; i < 8; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -418,8 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mma_commit(&m.bar3);
         }
-        // after the carry (Q read): dBa = dG'^T conj(C') into the columns of Q; then hand dS_{z-1}
-        // and <dS_{z-1}, H_z> to the chunk z-1 ticket
+        // after the carry (Q read): dBa = dG'^T conj(C') into the columns of Q
         mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
         {
@@ -428,18 +428,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int hp = 0; hp < 2; ++hp)
             mma_run4(tmem + COL_DBA, sdesc(sb + OFF_DGM, 8192, 1024),
                      sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idba, hp == 0);
-        }
-        if (qc.z > 0) {
-          float2 dg = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            dg.x += m.dgp[w].x;
-            dg.y += m.dgp[w].y;
-          }
-          __stcg(p.dgring + (long long)qc.bh * 4 + ((qc.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
-          // the workers' ring stores happened before their bar_ops3 arrivals
-          fence_proxy_async_global();
-          st_release_gpu(p.flags + (long long)qc.bh * p.nc + qc.z - 1, 1u);
         }
         // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them; its
         // commit also covers dBa
@@ -453,13 +441,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                      sdesc(sb + OFF_DS + hp * 16384u, 8192, 1024), 32, 2048, idbb, hp == 0);
           mma_commit(&m.bar4);
         }
+        // hand dS_{z-1} and <dS_{z-1}, H_z> to the chunk z-1 ticket (after the MMA issue: the
+        // release waits for this thread's earlier memory operations)
+        if (qc.z > 0) {
+          float2 dg = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            dg.x += m.dgp[w].x;
+            dg.y += m.dgp[w].y;
+          }
+          __stcg(p.dgring + (long long)qc.bh * 4 + ((qc.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
+          // the workers' ring stores happened before their bar_ops3 arrivals
+          fence_proxy_async_global();
+          st_release_gpu(p.flags + (long long)qc.bh * p.nc + qc.z - 1, 1u);
+        }
         // dC from its staging tile in sH; the epilogue of dC has read sC, and once dBa has too,
-        // the next C tile and record (its slot: the workers finished the ticket before this one);
-        // the next H_z into sH once the store has read it
+        // the next C tile and record (its slot was the previous ticket's, which every worker warp
+        // finished before arriving at bar_ops1 of this one); the next H_z into sH once the store
+        // has read it
         mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc);
         if (nxt < p.total) {
-          if (it > 0) mbar_wait(&m.bar_done, ph ^ 1u, p.err, kErrMmaWait);
           mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
           ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1));
         }
@@ -471,12 +473,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc);
         mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc);
-        if (nxt < p.total) {
-          ctl_load_b(&tmB, smem, &m, qn);
-          ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn);
-        }
+        if (nxt < p.total) ctl_load_b(&tmB, smem, &m, qn);
         bulk_wait_read_all();
         mbar_arrive(&m.bar_stfree);
+        if (nxt < p.total) ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn);
         cur = nxt;
         qc = qn;
         ++it;
@@ -620,7 +620,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             p.dapart[(long long)q.bh * p.nc + q.z] =
                 make_float2(dap[0].x + dap[1].x, dap[0].y + dap[1].y);
         }
-        warp_arrive(&m.bar_done, lane);
         ++it;
       }
       if (next >= p.total) break;
