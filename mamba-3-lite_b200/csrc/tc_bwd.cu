@@ -60,10 +60,10 @@ struct Misc {
   // read (stfree)
   uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
   // workers -> control (one arrival per worker warp)
-  // (ops1: x, dy, e dy, C', B' written; ops1b: conj(H), dS' written; ops2: epilogue 1 done;
-  // ops3: carry done). Every wait is on the phase of the current ticket: no barrier can complete
+  // (ops1: x, dy, e dy, C', B', conj(H) written; ops2: dS' written and epilogue 1 done; ops3:
+  // carry done). Every wait is on the phase of the current ticket: no barrier can complete
   // twice before its waiter looks, so a parity never repeats under a waiter.
-  uint64_t bar_ops1, bar_ops1b, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db;
+  uint64_t bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db;
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
   float2 rc[2][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the two 32-state halves
   float2 rb[2][64];  // sum_n dB'_{sn} conj(B'_{sn})
@@ -325,12 +325,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     uint64_t* one[10] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds, &m.bar_ctl,
                          &m.bar1,    &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
-    uint64_t* eight[8] = {&m.bar_ops1, &m.bar_ops1b, &m.bar_ops2, &m.bar_ops3,
-                          &m.bar_colfree, &m.bar_dc, &m.bar_dx, &m.bar_db};
+    uint64_t* eight[7] = {&m.bar_ops1,    &m.bar_ops2, &m.bar_ops3, &m.bar_colfree,
+                          &m.bar_dc,      &m.bar_dx,   &m.bar_db};
 #pragma unroll
     for (int i = 0; i < 10; ++i) mbar_init(one[i], 1);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mbar_init(eight[i], kWorkers / 32);
+    for (int i = 0; i < 7; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -382,21 +382,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mma_commit(&m.bar1);
         }
+        // dCb = dy conj(H)^T (columns nobody else uses); conj(H) is in sH already
+        const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+          mma_run4(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
+                   sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), 32, 2048, id128, hp == 0);
         // publish the next ticket (workers prefetch its x and dy)
         const int nxt = (int)atomicAdd(p.counter, 1u);
         m.tick[(it + 1) & 1] = nxt;
         mbar_arrive(&m.bar_ctl);
         const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
         // Each remaining contraction as soon as its operands are written and its TMEM columns
-        // read: dCb = dy conj(H)^T (columns nobody else uses) once conj(H) is in sH
-        const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
-        mbar_wait(&m.bar_ops1b, ph, p.err, kErrMmaWait);
-        tc_fence_after_sync();
-#pragma unroll
-        for (int hp = 0; hp < 2; ++hp)
-          mma_run4(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
-                   sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), 32, 2048, id128, hp == 0);
-        // after epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
+        // read        // after epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
         // dXb = conj(B') dS' into the columns of G and dM
         mbar_wait(&m.bar_ops2, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
@@ -656,18 +654,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                      sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w);
       }
       // ---- raw tiles -> split operands, in place: C' = C cis(theta_l) and
-      // conj(B') = conj(B conj(cis(theta_s))) stacked (16 lanes per row; then batch 1 may start),
-      // conj(H_z) hi | lo from the forward's thread-major state tile (float4 i of forward thread
+      // conj(B') = conj(B conj(cis(theta_s))) stacked (16 lanes per row), conj(H_z) hi | lo from
+      // the forward's thread-major state tile (float4 i of forward thread
       // f at [i][f]; f holds row 16 (f/32 mod 4) + f mod 16, columns 64 (f/128) + 32 (f/16 mod 2))
 #pragma unroll 1
-      for (int tile = 0; tile < 3; ++tile) {
-        if (tile == 1) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
-        if (tile == 2) {
-          warp_arrive(&m.bar_ops1, lane);
-          mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
-        }
-        const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_B : OFF_H);
-        const bool stacked = tile < 2;
+      for (int tile = 0; tile < 3; ++tile) {  // C (landed first), H_z, B (loaded last)
+        if (tile == 1) mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
+        if (tile == 2) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
+        const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_H : OFF_B);
+        const bool stacked = tile != 1;
         const float sg = tile == 0 ? 1.f : -1.f;
         float4 r4[4][2];
 #pragma unroll
@@ -699,6 +694,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           split8_store(hi, hi + (stacked ? 1024u : 16384u), v);
         }
       }
+
+      warp_arrive(&m.bar_ops1, lane);  // batch 1 and dCb may start
 
       // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
@@ -733,8 +730,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                        sb + OFF_DS + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
                        w + 8 * jj);
       }
-
-      warp_arrive(&m.bar_ops1b, lane);
 
       // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
       mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
