@@ -195,6 +195,9 @@ def _setup_context(ctx, inputs, output):
     ctx.chunk = chunk
     ctx.flags = flags
     ctx.mark_non_differentiable(states)
+    # no zero-filled gradient for `states` (hundreds of MB at training sizes): unused grads
+    # arrive as None
+    ctx.set_materialize_grads(False)
 
 
 def _backward(ctx, dy, _dstates):
