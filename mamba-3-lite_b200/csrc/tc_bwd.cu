@@ -32,8 +32,8 @@ namespace tc {
 
 namespace {
 
-constexpr int kWorkers = 256;              // warps 0-7: operand transforms and epilogues
-constexpr int kThreads = kWorkers + 32;    // warp 8: tickets, TMA/bulk loads, flags, MMA issue
+constexpr int kWorkers = 512;              // warps 0-15: operand transforms and epilogues
+constexpr int kThreads = kWorkers + 32;    // warp 16: tickets, TMA/bulk loads, flags, MMA issue
 // shared memory map
 constexpr uint32_t OFF_C = 0;        // C'x stacked [2 k-atoms][128][64]; raw C tile lands first
 constexpr uint32_t OFF_B = 32768;    // B'x (conjugate-interleaved) stacked; raw B tile lands first
@@ -65,9 +65,9 @@ struct Misc {
   // twice before its waiter looks, so a parity never repeats under a waiter.
   uint64_t bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db;
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
-  float2 rc[2][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the two 32-state halves
-  float2 rb[2][64];  // sum_n dB'_{sn} conj(B'_{sn})
-  float2 dgp[8];    // per-warp partials of <dS_{z-1}, H_z>
+  float2 rc[4][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the four 16-state column groups
+  float2 rb[4][64];  // sum_n dB'_{sn} conj(B'_{sn})
+  float2 dgp[kWorkers / 32];  // per-warp partials of <dS_{z-1}, H_z>
   int tick[2];
   uint32_t tmem_base;
 };
@@ -217,6 +217,17 @@ __device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)
     out[c] = (part ? v[16 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
   }
 }
+// the same over a 16-column block: columns [8 p, 8 p + 8)
+__device__ __forceinline__ void ld_exch8(uint32_t taddr, int part, float (&out)[8]) {
+  float v[16];
+  tmem_ld16(taddr, v);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float send = part ? v[c] : v[8 + c];
+    out[c] = (part ? v[8 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+}
 // the same over a 64-column block: columns [32 p, 32 p + 32)
 __device__ __forceinline__ void ld_exch32(uint32_t taddr, int part, float (&out)[32]) {
   float v[32];
@@ -263,26 +274,29 @@ __device__ __forceinline__ uint32_t stage_seg(uint32_t seg01, uint32_t seg23, ui
 }
 
 // ---------------------------------------------------------------- worker helpers (out of line)
-// Epilogue of dC and dB over this thread's 32 state columns of row `row` (accumulator blocks at
-// ta, tb): v = a + w b, staged as v conj(rot) (conjugated if conj_out), and the partial row sum
-// sum v conj(X) with X the split-bf16 operand row as the tensor core saw it (hi part in stacked row
-// xrow of the k-atom at xop, lo part 8 rows further). dC: w = e_l, rot = cis(theta_l), X = C', sum = dC' conj(C').
+// Epilogue of dC and dB over this thread's 16 state columns (8 complex) of row `row`
+// (32-column accumulator blocks at ta, tb): v = a + w b, staged as v conj(rot) (conjugated if
+// conj_out) into 16-byte chunks schunk0 .. schunk0+3 of the staging segment, and the partial row
+// sum sum v conj(X) with X the split-bf16 operand as the tensor core saw it (hi part in chunks
+// xch0, xch0+1 of stacked row xrow of the k-atom at xop, lo part 8 rows further).
+// dC: w = e_l, rot = cis(theta_l), X = C', sum = dC' conj(C').
 // dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out, X = conj(B'),
 // sum = conj(dB' conj(B')).
 static __device__ __noinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int part, float w,
                                                     float2 rot, bool conj_out, uint32_t seg,
-                                                    uint32_t row, uint32_t xop, uint32_t xrow,
+                                                    uint32_t row, uint32_t schunk0, uint32_t xop,
+                                                    uint32_t xrow, uint32_t xch0,
                                                     uint64_t* colfree, int lane) {
-  float a[32], bb[32];
-  ld_exch32(ta, part, a);
-  ld_exch32(tb, part, bb);
+  float a[16], bb[16];
+  ld_exch16(ta, part, a);
+  ld_exch16(tb, part, bb);
   if (colfree != nullptr) warp_arrive(colfree, lane);
   const float2 nr = make_float2(rot.x, -rot.y);
   const float cj = conj_out ? -1.f : 1.f;
   float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int jj = 0; jj < 4; ++jj) {
-    const uint32_t xa = xop + swz(xrow, 4u * (uint32_t)part + (uint32_t)jj);
+  for (int jj = 0; jj < 2; ++jj) {
+    const uint32_t xa = xop + swz(xrow, xch0 + (uint32_t)jj);
     const uint4 hi = ld_shared_u4(xa);
     const uint4 lo = ld_shared_u4(xa + 1024u);
     const float2 xv[4] = {unsplit2(hi.x, lo.x), unsplit2(hi.y, lo.y), unsplit2(hi.z, lo.z),
@@ -298,10 +312,10 @@ static __device__ __noinline__ float2 combine_stage(uint32_t ta, uint32_t tb, in
       o[2 * u] = r2.x;
       o[2 * u + 1] = cj * r2.y;
     }
-    st_shared_v4(stage_addr(seg, row, 2u * jj),
+    st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj),
                  make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
                             __float_as_uint(o[3])));
-    st_shared_v4(stage_addr(seg, row, 2u * jj + 1u),
+    st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj + 1u),
                  make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]),
                             __float_as_uint(o[7])));
   }
@@ -444,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (qc.z > 0) {
           float2 dg = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
+          for (int w = 0; w < kWorkers / 32; ++w) {
             dg.x += m.dgp[w].x;
             dg.y += m.dgp[w].y;
           }
@@ -483,15 +497,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // =============================== worker warps 0-7 ===============================
-    const int sub = warp & 3, wg = warp >> 2;
+    // =============================== worker warps 0-15 ===============================
+    // TMEM lane quadrant sub = warp mod 4; column group grp = warp / 4 takes 32 of the 128
+    // columns of a complex accumulator (16 of a 64-column one); the thread with `part` p keeps
+    // the full sums of half of those after the hi/lo exchange.
+    const int sub = warp & 3, grp = warp >> 2;
     const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
     const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
-    const int kb = 64 * wg + 32 * part;                        // this thread's state columns
+    const int kb = 32 * grp + 16 * part;  // this thread's 16 interleaved state columns
+    const int s0c = 16 * grp + 8 * part;  // this thread's 8 columns of a 64-column accumulator
+    const uint32_t kat = (uint32_t)kb >> 6;              // k-atom of its state columns
+    const uint32_t kch = ((uint32_t)kb & 63u) >> 3;      // first of its two 16-byte chunks there
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
-    // x / dy staging: rows xs0 and xs0 + 32, columns 8 (tid & 7) .. + 7 (8 lanes per row)
+    // x / dy staging: row xs0, columns 8 (tid & 7) .. + 7 (8 lanes per row)
     const int xs0 = tid >> 3, xp0 = 8 * (tid & 7);
-    float xv[16], gv[16];
+    float xv[8], gv[8];
     mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
     int next = m.tick[0];
     // The loop turns at the prefetch point: x and dy of ticket `next` are loaded into registers,
@@ -509,9 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* xr = p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2];
         const float* gr = p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2];
         load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
-        load8(xr + 32 * p.xs[1], p.xs[3], p.x_vec, tx + 32 < p.T, xp0, xv + 8);
         load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
-        load8(gr + 32 * p.dys[1], p.dys[3], p.dy_vec, tx + 32 < p.T, xp0, gv + 8);
       }
       if (active) {
         const uint32_t ph = it & 1u;
@@ -523,13 +541,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
         {
           float2 acc = combine_stage(
-              tmem + lane_off + COL_DCA + 64u * wg, tmem + lane_off + COL_DCB + 64u * wg, part,
+              tmem + lane_off + COL_DCA + 32u * grp, tmem + lane_off + COL_DCB + 32u * grp, part,
               rec.el[r], rec.cis[r], false,
-              stage_seg(sb + OFF_H, sb + OFF_H + 16384u, (uint32_t)(kb >> 5)), (uint32_t)r,
-              sb + OFF_C + (uint32_t)wg * 16384u, stack8((uint32_t)r, 0u), &m.bar_colfree, lane);
+              stage_seg(sb + OFF_H, sb + OFF_H + 16384u, (uint32_t)grp), (uint32_t)r,
+              4u * (uint32_t)part, sb + OFF_C + kat * 16384u, stack8((uint32_t)r, 0u), kch,
+              &m.bar_colfree, lane);
           acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
           acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
-          if (part == 0) m.rc[wg][r] = acc;
+          if (part == 0) m.rc[grp][r] = acc;
         }
         warp_arrive(&m.bar_dc, lane);
 
@@ -537,14 +556,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
         {
-          float xa[16], xb[16];
-          ld_exch16(tmem + lane_off + COL_DXA + 32u * wg, part, xa);
-          ld_exch16(tmem + lane_off + COL_DXB + 32u * wg, part, xb);
+          float xa[8], xb[8];
+          ld_exch8(tmem + lane_off + COL_DXA + 16u * grp, part, xa);
+          ld_exch8(tmem + lane_off + COL_DXB + 16u * grp, part, xb);
           const float d = rec.dec[r];
-          const uint32_t seg = sb + OFF_DGK + (uint32_t)wg * 8192u;
+          const uint32_t seg = sb + OFF_DGK + ((uint32_t)s0c >> 5) * 8192u;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            st_shared_v4(stage_addr(seg, (uint32_t)r, (uint32_t)(4 * part + i)),
+          for (int i = 0; i < 2; ++i)
+            st_shared_v4(stage_addr(seg, (uint32_t)r, (((uint32_t)s0c & 31u) >> 2) + (uint32_t)i),
                          make_uint4(__float_as_uint(xa[4 * i] + d * xb[4 * i]),
                                     __float_as_uint(xa[4 * i + 1] + d * xb[4 * i + 1]),
                                     __float_as_uint(xa[4 * i + 2] + d * xb[4 * i + 2]),
@@ -556,13 +575,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
         {
           float2 acc = combine_stage(
-              tmem + lane_off + COL_DBA + 64u * wg, tmem + lane_off + COL_DBB + 64u * wg, part,
-              rec.dec[r], rec.cis[r], true,
-              stage_seg(sb + OFF_DYT, sb + OFF_DGM, (uint32_t)(kb >> 5)), (uint32_t)r,
-              sb + OFF_B + (uint32_t)wg * 16384u, stack8((uint32_t)r, 0u), nullptr, lane);
+              tmem + lane_off + COL_DBA + 32u * grp, tmem + lane_off + COL_DBB + 32u * grp, part,
+              rec.dec[r], rec.cis[r], true, stage_seg(sb + OFF_DYT, sb + OFF_DGM, (uint32_t)grp),
+              (uint32_t)r, 4u * (uint32_t)part, sb + OFF_B + kat * 16384u, stack8((uint32_t)r, 0u),
+              kch, nullptr, lane);
           acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
           acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
-          if (part == 0) m.rb[wg][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
+          if (part == 0) m.rb[grp][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
         }
         warp_arrive(&m.bar_db, lane);
         workers_sync();
@@ -575,8 +594,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int l = lane + 32 * u;
-            dv[u] = make_float2(m.rc[0][l].x + m.rc[1][l].x - m.rb[0][l].x - m.rb[1][l].x,
-                                m.rc[0][l].y + m.rc[1][l].y - m.rb[0][l].y - m.rb[1][l].y);
+            dv[u] = make_float2(
+                (m.rc[0][l].x + m.rc[1][l].x) + (m.rc[2][l].x + m.rc[3][l].x) -
+                    ((m.rb[0][l].x + m.rb[1][l].x) + (m.rb[2][l].x + m.rb[3][l].x)),
+                (m.rc[0][l].y + m.rc[1][l].y) + (m.rc[2][l].y + m.rc[3][l].y) -
+                    ((m.rb[0][l].y + m.rb[1][l].y) + (m.rb[2][l].y + m.rb[3][l].y)));
           }
           if (lane == 31) {
             dv[1].x += dgam.x;
@@ -633,30 +655,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- x, dy stacked over rows (K = p); e_l dy stacked over p (MN) once the previous
       // ticket's dx / dB stores have read sDGK / sDYT / sDGM
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const uint32_t s = (uint32_t)(xs0 + 32 * hr);
+      {
+        const uint32_t s = (uint32_t)xs0;
         split8_store(sb + OFF_X + swz(stack8(s, 0), tid & 7), sb + OFF_X + swz(stack8(s, 1), tid & 7),
-                     xv + 8 * hr);
+                     xv);
         split8_store(sb + OFF_DY + swz(stack8(s, 0), tid & 7),
-                     sb + OFF_DY + swz(stack8(s, 1), tid & 7), gv + 8 * hr);
-      }
-      if (it > 0) mbar_wait(&m.bar_stfree, ph ^ 1u, p.err, kErrMmaWait);
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const uint32_t s = (uint32_t)(xs0 + 32 * hr);
+                     sb + OFF_DY + swz(stack8(s, 1), tid & 7), gv);
+        if (it > 0) mbar_wait(&m.bar_stfree, ph ^ 1u, p.err, kErrMmaWait);
         const float e = rec.el[s];
         float w[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) w[u] = e * gv[8 * hr + u];
+        for (int u = 0; u < 8; ++u) w[u] = e * gv[u];
         const uint32_t mh = stack8((uint32_t)xp0, 0u), ml = stack8((uint32_t)xp0, 1u);
         split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(s, (mh & 63u) >> 3),
                      sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w);
       }
       // ---- raw tiles -> split operands, in place: C' = C cis(theta_l) and
       // conj(B') = conj(B conj(cis(theta_s))) stacked (16 lanes per row), conj(H_z) hi | lo from
-      // the forward's thread-major state tile (float4 i of forward thread
-      // f at [i][f]; f holds row 16 (f/32 mod 4) + f mod 16, columns 64 (f/128) + 32 (f/16 mod 2))
+      // the forward's thread-major state tile (float4 i of forward thread f at [i][f]; f holds row
+      // 16 (f/32 mod 4) + f mod 16, columns 64 (f/128) + 32 (f/16 mod 2) .. +31)
 #pragma unroll 1
       for (int tile = 0; tile < 3; ++tile) {  // C (landed first), H_z, B (loaded last)
         if (tile == 1) mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
@@ -664,22 +681,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_H : OFF_B);
         const bool stacked = tile != 1;
         const float sg = tile == 0 ? 1.f : -1.f;
-        float4 r4[4][2];
+        const int f = tid & 255;  // forward thread whose state values this thread converts
+        float4 r4[2][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
           const int j = tid + kWorkers * i;
+          const int k = 2 * (tid >> 8) + i;  // its float4 pair (2k, 2k+1) of the state tile
           const float4* src = reinterpret_cast<const float4*>(smem + base) +
-                              (stacked ? (j >> 4) * 32 + 2 * (j & 15) : 2 * i * kWorkers + tid);
+                              (stacked ? (j >> 4) * 32 + 2 * (j & 15) : 2 * k * 256 + f);
           r4[i][0] = src[0];
-          r4[i][1] = src[stacked ? 1 : kWorkers];
+          r4[i][1] = src[stacked ? 1 : 256];
         }
         workers_sync();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
           const int j = tid + kWorkers * i;
-          const uint32_t l = stacked ? (uint32_t)j >> 4 : 16u * ((uint32_t)warp & 3u) + ((uint32_t)lane & 15u);
+          const uint32_t k = 2u * ((uint32_t)tid >> 8) + (uint32_t)i;
+          const uint32_t l = stacked ? (uint32_t)j >> 4
+                                     : 16u * (((uint32_t)f >> 5) & 3u) + ((uint32_t)f & 15u);
           const uint32_t qq = stacked ? (uint32_t)j & 15u
-                                      : 8u * ((uint32_t)warp >> 2) + 4u * ((uint32_t)lane >> 4) + (uint32_t)i;
+                                      : 8u * ((uint32_t)f >> 7) + 4u * (((uint32_t)f >> 4) & 1u) + k;
           const float2 cs = stacked ? rec.cis[l] : make_float2(1.f, 0.f);
           const float rv[8] = {r4[i][0].x, r4[i][0].y, r4[i][0].z, r4[i][0].w,
                                r4[i][1].x, r4[i][1].y, r4[i][1].z, r4[i][1].w};
@@ -694,16 +715,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           split8_store(hi, hi + (stacked ? 1024u : 16384u), v);
         }
       }
-
       warp_arrive(&m.bar_ops1, lane);  // batch 1 and dCb may start
 
       // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
-      float dsz[32];
+      float dsz[16];
       dgam = make_float2(0.f, 0.f);
       if (q.z < p.nc - 1) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const float4 v = ld_shared_f4(sb + OFF_DS + (uint32_t)(i * kWorkers + tid) * 16u);
           dsz[4 * i] = v.x;
           dsz[4 * i + 1] = v.y;
@@ -713,64 +733,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         dgam = make_float2(m.dgam.x, m.dgam.y);
       } else {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) dsz[c] = 0.f;
+        for (int c = 0; c < 16; ++c) dsz[c] = 0.f;
       }
       workers_sync();
       {
         const float2 ct = rec.ct;
-        float w[32];
+        float w[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {  // (Re, -Im) of conj(cis(theta_Gamma)) dS_z
+        for (int c = 0; c < 16; c += 2) {  // (Re, -Im) of conj(cis(theta_Gamma)) dS_z
           w[c] = dsz[c] * ct.x + dsz[c + 1] * ct.y;
           w[c + 1] = -(dsz[c + 1] * ct.x - dsz[c] * ct.y);
         }
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj)
-          split8_store(sb + OFF_DS + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
-                       sb + OFF_DS + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
-                       w + 8 * jj);
+        for (int jj = 0; jj < 2; ++jj)
+          split8_store(sb + OFF_DS + kat * 8192u + swz(r, kch + jj),
+                       sb + OFF_DS + 16384u + kat * 8192u + swz(r, kch + jj), w + 8 * jj);
       }
 
       // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
       mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
       tc_fence_after_sync();
       {
-        float gs[16], ms[16];
-        ld_exch16(tmem + lane_off + COL_G + 32u * wg, part, gs);
-        ld_exch16(tmem + lane_off + COL_DM + 32u * wg, part, ms);
-        const int s0 = 32 * wg + 16 * part;
+        float gs[8], ms[8];
+        ld_exch8(tmem + lane_off + COL_G + 16u * grp, part, gs);
+        ld_exch8(tmem + lane_off + COL_DM + 16u * grp, part, ms);
         const float rl = rec.rho[r];
-        float mrv[16], dgv[16];
+        float mrv[8], dgv[8];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int s = s0 + c;
+        for (int c = 0; c < 8; ++c) {
+          const int s = s0c + c;
           const float L = (s <= r) ? expf(rl - rec.rho[s]) : 0.f;
           mrv[c] = L * gs[c];
           dgv[c] = L * ms[c];
         }
-#pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          const uint32_t mh = stack8((uint32_t)(s0 + 8 * blk), 0u);
-          const uint32_t ml = stack8((uint32_t)(s0 + 8 * blk), 1u);
-          split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
-                       sb + OFF_DYT + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), mrv + 8 * blk);
-          split8_store(sb + OFF_DGM + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
-                       sb + OFF_DGM + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), dgv + 8 * blk);
-          split8_store(sb + OFF_DGK + swz(stack8(r, 0), (s0 >> 3) + blk),
-                       sb + OFF_DGK + swz(stack8(r, 1), (s0 >> 3) + blk), dgv + 8 * blk);
-        }
+        const uint32_t mh = stack8((uint32_t)s0c, 0u), ml = stack8((uint32_t)s0c, 1u);
+        split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
+                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), mrv);
+        split8_store(sb + OFF_DGM + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
+                     sb + OFF_DGM + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), dgv);
+        split8_store(sb + OFF_DGK + swz(stack8(r, 0), s0c >> 3),
+                     sb + OFF_DGK + swz(stack8(r, 1), s0c >> 3), dgv);
       }
       warp_arrive(&m.bar_ops2, lane);
       // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major), <dS_{z-1}, H_z>
       {
-        float qv[32];
-        ld_exch32(tmem + lane_off + COL_Q + 64u * wg, part, qv);
+        float qv[16];
+        ld_exch16(tmem + lane_off + COL_Q + 32u * grp, part, qv);
         float2 dg = make_float2(0.f, 0.f);
         if (q.z > 0) {
           const float2 g = rec.g;
           float4* slot = reinterpret_cast<float4*>(p.ring + ((long long)q.bh * 4 + ((q.z - 1) & 3)) * 64 * 128);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 4; ++i) {
             float o[4];
 #pragma unroll
             for (int u = 0; u < 4; u += 2) {
@@ -779,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               o[u + 1] = -qv[c + 1] + g.x * dsz[c + 1] - g.y * dsz[c];
             }
             __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
-            const uint32_t hoff = (uint32_t)wg * 8192u + swz(r, 4 * part + (i >> 1));
+            const uint32_t hoff = kat * 8192u + swz(r, kch + (uint32_t)(i >> 1));
             const uint4 hh = ld_shared_u4(sb + OFF_H + hoff);
             const uint4 hl = ld_shared_u4(sb + OFF_H + 16384u + hoff);
             const float2 h0 = unsplit2((i & 1) ? hh.z : hh.x, (i & 1) ? hl.z : hl.x);
