@@ -60,10 +60,11 @@ struct Misc {
   // read (stfree)
   uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
   // workers -> control (one arrival per worker warp)
-  // (ops1: x, dy, e dy, C', B', conj(H) written; ops2: dS' written and epilogue 1 done; ops3:
-  // carry done). Every wait is on the phase of the current ticket: no barrier can complete
+  // (opa: x, dy, e dy written; opc: C'; oph: conj(H); ops1: B' (all of batch 1's operands); ops2:
+  // dS' written and epilogue 1 done; ops3: carry done). Every wait is on the phase of the current ticket: no barrier can complete
   // twice before its waiter looks, so a parity never repeats under a waiter.
-  uint64_t bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx, bar_db;
+  uint64_t bar_opa, bar_opc, bar_oph, bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx,
+      bar_db;
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
   float2 rc[4][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the four 16-state column groups
   float2 rb[4][64];  // sum_n dB'_{sn} conj(B'_{sn})
@@ -339,12 +340,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     uint64_t* one[10] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds, &m.bar_ctl,
                          &m.bar1,    &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
-    uint64_t* eight[7] = {&m.bar_ops1,    &m.bar_ops2, &m.bar_ops3, &m.bar_colfree,
-                          &m.bar_dc,      &m.bar_dx,   &m.bar_db};
+    uint64_t* eight[10] = {&m.bar_opa,  &m.bar_opc, &m.bar_oph,     &m.bar_ops1, &m.bar_ops2,
+                           &m.bar_ops3, &m.bar_dc,  &m.bar_colfree, &m.bar_dx,   &m.bar_db};
 #pragma unroll
     for (int i = 0; i < 10; ++i) mbar_init(one[i], 1);
 #pragma unroll
-    for (int i = 0; i < 7; ++i) mbar_init(eight[i], kWorkers / 32);
+    for (int i = 0; i < 10; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -377,31 +378,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       while (cur < p.total) {
         const uint32_t ph = it & 1u;
-        // batch 1: G = C'x B'x^T, dM = dy x^T, Q^T = (e dy)^T C'x
-        mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
-        tc_fence_after_sync();
-        {
-          const uint32_t id64 = idesc_bf16(128, 64, 0, 0), idq = idesc_bf16(128, 128, 1, 1);
-#pragma unroll
-          for (int hp = 0; hp < 2; ++hp) {
-#pragma unroll
-            for (int ka = 0; ka < 2; ++ka)
-              mma_run4(tmem + COL_G, sdesc(sb + OFF_C + ka * 16384u, 16, 1024),
-                       sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), 32, 32, id64,
-                       hp == 0 && ka == 0);
-            mma_run4(tmem + COL_DM, sdesc(sb + OFF_DY, 16, 1024), sdesc(sb + OFF_X + hp * 1024u, 16, 2048),
-                     32, 32, id64, hp == 0);
-            mma_run4(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
-                     sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idq, hp == 0);
-          }
-          mma_commit(&m.bar1);
-        }
-        // dCb = dy conj(H)^T (columns nobody else uses); conj(H) is in sH already
+        // batch 1, each contraction once its operands are converted: dM = dy x^T, then
+        // Q^T = (e dy)^T C'x, dCb = dy conj(H)^T (columns nobody else uses), G = C'x B'x^T; the
+        // commit after G covers all four
+        const uint32_t id64 = idesc_bf16(128, 64, 0, 0), idq = idesc_bf16(128, 128, 1, 1);
         const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
+        mbar_wait(&m.bar_opa, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+          mma_run4(tmem + COL_DM, sdesc(sb + OFF_DY, 16, 1024), sdesc(sb + OFF_X + hp * 1024u, 16, 2048),
+                   32, 32, id64, hp == 0);
+        mbar_wait(&m.bar_opc, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+          mma_run4(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
+                   sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idq, hp == 0);
+        mbar_wait(&m.bar_oph, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
           mma_run4(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
                    sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), 32, 2048, id128, hp == 0);
+        mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+#pragma unroll
+          for (int ka = 0; ka < 2; ++ka)
+            mma_run4(tmem + COL_G, sdesc(sb + OFF_C + ka * 16384u, 16, 1024),
+                     sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), 32, 32, id64,
+                     hp == 0 && ka == 0);
+        mma_commit(&m.bar1);
         // publish the next ticket (workers prefetch its x and dy)
         const int nxt = (int)atomicAdd(p.counter, 1u);
         m.tick[(it + 1) & 1] = nxt;
@@ -670,6 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(s, (mh & 63u) >> 3),
                      sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w);
       }
+      warp_arrive(&m.bar_opa, lane);  // dM may start
       // ---- raw tiles -> split operands, in place: C' = C cis(theta_l) and
       // conj(B') = conj(B conj(cis(theta_s))) stacked (16 lanes per row), conj(H_z) hi | lo from
       // the forward's thread-major state tile (float4 i of forward thread f at [i][f]; f holds row
@@ -714,8 +724,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       : sb + base + (qq >> 3) * 8192u + swz(l, qq & 7u);
           split8_store(hi, hi + (stacked ? 1024u : 16384u), v);
         }
+        if (tile == 0) warp_arrive(&m.bar_opc, lane);  // Q may start
+        if (tile == 1) warp_arrive(&m.bar_oph, lane);  // dCb may start
       }
-      warp_arrive(&m.bar_ops1, lane);  // batch 1 and dCb may start
+      warp_arrive(&m.bar_ops1, lane);  // G may start
 
       // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
