@@ -229,20 +229,6 @@ __device__ __forceinline__ void ld_exch8(uint32_t taddr, int part, float (&out)[
     out[c] = (part ? v[8 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
   }
 }
-// the same over a 64-column block: columns [32 p, 32 p + 32)
-__device__ __forceinline__ void ld_exch32(uint32_t taddr, int part, float (&out)[32]) {
-  float v[32];
-  tmem_ld32(taddr, out);
-  tmem_ld32(taddr + 32u, v);
-  tmem_ld_wait();
-#pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const float keep = part ? v[c] : out[c];
-    const float send = part ? out[c] : v[c];
-    out[c] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-}
-
 __device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
   float w[8];
 #pragma unroll
@@ -283,7 +269,7 @@ __device__ __forceinline__ uint32_t stage_seg(uint32_t seg01, uint32_t seg23, ui
 // dC: w = e_l, rot = cis(theta_l), X = C', sum = dC' conj(C').
 // dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out, X = conj(B'),
 // sum = conj(dB' conj(B')).
-static __device__ __noinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int part, float w,
+__device__ __forceinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int part, float w,
                                                     float2 rot, bool conj_out, uint32_t seg,
                                                     uint32_t row, uint32_t schunk0, uint32_t xop,
                                                     uint32_t xrow, uint32_t xch0,
@@ -378,6 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       while (cur < p.total) {
         const uint32_t ph = it & 1u;
+        // claim the next ticket now; its value is only needed when it is published after batch 1
+        const int nxt = (int)atomicAdd(p.counter, 1u);
         // batch 1, each contraction once its operands are converted: dM = dy x^T, then
         // Q^T = (e dy)^T C'x, dCb = dy conj(H)^T (columns nobody else uses), G = C'x B'x^T; the
         // commit after G covers all four
@@ -412,7 +400,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                      hp == 0 && ka == 0);
         mma_commit(&m.bar1);
         // publish the next ticket (workers prefetch its x and dy)
-        const int nxt = (int)atomicAdd(p.counter, 1u);
         m.tick[(it + 1) & 1] = nxt;
         mbar_arrive(&m.bar_ctl);
         const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
@@ -523,8 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float xv[8], gv[8];
     mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
     int next = m.tick[0];
-    // The loop turns at the prefetch point: x and dy of ticket `next` are loaded into registers,
-    // then the epilogues of the ticket in flight run, then ticket `next` starts.
+    // The loop turns between tickets: the epilogues of the ticket in flight run (x and dy of
+    // ticket `next` are loaded into registers during them), then ticket `next` starts.
     bool active = false;  // a ticket's epilogues are pending
     uint32_t it = 0;      // index of that ticket
     TicketPos q{};
@@ -532,14 +519,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     float2 dgam = make_float2(0.f, 0.f);
     float2 Ah = make_float2(0.f, 0.f);  // A[h] of the ticket in flight
     for (;;) {
-      if (next < p.total) {
-        const TicketPos qx = ticket_pos(next, BH, p.H, p.nc);
-        const int tx = qx.z * 64 + xs0;
-        const float* xr = p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2];
-        const float* gr = p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2];
-        load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
-        load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
-      }
+      // x and dy of ticket `next` into registers: issued after the waits below, so that no wait
+      // that falls through to its (out-of-line) polling loop has to save registers whose loads
+      // are still in flight
+      auto prefetch = [&]() {
+        if (next < p.total) {
+          const TicketPos qx = ticket_pos(next, BH, p.H, p.nc);
+          const int tx = qx.z * 64 + xs0;
+          const float* xr = p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2];
+          const float* gr = p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2];
+          load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
+          load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
+        }
+      };
+      if (!active) prefetch();
       if (active) {
         const uint32_t ph = it & 1u;
         const ChunkRec& rec = m.rec[ph];
@@ -547,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // every warp's carry has read conj(H_z) there (bar2 can complete before that)
         mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
         mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
+        prefetch();
         tc_fence_after_sync();
         {
           float2 acc = combine_stage(
@@ -581,6 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         warp_arrive(&m.bar_dx, lane);
         // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s) -> staging tiles in sDYT, sDGM
         mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
+        if (warp == 0) Ah = p.A[q.h];  // for d Sigma below (no wait in between)
         tc_fence_after_sync();
         {
           float2 acc = combine_stage(
@@ -657,7 +652,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       active = true;
       q = ticket_pos(next, BH, p.H, p.nc);
       t0 = q.z * 64;
-      Ah = p.A[q.h];
       const uint32_t ph = it & 1u;
       const ChunkRec& rec = m.rec[ph];
       mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // C tile, decay record

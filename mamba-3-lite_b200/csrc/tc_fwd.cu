@@ -127,7 +127,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sub = warp & 3, wg = warp >> 2, part = lane >> 4;
   const int r = 16 * sub + (lane & 15);  // logical row of this TMEM lane (position l, or p)
-  const int kb = 64 * wg + 32 * part;    // this thread's 32 interleaved state columns
   const int BH = p.Bsz * p.H;
   // ticket counter, TMA issue and hand-off flags are handled by one lane of warp 7 so warps 0-1
   // (cumsum) and thread 0 (MMA issue) never stall on them
@@ -173,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   if (ctrl && ticket < p.total) issue_tma(ticket);
   int yb = 0, yh = 0, yt0 = 0;  // (ctrl) output tile staged by the previous ticket
+  uint32_t h_probe = 0;         // (ctrl) H_z flag as seen at the start of the ticket
 
   uint32_t iter = 0;
   while (ticket < p.total) {
@@ -190,8 +190,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       yb = b;
       yh = h;
       yt0 = t0;
-      // is H_z already published? (then its loads overlap the transform and first MMAs)
-      m.h_ready = (z == 0) ? 1 : (int)ld_acquire_gpu(p.flags + (long long)bh * p.nc + z);
+      // is H_z already published? (then its loads overlap the transform and first MMAs; the
+      // probe is stored to shared memory after the transform, by when it has returned)
+      h_probe = (z == 0) ? 1u : ld_acquire_gpu(p.flags + (long long)bh * p.nc + z);
     }
 
     // ---- TMA tiles of B and C land in the operand buffers; rotate and split them in place
@@ -251,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t c4 = 4u * (uint32_t)(pg & 1);
       split_store16(xtb + swz(s, c4 + 0), xtb + swz(s, c4 + 2), xt);
       split_store16(xtb + swz(s, c4 + 1), xtb + swz(s, c4 + 3), xt + 8);
+      if (ctrl) m.h_ready = (int)h_probe;
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -427,7 +429,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     next = m.nxt;
     // the barrier orders every thread's H stores before this gpu-scope release
     if (ctrl && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
-    if (next < p.total) prefetch_regs(next);
 
     // ---- output y = Y1 + exp(rho_l) Y2 into the staging tile in sXT; the next ticket's B, C
     // tiles and record load as soon as the last MMA has read sCX / sBX
@@ -435,6 +436,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_wait(&m.bar_mma3, ph, p.err, kErrMmaWait);
     tc_fence_after_sync();
     if (ctrl && next < p.total) issue_tma(next);
+    // x of the next ticket, issued after the waits (a wait that falls through to its out-of-line
+    // polling loop would first wait for loads in flight into registers it saves)
+    if (next < p.total) prefetch_regs(next);
     {
       float y1[32], y2[32];
       tmem_ld32(tmem + lane_off + COL_Y1 + 32u * wg, y1);
