@@ -507,7 +507,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
     // x / dy staging: row xs0, columns 8 (tid & 7) .. + 7 (8 lanes per row)
     const int xs0 = tid >> 3, xp0 = 8 * (tid & 7);
-    float xv[8], gv[8];
     mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
     int next = m.tick[0];
     // The loop turns between tickets: the epilogues of the ticket in flight run (x and dy of
@@ -519,20 +518,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     float2 dgam = make_float2(0.f, 0.f);
     float2 Ah = make_float2(0.f, 0.f);  // A[h] of the ticket in flight
     for (;;) {
-      // x and dy of ticket `next` into registers: issued after the waits below, so that no wait
-      // that falls through to its (out-of-line) polling loop has to save registers whose loads
-      // are still in flight
-      auto prefetch = [&]() {
+      // x and dy rows of ticket `next`: pulled into L2 during the epilogues (a register prefetch
+      // would keep 16 registers live through them and spill at this kernel's register budget);
+      // the register loads follow at the start of that ticket
+      auto prefetch_l2 = [&]() {
         if (next < p.total) {
           const TicketPos qx = ticket_pos(next, BH, p.H, p.nc);
           const int tx = qx.z * 64 + xs0;
-          const float* xr = p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2];
-          const float* gr = p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2];
-          load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
-          load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
+          if (tx < p.T) {
+            prefetch_l2_line(p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2] +
+                             (long long)xp0 * p.xs[3]);
+            prefetch_l2_line(p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2] +
+                             (long long)xp0 * p.dys[3]);
+          }
         }
       };
-      if (!active) prefetch();
       if (active) {
         const uint32_t ph = it & 1u;
         const ChunkRec& rec = m.rec[ph];
@@ -540,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // every warp's carry has read conj(H_z) there (bar2 can complete before that)
         mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
         mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
-        prefetch();
+        prefetch_l2();
         tc_fence_after_sync();
         {
           float2 acc = combine_stage(
@@ -654,6 +654,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       t0 = q.z * 64;
       const uint32_t ph = it & 1u;
       const ChunkRec& rec = m.rec[ph];
+      float xv[8], gv[8];  // this thread's 8 values of x and of dy (row xs0)
+      {
+        const int tx = t0 + xs0;
+        const float* xr = p.x + q.b * p.xs[0] + (long long)tx * p.xs[1] + q.h * p.xs[2];
+        const float* gr = p.dy + q.b * p.dys[0] + (long long)tx * p.dys[1] + q.h * p.dys[2];
+        load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
+        load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
+      }
       mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // C tile, decay record
 
       // ---- x, dy stacked over rows (K = p); e_l dy stacked over p (MN) once the previous

@@ -314,6 +314,10 @@ __device__ __forceinline__ float2 split_round2(float2 v) {
 namespace m3ssd {
 namespace tc {
 // Non-tensor bulk copy global -> shared (16-byte aligned, size a multiple of 16), counted on bar.
+// pull the 128-byte line holding `ptr` into L2 (no register, nothing to wait for)
+__device__ __forceinline__ void prefetch_l2_line(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(ptr)));
+}
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
   asm volatile(
