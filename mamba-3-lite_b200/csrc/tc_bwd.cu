@@ -218,6 +218,22 @@ __device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)
     out[c] = (part ? v[16 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
   }
 }
+// the same, with fewer registers live: each 16-column half is loaded and summed on its own (both
+// partners form both sums), then the thread keeps its half
+__device__ __forceinline__ void ld_exch16_lean(uint32_t taddr, int part, float (&out)[16]) {
+  float v[16];
+  tmem_ld16(taddr, out);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < 16; ++c) out[c] += __shfl_xor_sync(0xffffffffu, out[c], 8);
+  tmem_ld16(taddr + 16u, v);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const float t = v[c] + __shfl_xor_sync(0xffffffffu, v[c], 8);
+    out[c] = part ? t : out[c];
+  }
+}
 // the same over a 16-column block: columns [8 p, 8 p + 8)
 __device__ __forceinline__ void ld_exch8(uint32_t taddr, int part, float (&out)[8]) {
   float v[16];
@@ -275,8 +291,8 @@ __device__ __forceinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int pa
                                                     uint32_t xrow, uint32_t xch0,
                                                     uint64_t* colfree, int lane) {
   float a[16], bb[16];
-  ld_exch16(ta, part, a);
-  ld_exch16(tb, part, bb);
+  ld_exch16_lean(ta, part, a);
+  ld_exch16_lean(tb, part, bb);
   if (colfree != nullptr) warp_arrive(colfree, lane);
   const float2 nr = make_float2(rot.x, -rot.y);
   const float cj = conj_out ? -1.f : 1.f;
