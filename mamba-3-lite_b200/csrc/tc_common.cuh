@@ -19,6 +19,8 @@ namespace tc {
 
 // bounded waits: iterations before a wait gives up and records an error bit
 constexpr uint32_t kSpinLimit = 1u << 24;
+// mbarrier waits that sleep up to 1 us per attempt give up after this many attempts (~1 s or less)
+constexpr uint32_t kSpinLimitSleep = 1u << 20;
 
 enum ErrorBits : uint32_t {
   kErrTmaWait = 1u << 0,  // M3SSD_DEVERR_* in include/m3ssd.h
@@ -54,20 +56,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete. Gives up after kSpinLimit polls,
-// records `code` in *err and returns false (the kernel then finishes with garbage results
-// instead of hanging the GPU).
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes or
+// about `ns` nanoseconds pass, instead of re-polling the barrier in shared memory
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // The polling loop is out of line: inlined at every wait site, the compiler's peeling of its first
-// iterations made the persistent kernels several times larger than the instruction cache.
+// iterations made the persistent kernels several times larger than the instruction cache. Each
+// iteration sleeps in hardware (up to 1 us) rather than polling, which keeps 17 waiting warps from
+// competing with the tensor core for shared-memory bandwidth.
 static __device__ __noinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint32_t* err,
-                                       uint32_t code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (i > 32) __nanosleep(64);
-  }
+                                              uint32_t code) {
+  for (uint32_t i = 0; i < kSpinLimitSleep; ++i)
+    if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
   atomicOr(err, code);
   return false;
 }
+// Waits for the phase with the given parity to complete. Gives up after kSpinLimitSleep attempts,
+// records `code` in *err and returns false (the kernel then finishes with garbage results
+// instead of hanging the GPU).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
                                           uint32_t code) {
   return mbar_try_wait(bar, parity) || mbar_spin(bar, parity, err, code);
