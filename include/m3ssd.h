@@ -173,6 +173,15 @@ M3SSD_API int m3ssd_launch_count(const m3ssd_problem* prob, int backward);
  *   - Calls no cudaMalloc/cudaFree and no allocating library routine. */
 M3SSD_API int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* args, void* stream);
 
+/* Test aid, no counterpart in the reference: checks that the library's bounded waits end instead
+ * of hanging. One thread waits on an mbarrier nobody arrives at and on a hand-off flag nobody
+ * sets, with the same helpers the tensor-core kernels use; each gives up after about a second.
+ * `workspace` (>= 256 device bytes) is cleared first; once the work has run its status word reads
+ * M3SSD_DEVERR_MMA_WAIT | M3SSD_DEVERR_FLAG_WAIT and the CUDA context remains usable. Enqueues only.
+ * Returns M3SSD_ERR_WORKSPACE for a missing or smaller workspace, M3SSD_ERR_DEVICE without an
+ * sm_100 GPU. */
+M3SSD_API int m3ssd_selftest_bounded_waits(void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -291,4 +291,12 @@ int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* a, void* stream) {
   return m3ssd::tc::run_fwd(p, a->y, a->states, scratch, static_cast<cudaStream_t>(stream));
 }
 
+int m3ssd_selftest_bounded_waits(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < 256) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return M3SSD_ERR_ALIGN;
+  const int rc = check_device();
+  if (rc) return rc;
+  return m3ssd::tc::run_selftest_waits(workspace, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

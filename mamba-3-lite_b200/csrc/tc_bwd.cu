@@ -158,13 +158,7 @@ static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const fl
     mbar_arrive(&m->bar_ds);
     return;
   }
-  const uint32_t* f = flags + (long long)q.bh * nc + q.z;
-  uint32_t i = 0;
-  for (; i < kSpinLimit; ++i) {
-    if (ld_acquire_gpu(f) != 0u) break;
-    __nanosleep(64);
-  }
-  if (i == kSpinLimit) atomicOr(err, kErrFlagWait);
+  flag_wait(flags + (long long)q.bh * nc + q.z, err);
   fence_proxy_async_global();  // the ring was written with plain stores by another CTA
   mbar_arrive_expect_tx(&m->bar_ds, 32768u + 16u);
   bulk_load(smem + OFF_DS, ring + ((long long)q.bh * 4 + (q.z & 3)) * 64 * 128, 32768u,

@@ -18,7 +18,9 @@ namespace m3ssd {
 namespace tc {
 
 // bounded waits: iterations before a wait gives up and records an error bit
-constexpr uint32_t kSpinLimit = 1u << 24;
+// flag polls (each an L2 round trip plus a short sleep, well under 1 us) before a hand-off wait
+// gives up: about a second, against tens of microseconds for the longest legitimate wait
+constexpr uint32_t kSpinLimit = 1u << 21;
 // mbarrier waits that sleep up to 1 us per attempt give up after this many attempts (~1 s or less)
 constexpr uint32_t kSpinLimitSleep = 1u << 20;
 
@@ -278,6 +280,17 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+// Waits until the hand-off flag at f is nonzero (acquire, gpu scope). Gives up after kSpinLimit
+// polls and records kErrFlagWait in *err instead of hanging; returns whether the flag was seen.
+__device__ __forceinline__ bool flag_wait(const uint32_t* f, uint32_t* err) {
+#pragma unroll 1
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (ld_acquire_gpu(f) != 0u) return true;
+    __nanosleep(64);
+  }
+  atomicOr(err, kErrFlagWait);
+  return false;
 }
 __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

@@ -327,13 +327,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- H_z from the predecessor chunk (bounded wait on its release flag if not yet seen)
     if (z > 0 && !h_early) {
       if (tid == 0) {
-        const uint32_t* f = p.flags + (long long)bh * p.nc + z;
-        uint32_t i = 0;
-        for (; i < kSpinLimit; ++i) {
-          if (ld_acquire_gpu(f) != 0u) break;
-          __nanosleep(128);
-        }
-        if (i == kSpinLimit) atomicOr(p.err, kErrFlagWait);
+        flag_wait(p.flags + (long long)bh * p.nc + z, p.err);
         __threadfence();
       }
       __syncthreads();

@@ -44,6 +44,9 @@ size_t fwd_workspace_bytes(const Problem& p);
 int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st);
 
 bool bwd_supported(const Problem& p);
+
+// tc_selftest.cu: the bounded waits give up and report (status word in the first 256 bytes of ws)
+int run_selftest_waits(void* ws, cudaStream_t st);
 size_t bwd_workspace_bytes(const Problem& p);
 int run_bwd(const Problem& p, const float* dy, const long long dys[4], const void* states,
             float* dx, float2* dA, float2* dB, float2* dC, float* ddt, void* ws, cudaStream_t st);

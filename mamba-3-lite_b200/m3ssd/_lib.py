@@ -73,6 +73,8 @@ SIGNATURES = {
     "m3ssd_bwd_path": (ctypes.c_char_p, [ctypes.POINTER(Problem)]),
     "m3ssd_launch_count": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.c_int]),
     "m3ssd_fwd_static_scratch": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
+    "m3ssd_selftest_bounded_waits": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t,
+                                                    ctypes.c_void_p]),
 }
 
 _lib = None
