@@ -21,8 +21,9 @@ namespace tc {
 // flag polls (each an L2 round trip plus a short sleep, well under 1 us) before a hand-off wait
 // gives up: about a second, against tens of microseconds for the longest legitimate wait
 constexpr uint32_t kSpinLimit = 1u << 21;
-// mbarrier waits that sleep up to 1 us per attempt give up after this many attempts (~1 s or less)
-constexpr uint32_t kSpinLimitSleep = 1u << 20;
+// mbarrier waits give up after this many sleeping attempts: ~1 s (an attempt that does not see
+// the phase complete returns after several microseconds; one that does returns at once)
+constexpr uint32_t kSpinLimitSleep = 1u << 17;
 
 enum ErrorBits : uint32_t {
   kErrTmaWait = 1u << 0,  // M3SSD_DEVERR_* in include/m3ssd.h
@@ -73,7 +74,7 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 // The polling loop is out of line: inlined at every wait site, the compiler's peeling of its first
 // iterations made the persistent kernels several times larger than the instruction cache. Each
-// iteration sleeps in hardware (up to 1 us) rather than polling, which keeps 17 waiting warps from
+// iteration sleeps in hardware rather than polling, which keeps 17 waiting warps from
 // competing with the tensor core for shared-memory bandwidth.
 static __device__ __noinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint32_t* err,
                                               uint32_t code) {
