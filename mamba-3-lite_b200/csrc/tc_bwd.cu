@@ -112,21 +112,17 @@ __device__ __forceinline__ TicketPos ticket_pos(int tk, int BH, int H, int nc) {
   return q;
 }
 
-// Four K-steps of one accumulation: operand descriptors advance by `as` / `bs` bytes per step
-// (the descriptor's address field holds address >> 4 in its low word, so a step is one add).
+// Four K-steps of one accumulation, operand descriptors advancing by AS / BS bytes per step (the
+// descriptor's address field holds address >> 4). Fully unrolled: issued from a loop, each
+// tcgen05.mma waits on the previous iteration's bookkeeping, and the batches ran ~1.7x slower.
 // Starts the accumulator over when `fresh`.
-__device__ __forceinline__ void mma_run4(uint32_t d, uint64_t a, uint64_t b, uint32_t as,
-                                         uint32_t bs, uint32_t idesc, bool fresh) {
-  uint32_t alo = (uint32_t)a, blo = (uint32_t)b;
-  const uint32_t ahi = (uint32_t)(a >> 32), bhi = (uint32_t)(b >> 32);
-  uint32_t acc = fresh ? 0u : 1u;
-#pragma unroll 1
-  for (int j = 0; j < 4; ++j) {
-    mma_bf16_ss_w(d, alo, ahi, blo, bhi, idesc, acc);
-    alo += as >> 4;
-    blo += bs >> 4;
-    acc = 1u;
-  }
+template <uint32_t AS, uint32_t BS>
+__device__ __forceinline__ void mma_run4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         bool fresh) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    mma_bf16_ss(d, a + (uint64_t)(j * (AS >> 4)), b + (uint64_t)(j * (BS >> 4)), idesc,
+                (fresh && j == 0) ? 0u : 1u);
 }
 
 // ---------------------------------------------------------------- control-warp helpers
@@ -385,29 +381,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
-          mma_run4(tmem + COL_DM, sdesc(sb + OFF_DY, 16, 1024), sdesc(sb + OFF_X + hp * 1024u, 16, 2048),
-                   32, 32, id64, hp == 0);
+          mma_run4<32, 32>(tmem + COL_DM, sdesc(sb + OFF_DY, 16, 1024),
+                           sdesc(sb + OFF_X + hp * 1024u, 16, 2048), id64, hp == 0);
         mbar_wait(&m.bar_opc, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
-          mma_run4(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
-                   sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idq, hp == 0);
+          mma_run4<2048, 4096>(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
+                               sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), idq, hp == 0);
         mbar_wait(&m.bar_oph, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
-          mma_run4(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
-                   sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), 32, 2048, id128, hp == 0);
+          mma_run4<32, 2048>(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
+                             sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), id128, hp == 0);
         mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
 #pragma unroll
           for (int ka = 0; ka < 2; ++ka)
-            mma_run4(tmem + COL_G, sdesc(sb + OFF_C + ka * 16384u, 16, 1024),
-                     sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), 32, 32, id64,
-                     hp == 0 && ka == 0);
+            mma_run4<32, 32>(tmem + COL_G, sdesc(sb + OFF_C + ka * 16384u, 16, 1024),
+                             sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), id64, hp == 0 && ka == 0);
         mma_commit(&m.bar1);
         // publish the next ticket (workers prefetch its x and dy)
         m.tick[(it + 1) & 1] = nxt;
@@ -421,19 +416,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
 #pragma unroll
           for (int hp = 0; hp < 2; ++hp)
-            mma_run4(tmem + COL_DCA, sdesc(sb + OFF_DGK, 16, 1024),
-                     sdesc(sb + OFF_B + hp * 1024u, 16384, 2048), 32, 4096, id128, hp == 0);
+            mma_run4<32, 4096>(tmem + COL_DCA, sdesc(sb + OFF_DGK, 16, 1024),
+                               sdesc(sb + OFF_B + hp * 1024u, 16384, 2048), id128, hp == 0);
           mma_commit(&m.bar2);
           const uint32_t idxa = idesc_bf16(128, 64, 1, 1), idxb = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
           for (int hp = 0; hp < 2; ++hp) {
-            mma_run4(tmem + COL_DXA, sdesc(sb + OFF_DYT, 8192, 1024),
-                     sdesc(sb + OFF_DY + hp * 1024u, 8192, 2048), 2048, 4096, idxa, hp == 0);
+            mma_run4<2048, 4096>(tmem + COL_DXA, sdesc(sb + OFF_DYT, 8192, 1024),
+                                 sdesc(sb + OFF_DY + hp * 1024u, 8192, 2048), idxa, hp == 0);
 #pragma unroll
             for (int ka = 0; ka < 2; ++ka)
-              mma_run4(tmem + COL_DXB, sdesc(sb + OFF_B + ka * 16384u, 16, 1024),
-                       sdesc(sb + OFF_DS + hp * 16384u + ka * 8192u, 16, 1024), 32, 32, idxb,
-                       hp == 0 && ka == 0);
+              mma_run4<32, 32>(tmem + COL_DXB, sdesc(sb + OFF_B + ka * 16384u, 16, 1024),
+                               sdesc(sb + OFF_DS + hp * 16384u + ka * 8192u, 16, 1024), idxb, hp == 0 && ka == 0);
           }
           mma_commit(&m.bar3);
         }
@@ -444,8 +438,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t idba = idesc_bf16(128, 128, 1, 1);
 #pragma unroll
           for (int hp = 0; hp < 2; ++hp)
-            mma_run4(tmem + COL_DBA, sdesc(sb + OFF_DGM, 8192, 1024),
-                     sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), 2048, 4096, idba, hp == 0);
+            mma_run4<2048, 4096>(tmem + COL_DBA, sdesc(sb + OFF_DGM, 8192, 1024),
+                                 sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), idba, hp == 0);
         }
         // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them; its
         // commit also covers dBa
@@ -455,8 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t idbb = idesc_bf16(128, 128, 0, 1);
 #pragma unroll
           for (int hp = 0; hp < 2; ++hp)
-            mma_run4(tmem + COL_DBB, sdesc(sb + OFF_X, 16, 1024),
-                     sdesc(sb + OFF_DS + hp * 16384u, 8192, 1024), 32, 2048, idbb, hp == 0);
+            mma_run4<32, 2048>(tmem + COL_DBB, sdesc(sb + OFF_X, 16, 1024),
+                               sdesc(sb + OFF_DS + hp * 16384u, 8192, 1024), idbb, hp == 0);
           mma_commit(&m.bar4);
         }
         // hand dS_{z-1} and <dS_{z-1}, H_z> to the chunk z-1 ticket (after the MMA issue: the
