@@ -60,7 +60,7 @@ struct Misc {
   // read (stfree)
   uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
   // workers -> control (one arrival per worker warp)
-  // (opa: x, dy, e dy written; opc: C'; oph: conj(H); ops1: B' (all of batch 1's operands); ops2:
+  // (opa: x, dy, e dy written; opc: C'; ops1: B'; oph: conj(H); ops2:
   // dS' written and epilogue 1 done; ops3: carry done). Every wait is on the phase of the current ticket: no barrier can complete
   // twice before its waiter looks, so a parity never repeats under a waiter.
   uint64_t bar_opa, bar_opc, bar_oph, bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx,
@@ -373,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // claim the next ticket now; its value is only needed when it is published after batch 1
         const int nxt = (int)atomicAdd(p.counter, 1u);
         // batch 1, each contraction once its operands are converted: dM = dy x^T, then
-        // Q^T = (e dy)^T C'x, dCb = dy conj(H)^T (columns nobody else uses), G = C'x B'x^T; the
-        // commit after G covers all four
+        // Q^T = (e dy)^T C'x, G = C'x B'x^T (the commit after G covers these three), then
+        // dCb = dy conj(H)^T (columns nobody else uses; the next commit covers it)
         const uint32_t id64 = idesc_bf16(128, 64, 0, 0), idq = idesc_bf16(128, 128, 1, 1);
         const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
         mbar_wait(&m.bar_opa, ph, p.err, kErrMmaWait);
@@ -389,12 +389,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int hp = 0; hp < 2; ++hp)
           mma_run4<2048, 4096>(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
                                sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), idq, hp == 0);
-        mbar_wait(&m.bar_oph, ph, p.err, kErrMmaWait);
-        tc_fence_after_sync();
-#pragma unroll
-        for (int hp = 0; hp < 2; ++hp)
-          mma_run4<32, 2048>(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
-                             sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), id128, hp == 0);
         mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
 #pragma unroll
@@ -404,6 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_run4<32, 32>(tmem + COL_G, sdesc(sb + OFF_C + ka * 16384u, 16, 1024),
                              sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), id64, hp == 0 && ka == 0);
         mma_commit(&m.bar1);
+        mbar_wait(&m.bar_oph, ph, p.err, kErrMmaWait);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+          mma_run4<32, 2048>(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
+                             sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), id128, hp == 0);
         // publish the next ticket (workers prefetch its x and dy)
         m.tick[(it + 1) & 1] = nxt;
         mbar_arrive(&m.bar_ctl);
@@ -691,11 +691,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the forward's thread-major state tile (float4 i of forward thread f at [i][f]; f holds row
       // 16 (f/32 mod 4) + f mod 16, columns 64 (f/128) + 32 (f/16 mod 2) .. +31)
 #pragma unroll 1
-      for (int tile = 0; tile < 3; ++tile) {  // C (landed first), H_z, B (loaded last)
-        if (tile == 1) mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
-        if (tile == 2) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
-        const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_H : OFF_B);
-        const bool stacked = tile != 1;
+      for (int tile = 0; tile < 3; ++tile) {  // C (then Q may start), B (then G), H_z (then dCb)
+        if (tile == 1) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
+        if (tile == 2) mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
+        const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_B : OFF_H);
+        const bool stacked = tile != 2;
         const float sg = tile == 0 ? 1.f : -1.f;
         const int f = tid & 255;  // forward thread whose state values this thread converts
         float4 r4[2][2];
@@ -730,10 +730,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       : sb + base + (qq >> 3) * 8192u + swz(l, qq & 7u);
           split8_store(hi, hi + (stacked ? 1024u : 16384u), v);
         }
-        if (tile == 0) warp_arrive(&m.bar_opc, lane);  // Q may start
-        if (tile == 1) warp_arrive(&m.bar_oph, lane);  // dCb may start
+        if (tile == 0) warp_arrive(&m.bar_opc, lane);   // Q may start
+        if (tile == 1) warp_arrive(&m.bar_ops1, lane);  // G may start
+        if (tile == 2) warp_arrive(&m.bar_oph, lane);   // dCb may start
       }
-      warp_arrive(&m.bar_ops1, lane);  // G may start
 
       // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
