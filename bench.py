@@ -296,28 +296,50 @@ def main():
     h2d = sum(v.numel() * v.element_size() for v in h.values())
     d2h = sum(v.numel() * v.element_size() for v in outs_h.values())
 
-    def e2e_step():
-        dd = {k: v.to(dev, non_blocking=True) for k, v in h.items()}
-        xs = [dd[k].requires_grad_(True) for k in ("x", "A", "B_t", "C_t", "dt")]
-        y = m3ssd.ssd_complex_chunkwise(*xs, chunk_size=CHUNK, precision=args.precision)
-        y.backward(dd["dy"])
-        outs_h["y"].copy_(y.detach(), non_blocking=True)
-        for k, v in zip(("dx", "dA", "dB", "dC", "ddt"), xs):
-            outs_h[k].copy_(v.grad, non_blocking=True)
+    # Steps are pipelined over three streams the way a streaming caller would drive the op: the
+    # next step's inputs go host -> device while the previous step's outputs go device -> host
+    # (PCIe is full duplex) and the GPU computes in between. Every step still copies all of its
+    # inputs in from pinned host memory and all of its outputs back, inside the timed region.
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    keys_in = ("x", "A", "B_t", "C_t", "dt", "dy")
+    dbuf = [{k: torch.empty_like(v, device=dev) for k, v in h.items()} for _ in range(2)]
+    freed = [torch.cuda.Event(), torch.cuda.Event()]  # input buffer set no longer read
+
+    def e2e_steps(n):
+        for i in range(n):
+            bi = i % 2
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(freed[bi])
+                for k in keys_in:
+                    dbuf[bi][k].copy_(h[k], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+            stream.wait_event(ev)
+            xs = [dbuf[bi][k].detach().requires_grad_(True) for k in ("x", "A", "B_t", "C_t", "dt")]
+            y = m3ssd.ssd_complex_chunkwise(*xs, chunk_size=CHUNK, precision=args.precision)
+            y.backward(dbuf[bi]["dy"])
+            freed[bi].record(stream)
+            done = torch.cuda.Event()
+            done.record(stream)
+            outs = [y.detach()] + [v.grad for v in xs]
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                for k, t in zip(("y", "dx", "dA", "dB", "dC", "ddt"), outs):
+                    t.record_stream(s_out)
+                    outs_h[k].copy_(t, non_blocking=True)
 
     e2e_ms = float("nan")
     if not args.no_e2e:
-        for _ in range(2):
-            e2e_step()
+        e2e_steps(2)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e1.record(stream)
+        e0.record(s_in)
+        e2e_steps(args.e2e_steps)
+        e1.record(s_out)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1)
 
