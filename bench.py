@@ -16,6 +16,12 @@ against the measured HBM copy bandwidth. ``cpu_baseline`` times the reference's 
 path (restated in oracle/ssd_torch_cpu.py) on the host cores over a bounded sample.
 
 ``--impl reference`` times that CPU path alone, as the reference arm.
+
+``--workload proj`` (one GPU) measures the block's whole SSD input path instead
+(models/mamba_block.py:73-88): from the in_proj output (B, T, H(D+4N+1)) fp32 to y and back to
+d(proj) and dA, once through the fused in_proj entry points (``m3ssd.ssd_from_proj``) and once
+through the block's own composition (slices, torch.complex, the operator, autograd through the
+slices), and prints one JSON line with both.
 """
 from __future__ import annotations
 
@@ -193,6 +199,89 @@ def run_reference_arm(args):
     return 0
 
 
+def run_proj_workload(args):
+    """The block's SSD input path (in_proj output -> y -> d(proj), dA), fused vs composed."""
+    import torch
+    import m3ssd
+    from oracle import cases  # seeded block-shape draws laid out as an in_proj output
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m3ssd.load()
+    B, T, H, D, N = args.batch, SHAPE["T"], SHAPE["H"], SHAPE["D"], SHAPE["N"]
+    proj_np, A_np = cases.proj_inputs(1000, B, T, H, D, N)
+    proj = torch.from_numpy(proj_np).to(dev)
+    A = torch.from_numpy(A_np).to(dev)
+    dy = torch.randn(B, T, H, D, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fused():
+        p = proj.detach().requires_grad_(True)
+        a = A.detach().requires_grad_(True)
+        y = m3ssd.ssd_from_proj(p, a, H, D, N, chunk_size=CHUNK, precision=args.precision)
+        y.backward(dy)
+        return p.grad
+
+    def composed():
+        p = proj.detach().requires_grad_(True)
+        a = A.detach().requires_grad_(True)
+        x, Bt, Ct, dt = m3ssd.unpack_proj(p, H, D, N)
+        y = m3ssd.ssd_complex_chunkwise(x, a, Bt, Ct, dt, chunk_size=CHUNK,
+                                        precision=args.precision)
+        y.backward(dy)
+        return p.grad
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    ms_fused = timed(fused)
+    ms_composed = timed(composed)
+    clocks = sampler.stop()
+    os.environ["M3SSD_CHECK"] = "1"
+    same = bool(torch.equal(fused(), composed()))
+    torch.cuda.synchronize()
+    os.environ["M3SSD_CHECK"] = "0"
+    tokens = B * T
+    peak, peak_kind = measured_peaks()
+    step_bytes = (FWD_BYTES_PER_TOKHEAD + BWD_BYTES_PER_TOKHEAD) * tokens * H
+    line = {
+        "metric": "SSD from in_proj fwd+bwd Mtokens/s/GPU @B16 L2048 H16 D64 N64",
+        "value": tokens / (ms_fused / 1e3) / 1e6, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_fused,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "in_proj output (B16, T2048, 5136 fp32 columns) -> y -> d(proj), "
+                               "dA; models/mamba_block.py:73-88",
+                   "chunk": CHUNK, "precision": args.precision,
+                   "l2": "proj 673 MB > 126 MB L2 (no flush needed)"},
+        "composed": {"value": tokens / (ms_composed / 1e3) / 1e6, "ms_per_step": ms_composed,
+                     "what": "block's slices + torch.complex + m3ssd.ssd_complex_chunkwise + "
+                             "autograd through the slices"},
+        "speedup_vs_composed": ms_composed / ms_fused,
+        "dproj_bitwise_equal": same,
+        "roofline": {"bound": "hbm", "kernel": "fwd+bwd step (fused)",
+                     "achieved": step_bytes / (ms_fused / 1e3) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": step_bytes / (ms_fused / 1e3) / 1e9 / peak,
+                     "peak_kind": peak_kind, "traffic": None},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -205,11 +294,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
     ap.add_argument("--batch", type=int, default=SHAPE["B"],
                     help="batch per rank (a smaller batch is only for profiling captures)")
+    ap.add_argument("--workload", choices=["op", "proj"], default="op",
+                    help="op: the operator on unpacked inputs (default); proj: the block's SSD "
+                         "input path from its in_proj output, fused vs composed")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "proj":
+        return run_proj_workload(args)
 
     import torch
     import torch.distributed as dist

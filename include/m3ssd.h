@@ -173,6 +173,48 @@ M3SSD_API int m3ssd_launch_count(const m3ssd_problem* prob, int backward);
  *   - Calls no cudaMalloc/cudaFree and no allocating library routine. */
 M3SSD_API int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* args, void* stream);
 
+/* ---- The block's input projection as the operator's input -------------------------------------
+ * models/mamba_block.py:73-88 slices the in_proj output `proj` (B, T, H(D + 4N + 1)) into x, B, C
+ * and dt, upcasts the slices and interleaves B and C into new complex64 tensors (torch.complex,
+ * :78 and :82) before calling ssd_complex_chunkwise; its backward then assembles the projection's
+ * gradient from six slice gradients. These two entry points take `proj` itself: columns, per
+ * token, in the block's order
+ *     x [H*D] | Re B [H*N] | Im B [H*N] | Re C [H*N] | Im C [H*N] | dt [H]
+ * (head-major inside each block, float32, last dimension contiguous). The forward computes the same
+ * y as m3ssd_fwd on the unpacked tensors and writes the same `states`; the backward writes dA and
+ * the gradient of the whole projection, `dproj`, in the same column layout (every column written).
+ *   - Tensor-core shapes only: head_dim = state_dim = 64, flags M3SSD_PREC_AUTO or
+ *     M3SSD_PREC_TENSOR (no M3SSD_X_COMPLEX); otherwise M3SSD_ERR_SHAPE.
+ *   - proj, dproj, y: 16-byte aligned; batch and time strides of proj and dproj (in floats)
+ *     multiples of 4 and H*D a multiple of 4 (the B and C blocks are read and written by TMA);
+ *     otherwise M3SSD_ERR_ALIGN.
+ *   - states / workspace sizes: m3ssd_states_bytes, m3ssd_fwd_workspace_bytes,
+ *     m3ssd_bwd_workspace_bytes of the same problem. No counterpart in the reference's API. */
+typedef struct m3ssd_proj_fwd_args {
+  m3ssd_problem prob;
+  const float* proj; int64_t proj_strides[2];  /* (B, T, H(D+4N+1)) fp32; strides of b, t */
+  const void* A;                               /* (H,) complex64 */
+  float* y;                                    /* out: (B,T,H,D) float32 contiguous */
+  void* states;                                /* out: as m3ssd_fwd */
+  void* workspace;
+  size_t workspace_bytes;
+} m3ssd_proj_fwd_args;
+
+typedef struct m3ssd_proj_bwd_args {
+  m3ssd_problem prob;                          /* identical to the forward call */
+  const float* proj; int64_t proj_strides[2];
+  const void* A;
+  const float* dy; int64_t dy_strides[4];      /* (B,T,H,D) float32: gradient of y */
+  const void* states;                          /* from the matching m3ssd_fwd_proj / m3ssd_fwd */
+  float* dproj; int64_t dproj_strides[2];      /* out: (B, T, H(D+4N+1)) fp32, proj's layout */
+  void* dA;                                    /* out: (H,) complex64 */
+  void* workspace;
+  size_t workspace_bytes;
+} m3ssd_proj_bwd_args;
+
+M3SSD_API int m3ssd_fwd_proj(const m3ssd_proj_fwd_args* args, void* stream);
+M3SSD_API int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* args, void* stream);
+
 /* Test aid, no counterpart in the reference: checks that the library's bounded waits end instead
  * of hanging. One thread waits on an mbarrier nobody arrives at and on a hand-off flag nobody
  * sets, with the same helpers the tensor-core kernels use; each gives up after about a second.

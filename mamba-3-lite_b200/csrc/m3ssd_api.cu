@@ -145,6 +145,60 @@ int static_scratch_address(void** out) {
   return M3SSD_OK;
 }
 
+// Column offsets (floats) of the in_proj output of one token, in the order the block slices it
+// (models/mamba_block.py:74-84): x, Re B, Im B, Re C, Im C, dt
+struct ProjCols {
+  int64_t x, b_re, b_im, c_re, c_im, dt, width;
+};
+ProjCols proj_cols(const m3ssd_problem& pr) {
+  const int64_t H = pr.nheads, D = pr.headdim, N = pr.dstate;
+  ProjCols c;
+  c.x = 0;
+  c.b_re = H * D;
+  c.b_im = c.b_re + H * N;
+  c.c_re = c.b_im + H * N;
+  c.c_im = c.c_re + H * N;
+  c.dt = c.c_im + H * N;
+  c.width = c.dt + H;
+  return c;
+}
+
+// Problem view of the in_proj form: x, B, C, dt are column blocks of `proj`, B and C planar.
+// Tensor-core shapes only; TMA reads the B and C blocks, so the projection must be 16-byte aligned
+// with batch / time strides (and the column offsets) multiples of 4 floats.
+int proj_problem(const m3ssd_problem* pr, const float* proj, const int64_t ps[2], const void* A,
+                 Problem* out) {
+  int rc = check_problem(pr);
+  if (rc) return rc;
+  if (!tc_shape(pr)) return M3SSD_ERR_SHAPE;
+  if (!proj || !A) return M3SSD_ERR_NULL;
+  if (ps[0] <= 0 || ps[1] <= 0) return M3SSD_ERR_SHAPE;
+  const ProjCols c = proj_cols(*pr);
+  if (!aligned(proj, 16) || !aligned(A, 8) || ps[0] % 4 || ps[1] % 4 || c.b_re % 4)
+    return M3SSD_ERR_ALIGN;
+  Problem p = make_problem(pr);
+  p.x = proj + c.x;
+  p.xs[0] = ps[0];
+  p.xs[1] = ps[1];
+  p.xs[2] = pr->headdim;
+  p.xs[3] = 1;
+  p.A = static_cast<const float2*>(A);
+  p.bc_planar = 1;
+  p.Bm = reinterpret_cast<const float2*>(proj + c.b_re);
+  p.Cm = reinterpret_cast<const float2*>(proj + c.c_re);
+  p.bs[0] = p.cs[0] = ps[0];
+  p.bs[1] = p.cs[1] = ps[1];
+  p.bs[2] = p.cs[2] = pr->dstate;
+  p.bs[3] = p.cs[3] = 1;
+  p.dt = proj + c.dt;
+  p.dts[0] = ps[0];
+  p.dts[1] = ps[1];
+  p.dts[2] = 1;
+  if (!m3ssd::tc::fwd_supported(p)) return M3SSD_ERR_ALIGN;
+  *out = p;
+  return M3SSD_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -257,9 +311,10 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p)) {
     if (!aligned(a->dx, 16) || !aligned(a->dB, 16) || !aligned(a->dC, 16))
       return M3SSD_ERR_ALIGN;
-    return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, static_cast<float*>(a->dx),
-                              static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
-                              static_cast<float2*>(a->dC), a->ddt, a->workspace,
+    const m3ssd::tc::BwdOut out = m3ssd::tc::contiguous_bwd_out(
+        p, static_cast<float*>(a->dx), static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
+        static_cast<float2*>(a->dC), a->ddt);
+    return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
                               static_cast<cudaStream_t>(stream));
   }
   return m3ssd::simt::run_bwd(p, a->dy, dys, a->states, a->dx, static_cast<float2*>(a->dA),
@@ -289,6 +344,53 @@ int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* a, void* stream) {
   if (rc) return rc;
   // run_fwd clears the status word, ticket counter and flags it uses before its kernel runs
   return m3ssd::tc::run_fwd(p, a->y, a->states, scratch, static_cast<cudaStream_t>(stream));
+}
+
+int m3ssd_fwd_proj(const m3ssd_proj_fwd_args* a, void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  Problem p;
+  int rc = proj_problem(&a->prob, a->proj, a->proj_strides, a->A, &p);
+  if (rc) return rc;
+  if (!a->y || !a->states) return M3SSD_ERR_NULL;
+  if (!aligned(a->y, 16) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
+  const size_t need = fwd_ws(p);
+  if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
+  rc = check_device();
+  if (rc) return rc;
+  return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream));
+}
+
+int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* a, void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  Problem p;
+  int rc = proj_problem(&a->prob, a->proj, a->proj_strides, a->A, &p);
+  if (rc) return rc;
+  if (!a->dy || !a->states || !a->dproj || !a->dA) return M3SSD_ERR_NULL;
+  if (!aligned(a->dy, 4) || !aligned(a->states, 16) || !aligned(a->dA, 8)) return M3SSD_ERR_ALIGN;
+  // dproj: same conditions as proj (its column blocks leave through TMA stores)
+  const int64_t sb = a->dproj_strides[0], st = a->dproj_strides[1];
+  if (sb <= 0 || st <= 0) return M3SSD_ERR_SHAPE;
+  if (!aligned(a->dproj, 16) || sb % 4 || st % 4) return M3SSD_ERR_ALIGN;
+  const size_t need = bwd_ws(p);
+  if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
+  rc = check_device();
+  if (rc) return rc;
+  long long dys[4];
+  for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
+  const ProjCols c = proj_cols(a->prob);
+  m3ssd::tc::BwdOut out{};
+  out.dx = a->dproj + c.x;
+  out.dA = static_cast<float2*>(a->dA);
+  out.dB = a->dproj + c.b_re;
+  out.dC = a->dproj + c.c_re;
+  out.ddt = a->dproj + c.dt;
+  out.planar = 1;
+  out.s_b = sb;
+  out.s_t = st;
+  return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
+                            static_cast<cudaStream_t>(stream));
 }
 
 int m3ssd_selftest_bounded_waits(void* workspace, size_t workspace_bytes, void* stream) {

@@ -52,6 +52,10 @@ struct Problem {
   const float2* Bm; long long bs[4];
   const float2* Cm; long long cs[4];
   const float* dt; long long dts[3];
+  // B and C in the column layout of the block's in_proj output (models/mamba_block.py:76-82):
+  // planar fp32, real parts at Bm / Cm (read as float), imaginary parts H*N floats further;
+  // bs / cs then count floats. Only the tensor-core kernels take this form.
+  int bc_planar;
   __host__ __device__ __forceinline__ long long Tp() const { return (long long)nc * C; }
 };
 

@@ -90,6 +90,8 @@ struct BwdParams {
   const ChunkRec* recs;
   const float* states;
   float* ddt;
+  long long ddt_sb, ddt_st;  // ddt[b, t, h] at b * ddt_sb + t * ddt_st + h
+  int hp;                    // planar B / C and dB / dC: H (the Im rows' offset), else 0
   float2* dapart;
   float* ring;
   float4* dgring;
@@ -129,17 +131,22 @@ __device__ __forceinline__ void mma_run4(uint32_t d, uint64_t a, uint64_t b, uin
 // (out of line: each runs once per ticket, and the kernel must stay small for the I-cache)
 // C tile and decay record (bar_tma), once the epilogue of dC has read sC; B tile (bar_tmb) once the
 // epilogue of dB has read sB
+// (hp > 0: planar tiles, the real part into the first 16 KB and the imaginary part, row hp + h of
+// the map, into the second)
 static __device__ __noinline__ void ctl_load_c(const CUtensorMap* tmC, uint8_t* smem, Misc* m,
-                                               const ChunkRec* recs, int nc, TicketPos q, int slot) {
+                                               const ChunkRec* recs, int nc, TicketPos q, int slot,
+                                               int hp) {
   mbar_arrive_expect_tx(&m->bar_tma, kLoadBytes);
   tma_load_4d(smem + OFF_C, tmC, &m->bar_tma, 0, q.h, q.z * 64, q.b);
+  if (hp > 0) tma_load_4d(smem + OFF_C + 16384, tmC, &m->bar_tma, 0, hp + q.h, q.z * 64, q.b);
   bulk_load(&m->rec[slot], recs + (long long)q.bh * nc + q.z, (uint32_t)sizeof(ChunkRec),
             &m->bar_tma);
 }
 static __device__ __noinline__ void ctl_load_b(const CUtensorMap* tmB, uint8_t* smem, Misc* m,
-                                               TicketPos q) {
+                                               TicketPos q, int hp) {
   mbar_arrive_expect_tx(&m->bar_tmb, 64u * 128u * 4u);
   tma_load_4d(smem + OFF_B, tmB, &m->bar_tmb, 0, q.h, q.z * 64, q.b);
+  if (hp > 0) tma_load_4d(smem + OFF_B + 16384, tmB, &m->bar_tmb, 0, hp + q.h, q.z * 64, q.b);
 }
 static __device__ __noinline__ void ctl_load_h(uint8_t* smem, Misc* m, const float* states, int nc,
                                                TicketPos q) {
@@ -162,12 +169,14 @@ static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const fl
   bulk_load(&m->dgam, dgring + (long long)q.bh * 4 + (q.z & 3), 16u, &m->bar_ds);
 }
 // TMA stores of a 64-row output tile from its 32-float staging segments (segments 0, 1 at off01,
-// 2, 3 at off23), one bulk group
+// 2, 3 at off23), one bulk group. hp > 0: planar complex tile, segments 0, 1 hold the real parts
+// (row h of the map) and 2, 3 the imaginary parts (row hp + h).
 static __device__ __noinline__ void ctl_store_tile(const CUtensorMap* map, uint8_t* smem,
                                                    uint32_t off01, uint32_t off23, int nseg,
-                                                   TicketPos q) {
+                                                   TicketPos q, int hp) {
   for (int seg = 0; seg < nseg; ++seg)
-    tma_store_4d(map, smem + (seg < 2 ? off01 : off23) + (seg & 1) * 8192, 32 * seg, q.h,
+    tma_store_4d(map, smem + (seg < 2 ? off01 : off23) + (seg & 1) * 8192,
+                 hp > 0 ? 32 * (seg & 1) : 32 * seg, hp > 0 ? q.h + hp * (seg >> 1) : q.h,
                  q.z * 64, q.b);
   bulk_commit_group();
 }
@@ -275,8 +284,12 @@ __device__ __forceinline__ uint32_t stage_seg(uint32_t seg01, uint32_t seg23, ui
 // dC: w = e_l, rot = cis(theta_l), X = C', sum = dC' conj(C').
 // dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out, X = conj(B'),
 // sum = conj(dB' conj(B')).
+// kPlanar: the real parts go to chunks schunk0, schunk0+1 of segment seg and the imaginary parts
+// to the same chunks of segment seg_im (the in_proj layout of dB and dC).
+template <bool kPlanar>
 __device__ __forceinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int part, float w,
                                                     float2 rot, bool conj_out, uint32_t seg,
+                                                    uint32_t seg_im,
                                                     uint32_t row, uint32_t schunk0, uint32_t xop,
                                                     uint32_t xrow, uint32_t xch0,
                                                     uint64_t* colfree, int lane) {
@@ -305,18 +318,30 @@ __device__ __forceinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int pa
       o[2 * u] = r2.x;
       o[2 * u + 1] = cj * r2.y;
     }
-    st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj),
-                 make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
-                            __float_as_uint(o[3])));
-    st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj + 1u),
-                 make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]),
-                            __float_as_uint(o[7])));
+    if constexpr (kPlanar) {
+      st_shared_v4(stage_addr(seg, row, schunk0 + (uint32_t)jj),
+                   make_uint4(__float_as_uint(o[0]), __float_as_uint(o[2]), __float_as_uint(o[4]),
+                              __float_as_uint(o[6])));
+      st_shared_v4(stage_addr(seg_im, row, schunk0 + (uint32_t)jj),
+                   make_uint4(__float_as_uint(o[1]), __float_as_uint(o[3]), __float_as_uint(o[5]),
+                              __float_as_uint(o[7])));
+    } else {
+      st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj),
+                   make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
+                              __float_as_uint(o[3])));
+      st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj + 1u),
+                   make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]),
+                              __float_as_uint(o[7])));
+    }
   }
   return acc;
 }
 
 }  // namespace
 
+// kPlanar: B and C arrive, and dB and dC leave, as separate real and imaginary tiles (the in_proj
+// column layout); everything else is shared
+template <bool kPlanar>
 __global__ void __launch_bounds__(kThreads, 1)
     k_bwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDB,
@@ -362,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&m.bar_ctl);
       TicketPos qc = ticket_pos(cur, BH, p.H, p.nc);
       if (cur < p.total) {
-        ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qc, 0);
-        ctl_load_b(&tmB, smem, &m, qc);
+        ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qc, 0, p.hp);
+        ctl_load_b(&tmB, smem, &m, qc, p.hp);
         ctl_load_h(smem, &m, p.states, p.nc, qc);
         ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qc);
       }
@@ -472,20 +497,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         // finished before arriving at bar_ops1 of this one); the next H_z into sH once the store
         // has read it
         mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
-        ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc);
+        ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc, p.hp);
         if (nxt < p.total) {
           mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
-          ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1));
+          ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1), p.hp);
         }
         bulk_wait_read_all();
         if (nxt < p.total) ctl_load_h(smem, &m, p.states, p.nc, qn);
         // dx from sDGK, dB from sDYT / sDGM; the next B tile (the epilogue of dB has read sB) and
         // the next dS (dBb has read sDS)
         mbar_wait(&m.bar_dx, ph, p.err, kErrMmaWait);
-        ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc);
+        ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc, 0);
         mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
-        ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc);
-        if (nxt < p.total) ctl_load_b(&tmB, smem, &m, qn);
+        ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc, p.hp);
+        if (nxt < p.total) ctl_load_b(&tmB, smem, &m, qn, p.hp);
         bulk_wait_read_all();
         mbar_arrive(&m.bar_stfree);
         if (nxt < p.total) ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn);
@@ -506,6 +531,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
     const int kb = 32 * grp + 16 * part;  // this thread's 16 interleaved state columns
     const int s0c = 16 * grp + 8 * part;  // this thread's 8 columns of a 64-column accumulator
+    // staging place of its 8 complex values of dC / dB (state columns 16 grp + 8 part .. +7):
+    // interleaved, floats 32 grp + 16 part .. +15 = segment grp, chunks 4 part .. +3; planar, Re
+    // (and Im) n = 16 grp + 8 part .. +7 = segment grp / 2 (and 2 + grp / 2), chunks
+    // 4 (grp mod 2) + 2 part, +1
+    const uint32_t sseg = kPlanar ? (uint32_t)grp >> 1 : (uint32_t)grp;
+    const uint32_t schunk0 = kPlanar ? 4u * ((uint32_t)grp & 1u) + 2u * (uint32_t)part
+                                     : 4u * (uint32_t)part;
     const uint32_t kat = (uint32_t)kb >> 6;              // k-atom of its state columns
     const uint32_t kch = ((uint32_t)kb & 63u) >> 3;      // first of its two 16-byte chunks there
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
@@ -547,12 +579,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_l2();
         tc_fence_after_sync();
         {
-          float2 acc = combine_stage(
+          float2 acc = combine_stage<kPlanar>(
               tmem + lane_off + COL_DCA + 32u * grp, tmem + lane_off + COL_DCB + 32u * grp, part,
-              rec.el[r], rec.cis[r], false,
-              stage_seg(sb + OFF_H, sb + OFF_H + 16384u, (uint32_t)grp), (uint32_t)r,
-              4u * (uint32_t)part, sb + OFF_C + kat * 16384u, stack8((uint32_t)r, 0u), kch,
-              &m.bar_colfree, lane);
+              rec.el[r], rec.cis[r], false, stage_seg(sb + OFF_H, sb + OFF_H + 16384u, sseg),
+              stage_seg(sb + OFF_H, sb + OFF_H + 16384u, sseg + 2u), (uint32_t)r, schunk0,
+              sb + OFF_C + kat * 16384u, stack8((uint32_t)r, 0u), kch, &m.bar_colfree, lane);
           acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
           acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
           if (part == 0) m.rc[grp][r] = acc;
@@ -582,11 +613,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (warp == 0) Ah = p.A[q.h];  // for d Sigma below (no wait in between)
         tc_fence_after_sync();
         {
-          float2 acc = combine_stage(
+          float2 acc = combine_stage<kPlanar>(
               tmem + lane_off + COL_DBA + 32u * grp, tmem + lane_off + COL_DBB + 32u * grp, part,
-              rec.dec[r], rec.cis[r], true, stage_seg(sb + OFF_DYT, sb + OFF_DGM, (uint32_t)grp),
-              (uint32_t)r, 4u * (uint32_t)part, sb + OFF_B + kat * 16384u, stack8((uint32_t)r, 0u),
-              kch, nullptr, lane);
+              rec.dec[r], rec.cis[r], true, stage_seg(sb + OFF_DYT, sb + OFF_DGM, sseg),
+              stage_seg(sb + OFF_DYT, sb + OFF_DGM, sseg + 2u), (uint32_t)r, schunk0,
+              sb + OFF_B + kat * 16384u, stack8((uint32_t)r, 0u), kch, nullptr, lane);
           acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
           acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
           if (part == 0) m.rb[grp][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
@@ -634,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int l = lane + 32 * u, t = t0 + l;
             const float2 da = u ? s1 : s0;
             if (t < p.T) {
-              p.ddt[((long long)q.b * p.T + t) * p.H + q.h] =
+              p.ddt[q.b * p.ddt_sb + (long long)t * p.ddt_st + q.h] =
                   (da.x * Ah.x + da.y * Ah.y) * rec.dsp[l];
               dap[u] = make_float2(da.x * rec.sp[l], da.y * rec.sp[l]);
             }
@@ -703,10 +734,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
           const int j = tid + kWorkers * i;
           const int k = 2 * (tid >> 8) + i;  // its float4 pair (2k, 2k+1) of the state tile
-          const float4* src = reinterpret_cast<const float4*>(smem + base) +
-                              (stacked ? (j >> 4) * 32 + 2 * (j & 15) : 2 * k * 256 + f);
-          r4[i][0] = src[0];
-          r4[i][1] = src[stacked ? 1 : 256];
+          if (kPlanar && stacked) {  // Re and Im of complex 4q .. 4q+3 of row l, 16 KB apart
+            const float4* src = reinterpret_cast<const float4*>(smem + base) + (j >> 4) * 16 + (j & 15);
+            const float4 re = src[0], im = src[1024];
+            r4[i][0] = make_float4(re.x, im.x, re.y, im.y);
+            r4[i][1] = make_float4(re.z, im.z, re.w, im.w);
+          } else {
+            const float4* src = reinterpret_cast<const float4*>(smem + base) +
+                                (stacked ? (j >> 4) * 32 + 2 * (j & 15) : 2 * k * 256 + f);
+            r4[i][0] = src[0];
+            r4[i][1] = src[stacked ? 1 : 256];
+          }
         }
         workers_sync();
 #pragma unroll
@@ -891,9 +929,21 @@ bool bwd_supported(const Problem& p) { return fwd_supported(p); }
 
 size_t bwd_workspace_bytes(const Problem& p) { return bwd_layout(p).total; }
 
+BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, float2* dC,
+                          float* ddt) {
+  (void)p;
+  BwdOut o{};
+  o.dx = dx;
+  o.dA = dA;
+  o.dB = reinterpret_cast<float*>(dB);
+  o.dC = reinterpret_cast<float*>(dC);
+  o.ddt = ddt;
+  o.planar = 0;
+  return o;
+}
+
 int run_bwd(const Problem& p, const float* dy, const long long dys[4], const void* states,
-            float* dx, float2* dA, float2* dB, float2* dC, float* ddt, void* ws,
-            cudaStream_t st) {
+            const BwdOut& out, void* ws, cudaStream_t st) {
   const BwdLayout L = bwd_layout(p);
   BwdParams bp{};
   bp.Bsz = p.Bsz;
@@ -922,7 +972,12 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
   }
   bp.states = static_cast<const float*>(states);
   bp.recs = reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
-  bp.ddt = ddt;
+  bp.ddt = out.ddt;
+  // planar B / C in and planar dB / dC out go together (the in_proj entry points)
+  if ((out.planar != 0) != (p.bc_planar != 0)) return M3SSD_ERR_SHAPE;
+  bp.hp = out.planar ? p.H : 0;
+  bp.ddt_sb = out.planar ? out.s_b : (long long)p.T * p.H;
+  bp.ddt_st = out.planar ? out.s_t : (long long)p.H;
   char* base = static_cast<char*>(ws);
   bp.err = reinterpret_cast<uint32_t*>(base);
   bp.counter = reinterpret_cast<uint32_t*>(base) + 1;
@@ -931,20 +986,30 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
   bp.dgring = reinterpret_cast<float4*>(base + L.dgring);
   bp.dapart = reinterpret_cast<float2*>(base + L.dapart);
   CUtensorMap tmB, tmC, tmDX, tmDB, tmDC;
-  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs) ||
-      !encode_out_tensor_map(&tmDX, dx, p, 64) || !encode_out_tensor_map(&tmDB, dB, p, 128) ||
-      !encode_out_tensor_map(&tmDC, dC, p, 128))
+  if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
     return M3SSD_ERR_LAUNCH;
+  if (out.planar) {
+    // dx rows of D = 64 floats per head; dB, dC as (2H rows of N = 64 floats), Im rows after Re
+    if (!encode_out_map_strided(&tmDX, out.dx, p, 64, p.H, 64, out.s_t, out.s_b) ||
+        !encode_out_map_strided(&tmDB, out.dB, p, 64, 2 * p.H, 64, out.s_t, out.s_b) ||
+        !encode_out_map_strided(&tmDC, out.dC, p, 64, 2 * p.H, 64, out.s_t, out.s_b))
+      return M3SSD_ERR_LAUNCH;
+  } else if (!encode_out_tensor_map(&tmDX, out.dx, p, 64) ||
+             !encode_out_tensor_map(&tmDB, out.dB, p, 128) ||
+             !encode_out_tensor_map(&tmDC, out.dC, p, 128)) {
+    return M3SSD_ERR_LAUNCH;
+  }
   if (cudaMemsetAsync(ws, 0, L.ring, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaFuncSetAttribute(k_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kSmemBytes) != cudaSuccess)
+  auto kern = out.planar ? k_bwd_tc<true> : k_bwd_tc<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+      cudaSuccess)
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
-  k_bwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmDX, tmDB, tmDC, bp);
-  k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, dA);
+  kern<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmDX, tmDB, tmDC, bp);
+  k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, out.dA);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }
 

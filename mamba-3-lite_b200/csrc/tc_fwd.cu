@@ -36,7 +36,8 @@ constexpr int kThreads = 256;
 
 // Shared memory map (offsets from a 1024-aligned base), ~100 KB so two CTAs share an SM:
 // one CTA's memory waits and barriers overlap the other's MMAs and epilogues.
-constexpr uint32_t OFF_CX = 0;       // TMA tile of C (fp32 64 x 128), then C'x stacked (A operand)
+constexpr uint32_t OFF_CX = 0;       // TMA tile of C (fp32 64 x 128, or Re | Im 64 x 64 each),
+                                     // then C'x stacked (A operand)
 constexpr uint32_t OFF_BX = 32768;   // TMA tile of B, then B'x hi | lo (64 x 128 each 16 KB),
                                      // then conj(H_z) hi | lo as [k-atom][p][64] (K-major B)
 constexpr uint32_t OFF_XH = 65536;   // x hi [s][p]
@@ -116,6 +117,9 @@ __device__ __forceinline__ void split_store16(uint32_t hi_addr, uint32_t lo_addr
 
 }  // namespace
 
+// kPlanar: B and C tiles arrive as separate real and imaginary 64 x 64 fp32 tiles (the in_proj
+// column layout) instead of one interleaved 64 x 128 tile; everything after the transform is shared
+template <bool kPlanar>
 __global__ void __launch_bounds__(kThreads, 2)
     k_fwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmY, const FwdParams p) {
@@ -168,6 +172,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec));
     tma_load_4d(smem + OFF_BX, &tmB, &m.bar_tma, 0, h, z * 64, b);
     tma_load_4d(smem + OFF_CX, &tmC, &m.bar_tma, 0, h, z * 64, b);
+    if constexpr (kPlanar) {  // imaginary parts: H*N floats after the real parts (row h + H)
+      tma_load_4d(smem + OFF_BX + 16384, &tmB, &m.bar_tma, 0, p.H + h, z * 64, b);
+      tma_load_4d(smem + OFF_CX + 16384, &tmC, &m.bar_tma, 0, p.H + h, z * 64, b);
+    }
     bulk_load(&m.rec, p.recs + (long long)bh * p.nc + z, (uint32_t)sizeof(ChunkRec), &m.bar_tma);
   };
   if (ctrl && ticket < p.total) issue_tma(ticket);
@@ -206,9 +214,17 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
           const int j = tid + kThreads * it;
-          const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
-          r4[it][0] = *reinterpret_cast<const float4*>(src);
-          r4[it][1] = *reinterpret_cast<const float4*>(src + 4);
+          if constexpr (kPlanar) {  // Re and Im of complex 4q .. 4q+3 of row l, interleaved here
+            const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 64 + 4 * (j & 15);
+            const float4 re = *reinterpret_cast<const float4*>(src);
+            const float4 im = *reinterpret_cast<const float4*>(src + 4096);
+            r4[it][0] = make_float4(re.x, im.x, re.y, im.y);
+            r4[it][1] = make_float4(re.z, im.z, re.w, im.w);
+          } else {
+            const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
+            r4[it][0] = *reinterpret_cast<const float4*>(src);
+            r4[it][1] = *reinterpret_cast<const float4*>(src + 4);
+          }
         }
         if (ctrl && tile == 0) bulk_wait_read_all();  // sXT (y staging) is rewritten below
         __syncthreads();
@@ -478,10 +494,17 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------------------------
 namespace {
 
-bool bc_tma_ok(const void* ptr, const long long st[4]) {
+// TMA needs a 16-byte aligned base and 16-byte multiples for every stride but the innermost
+bool bc_tma_ok(const Problem& p, const void* ptr, const long long st[4]) {
   if (st[3] != 1) return false;
-  for (int i = 0; i < 3; ++i)
-    if (st[i] <= 0 || (st[i] % 2) != 0) return false;
+  if (p.bc_planar) {  // float strides; the imaginary rows sit H*N floats after the real ones
+    if (st[2] != p.N) return false;
+    for (int i = 0; i < 2; ++i)
+      if (st[i] <= 0 || (st[i] % 4) != 0) return false;
+  } else {            // complex strides
+    for (int i = 0; i < 3; ++i)
+      if (st[i] <= 0 || (st[i] % 2) != 0) return false;
+  }
   return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0;
 }
 
@@ -505,11 +528,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 static bool encode_bc_map_impl(CUtensorMap* map, const void* ptr, const Problem& p, const long long st[4]) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   if (!encode) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)(2 * p.N), (cuuint64_t)p.H, (cuuint64_t)p.T,
-                        (cuuint64_t)p.Bsz};
-  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 8u, (cuuint64_t)st[1] * 8u,
-                           (cuuint64_t)st[0] * 8u};
-  cuuint32_t box[4] = {128u, 1u, 64u, 1u};
+  // interleaved: (B, T, H, 2N floats), box 64 steps x 2N floats of one head.
+  // planar: (B, T, 2H, N floats) where row h is Re of head h and row H + h its Im (Im follows
+  // Re by H*N floats in the in_proj layout), box 64 steps x N floats.
+  const bool pl = p.bc_planar != 0;
+  cuuint64_t dims[4] = {(cuuint64_t)(pl ? p.N : 2 * p.N), (cuuint64_t)(pl ? 2 * p.H : p.H),
+                        (cuuint64_t)p.T, (cuuint64_t)p.Bsz};
+  const cuuint64_t esz = pl ? 4u : 8u;
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * esz, (cuuint64_t)st[1] * esz,
+                           (cuuint64_t)st[0] * esz};
+  cuuint32_t box[4] = {pl ? 64u : 128u, 1u, 64u, 1u};
   cuuint32_t es[4] = {1u, 1u, 1u, 1u};
   const CUresult rc = encode(
       map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), dims, strides, box, es,
@@ -524,12 +552,18 @@ bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
 }
 
 bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int row_floats) {
+  const long long rf = row_floats;
+  return encode_out_map_strided(map, ptr, p, row_floats, p.H, rf, rf * p.H, rf * p.H * p.T);
+}
+
+bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int row_floats,
+                            int rows, long long s_row, long long s_t, long long s_b) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   if (!encode || (reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
-  const cuuint64_t rf = (cuuint64_t)row_floats;
-  cuuint64_t dims[4] = {rf, (cuuint64_t)p.H, (cuuint64_t)p.T, (cuuint64_t)p.Bsz};
-  cuuint64_t strides[3] = {rf * 4u, rf * 4u * (cuuint64_t)p.H,
-                           rf * 4u * (cuuint64_t)p.H * (cuuint64_t)p.T};
+  if (s_row <= 0 || s_t <= 0 || s_b <= 0 || s_row % 4 || s_t % 4 || s_b % 4) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)row_floats, (cuuint64_t)rows, (cuuint64_t)p.T,
+                        (cuuint64_t)p.Bsz};
+  cuuint64_t strides[3] = {(cuuint64_t)s_row * 4u, (cuuint64_t)s_t * 4u, (cuuint64_t)s_b * 4u};
   cuuint32_t box[4] = {32u, 1u, 64u, 1u};
   cuuint32_t es[4] = {1u, 1u, 1u, 1u};
   const CUresult rc = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, es,
@@ -540,7 +574,7 @@ bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int ro
 
 bool fwd_supported(const Problem& p) {
   if (p.D != 64 || p.N != 64 || p.x_complex) return false;
-  if (!bc_tma_ok(p.Bm, p.bs) || !bc_tma_ok(p.Cm, p.cs)) return false;
+  if (!bc_tma_ok(p, p.Bm, p.bs) || !bc_tma_ok(p, p.Cm, p.cs)) return false;
   const long long total = (long long)p.Bsz * p.H * ((p.T + 63) / 64);
   return total < (1ll << 30);
 }
@@ -582,11 +616,12 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaFuncSetAttribute(k_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kSmemBytes) != cudaSuccess)
+  auto kern = p.bc_planar ? k_fwd_tc<true> : k_fwd_tc<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+      cudaSuccess)
     return M3SSD_ERR_LAUNCH;
   const int grid = fp.total < 2 * sms ? fp.total : 2 * sms;
-  k_fwd_tc<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmY, fp);
+  kern<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmY, fp);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }
 

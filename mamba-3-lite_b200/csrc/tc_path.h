@@ -30,13 +30,19 @@ size_t chunk_prep_bytes(const Problem& p);
 int run_chunk_prep(const Problem& p, ChunkRec* out, cudaStream_t st);
 
 // TMA descriptor for a (B, T, H, N) complex64 tensor viewed as (B, T, H, 2N) fp32, box of
-// 64 time steps x 2N floats of one head (zero fill past T)
+// 64 time steps x 2N floats of one head (zero fill past T); for planar B / C (p.bc_planar) a
+// (B, T, 2H, N) fp32 view whose rows h and H + h are the real and imaginary parts of head h, box
+// of 64 time steps x N floats
 bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
                           const long long st[4]);
 // 4D map over a contiguous (B, T, H, row_floats) fp32 output for TMA stores of 64-row tiles in
 // 32-float (128-byte) column segments, 128-byte swizzled in shared memory. False if the pointer
 // is not 16-byte aligned.
 bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int row_floats);
+// the same over a strided (B, T, rows, row_floats) fp32 output: strides of a row, a time step and
+// a batch entry in floats, each a multiple of 4. False for a misaligned pointer or stride.
+bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int row_floats,
+                            int rows, long long s_row, long long s_t, long long s_b);
 
 // head_dim = state_dim = 64, real x, B/C with contiguous state dim and 16-byte aligned strides
 bool fwd_supported(const Problem& p);
@@ -48,8 +54,23 @@ bool bwd_supported(const Problem& p);
 // tc_selftest.cu: the bounded waits give up and report (status word in the first 256 bytes of ws)
 int run_selftest_waits(void* ws, cudaStream_t st);
 size_t bwd_workspace_bytes(const Problem& p);
+
+// Where the backward writes its gradients. Contiguous (B, T, H, ...) tensors by default; the
+// in_proj form (planar = 1) writes dx, dB, dC, ddt into one (B, T, H(D + 4N + 1)) fp32 gradient of
+// the projection, strides s_b, s_t in floats, with dB and dC planar (Re, then Im H*N floats on).
+struct BwdOut {
+  float* dx;
+  float2* dA;
+  float* dB;      // real parts (planar) or interleaved complex64
+  float* dC;
+  float* ddt;
+  int planar;
+  long long s_b, s_t;  // planar: strides of the projection gradient (floats)
+};
+BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, float2* dC,
+                          float* ddt);
 int run_bwd(const Problem& p, const float* dy, const long long dys[4], const void* states,
-            float* dx, float2* dA, float2* dB, float2* dC, float* ddt, void* ws, cudaStream_t st);
+            const BwdOut& out, void* ws, cudaStream_t st);
 
 }  // namespace tc
 }  // namespace m3ssd

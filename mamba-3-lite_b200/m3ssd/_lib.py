@@ -59,6 +59,29 @@ class BwdArgs(ctypes.Structure):
                 ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
 
 
+I64x2 = ctypes.c_int64 * 2
+
+
+class ProjFwdArgs(ctypes.Structure):
+    _fields_ = [("prob", Problem),
+                ("proj", ctypes.c_void_p), ("proj_strides", I64x2),
+                ("A", ctypes.c_void_p),
+                ("y", ctypes.c_void_p),
+                ("states", ctypes.c_void_p),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+
+
+class ProjBwdArgs(ctypes.Structure):
+    _fields_ = [("prob", Problem),
+                ("proj", ctypes.c_void_p), ("proj_strides", I64x2),
+                ("A", ctypes.c_void_p),
+                ("dy", ctypes.c_void_p), ("dy_strides", I64x4),
+                ("states", ctypes.c_void_p),
+                ("dproj", ctypes.c_void_p), ("dproj_strides", I64x2),
+                ("dA", ctypes.c_void_p),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+
+
 # every symbol include/m3ssd.h declares, with its ctypes signature
 SIGNATURES = {
     "m3ssd_abi_version": (ctypes.c_int, []),
@@ -73,6 +96,8 @@ SIGNATURES = {
     "m3ssd_bwd_path": (ctypes.c_char_p, [ctypes.POINTER(Problem)]),
     "m3ssd_launch_count": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.c_int]),
     "m3ssd_fwd_static_scratch": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
+    "m3ssd_fwd_proj": (ctypes.c_int, [ctypes.POINTER(ProjFwdArgs), ctypes.c_void_p]),
+    "m3ssd_bwd_proj": (ctypes.c_int, [ctypes.POINTER(ProjBwdArgs), ctypes.c_void_p]),
     "m3ssd_selftest_bounded_waits": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t,
                                                     ctypes.c_void_p]),
 }

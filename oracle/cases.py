@@ -115,3 +115,34 @@ def make_case(name):
     Bsz, T, H, D = inp["x"].shape
     dy = upstream_grad(kw["seed"], Bsz, T, H, D)
     return inp, dy, chunk
+
+
+# ------------------------------------------------------------------ in_proj form of the inputs
+def proj_inputs(seed, B, T, H, D, N, dt_mode="raw"):
+    """(proj, A): block-shape draws (``block_inputs``) laid out as the block's in_proj output,
+    columns x | Re B | Im B | Re C | Im C | dt (models/mamba_block.py:74-84)."""
+    inp = block_inputs(seed, B, T, H, D, N, dt_mode=dt_mode)
+    hn = H * N
+    proj = np.concatenate([
+        inp["x"].reshape(B, T, H * D),
+        inp["B_t"].real.reshape(B, T, hn), inp["B_t"].imag.reshape(B, T, hn),
+        inp["C_t"].real.reshape(B, T, hn), inp["C_t"].imag.reshape(B, T, hn),
+        inp["dt"].reshape(B, T, H)], axis=-1).astype(np.float32)
+    return np.ascontiguousarray(proj), inp["A"]
+
+
+# name -> (proj_inputs kwargs, chunk size)
+PROJ_CASES = {
+    "proj_small":  (dict(seed=41, B=2, T=20, H=2, D=8, N=8), 8),
+    "proj_block":  (dict(seed=42, B=1, T=160, H=4, D=64, N=64), 64),
+}
+PROJ_SAMPLED = ("proj_block",)
+
+
+def make_proj_case(name):
+    """Return (proj, A, dy, chunk, (H, D, N)) for a named in_proj case."""
+    kw, chunk = PROJ_CASES[name]
+    proj, A = proj_inputs(**kw)
+    H, D, N = kw["H"], kw["D"], kw["N"]
+    dy = upstream_grad(kw["seed"], kw["B"], kw["T"], H, D)
+    return proj, A, dy, chunk, (H, D, N)

@@ -4,6 +4,10 @@ Run from the repository root in a container where the reference checkout is pres
 
     python tests/golden/make_golden.py --reference /root/reference
 
+For every in_proj case (``PROJ_CASES`` in ``oracle/cases.py``) it runs the reference block's own
+unpacking of its in_proj output and the operator call inside it (models/mamba_block.py:73-104), and
+records the unpacked operands, y, and the gradients of proj and A (see ``run_reference_block``).
+
 For every case in ``oracle/cases.py`` it runs the reference's own ``ssd_complex_chunkwise``
 (models/ssd_complex.py:58-119, ``ssd_dispatch="pytorch"``) on CPU, backpropagates
 ``sum(dy * y)`` through it with torch.autograd, and stores outputs and gradients. Small cases store
@@ -25,7 +29,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from oracle.cases import CASES, SAMPLED_CASES, make_case  # noqa: E402
+from oracle.cases import (CASES, PROJ_CASES, PROJ_SAMPLED, SAMPLED_CASES,  # noqa: E402
+                          make_case, make_proj_case)
 
 N_SAMPLE = 4096
 
@@ -48,6 +53,81 @@ def run_reference(ssd_complex_chunkwise, inp, dy, chunk):
     return out
 
 
+def run_reference_block(proj_np, A_np, dy, chunk, dims):
+    """The reference block's own SSD input path on a given projection.
+
+    A Mamba3Block (models/mamba_block.py) whose in_proj returns `proj` runs its forward; the
+    operator call inside it (models/mamba_block.py:100-104) is wrapped to record its arguments and
+    result. The gradient of sum(dy * y) is then taken with respect to proj and A through the
+    block's slicing and torch.complex (:73-84) and the reference operator.
+    """
+    import torch.nn as nn
+    import models.mamba_block as mb  # the reference itself
+
+    H, D, N = dims
+    cfg = dict(d_model=16, n_heads=H, head_dim=D, state_dim=N, chunk_size=chunk, ffn_dim=32)
+    block = mb.Mamba3Block(cfg)
+    proj = torch.from_numpy(proj_np.copy()).requires_grad_(True)
+
+    class FixedProj(nn.Module):
+        def forward(self, h):
+            return proj
+
+    block.in_proj = FixedProj()
+    with torch.no_grad():
+        block.A.copy_(torch.from_numpy(A_np))
+    seen = {}
+    original = mb.ssd_complex_chunkwise
+
+    def recording(x_ssm, A, B_t, C_t, dt, **kw):
+        y = original(x_ssm, A, B_t, C_t, dt, **kw)
+        seen.update(x=x_ssm, B_t=B_t, C_t=C_t, dt=dt, y=y)
+        return y
+
+    mb.ssd_complex_chunkwise = recording
+    try:
+        block._forward_impl(torch.zeros(proj.shape[0], proj.shape[1], 16))
+    finally:
+        mb.ssd_complex_chunkwise = original
+    y = seen["y"]
+    dproj, dA = torch.autograd.grad((y * torch.from_numpy(dy)).sum(), [proj, block.A])
+    out = {"y": y.detach().numpy(), "dproj": dproj.numpy(), "dA": dA.numpy()}
+    unpacked = {k: seen[k].detach().numpy() for k in ("x", "B_t", "C_t", "dt")}
+    return out, unpacked
+
+
+def make_proj_fixtures(only):
+    for name in PROJ_CASES:
+        if only and name not in only:
+            continue
+        proj, A, dy, chunk, dims = make_proj_case(name)
+        ref, unpacked = run_reference_block(proj, A, dy, chunk, dims)
+        rec = {"chunk": np.int64(chunk), "dims": np.array(dims, np.int64),
+               "sum_proj": checksum(proj), "sum_dy": checksum(dy), "sum_A": checksum(A)}
+        if name in PROJ_SAMPLED:
+            rng = np.random.Generator(np.random.PCG64(4321))
+            for k, v in ref.items():
+                v = np.asarray(v)
+                idx = (np.sort(rng.choice(v.size, N_SAMPLE, replace=False)).astype(np.int64)
+                       if v.size > N_SAMPLE else np.arange(v.size, dtype=np.int64))
+                rec["idx_" + k] = idx
+                rec[k] = v.reshape(-1)[idx]
+                rec["nonfinite_" + k] = np.float64(np.mean(~np.isfinite(v)))
+        else:
+            rec["in_proj"] = proj
+            rec["in_A"] = A
+            rec["in_dy"] = dy
+            for k, v in unpacked.items():
+                rec["unpacked_" + k] = v
+            for k, v in ref.items():
+                rec[k] = v
+                rec["nonfinite_" + k] = np.float64(np.mean(~np.isfinite(v)))
+        path = os.path.join(HERE, name + ".npz")
+        np.savez_compressed(path, **rec)
+        print(f"{name:16s} chunk={chunk:3d} nonfinite(y)={rec['nonfinite_y']:.3f} "
+              f"-> {os.path.getsize(path) / 1024:.1f} KiB")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -57,6 +137,7 @@ def main():
     from models.ssd_complex import ssd_complex_chunkwise  # the reference itself
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    make_proj_fixtures(args.only)
     for name in CASES:
         if args.only and name not in args.only:
             continue
