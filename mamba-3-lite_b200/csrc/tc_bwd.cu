@@ -739,11 +739,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4 re = src[0], im = src[1024];
             r4[i][0] = make_float4(re.x, im.x, re.y, im.y);
             r4[i][1] = make_float4(re.z, im.z, re.w, im.w);
+          } else if (stacked) {
+            // 32 bytes per thread: lanes 4-7 of each group of 8 read their second float4 first,
+            // so each 8-lane phase of a 128-bit load covers all 32 banks once
+            const float4* src = reinterpret_cast<const float4*>(smem + base) + (j >> 4) * 32 + 2 * (j & 15);
+            const int sw = (j >> 2) & 1;
+            const float4 a = src[sw], b = src[1 - sw];
+            r4[i][0] = sw ? b : a;
+            r4[i][1] = sw ? a : b;
           } else {
-            const float4* src = reinterpret_cast<const float4*>(smem + base) +
-                                (stacked ? (j >> 4) * 32 + 2 * (j & 15) : 2 * k * 256 + f);
+            const float4* src = reinterpret_cast<const float4*>(smem + base) + 2 * k * 256 + f;
             r4[i][0] = src[0];
-            r4[i][1] = src[stacked ? 1 : 256];
+            r4[i][1] = src[256];
           }
         }
         workers_sync();

@@ -282,12 +282,33 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// A probe that does not order anything by itself: pair a nonzero result with fence_acquire_gpu()
+// before reading what the flag publishes (relaxed load + fence = acquire). Unlike an acquire
+// load, the thread need not wait for the value until it uses it.
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acquire_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
 // Waits until the hand-off flag at f is nonzero (acquire, gpu scope). Gives up after kSpinLimit
 // polls and records kErrFlagWait in *err instead of hanging; returns whether the flag was seen.
 __device__ __forceinline__ bool flag_wait(const uint32_t* f, uint32_t* err) {
 #pragma unroll 1
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (ld_acquire_gpu(f) != 0u) return true;
+    __nanosleep(64);
+  }
+  atomicOr(err, kErrFlagWait);
+  return false;
+}
+// flag_wait with relaxed polls: the caller follows it with fence_acquire_gpu()
+__device__ __forceinline__ bool flag_wait_relaxed(const uint32_t* f, uint32_t* err) {
+#pragma unroll 1
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (ld_relaxed_gpu(f) != 0u) return true;
     __nanosleep(64);
   }
   atomicOr(err, kErrFlagWait);

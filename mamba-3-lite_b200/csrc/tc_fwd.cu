@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   if (ctrl && ticket < p.total) issue_tma(ticket);
   int yb = 0, yh = 0, yt0 = 0;  // (ctrl) output tile staged by the previous ticket
-  uint32_t h_probe = 0;         // (ctrl) H_z flag as seen at the start of the ticket
+  uint32_t h_probe = 0;         // (ctrl) H_z flag as seen halfway through the operand transform
 
   uint32_t iter = 0;
   while (ticket < p.total) {
@@ -198,9 +198,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       yb = b;
       yh = h;
       yt0 = t0;
-      // is H_z already published? (then its loads overlap the transform and first MMAs; the
-      // probe is stored to shared memory after the transform, by when it has returned)
-      h_probe = (z == 0) ? 1u : ld_acquire_gpu(p.flags + (long long)bh * p.nc + z);
     }
 
     // ---- TMA tiles of B and C land in the operand buffers; rotate and split them in place
@@ -221,9 +218,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             r4[it][0] = make_float4(re.x, im.x, re.y, im.y);
             r4[it][1] = make_float4(re.z, im.z, re.w, im.w);
           } else {
+            // 32 bytes per thread: lanes 4-7 of each group of 8 read their second float4 first,
+            // so each 8-lane phase of a 128-bit load covers all 32 banks once
             const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
-            r4[it][0] = *reinterpret_cast<const float4*>(src);
-            r4[it][1] = *reinterpret_cast<const float4*>(src + 4);
+            const int sw = (j >> 2) & 1;
+            const float4 a = *reinterpret_cast<const float4*>(src + 4 * sw);
+            const float4 b = *reinterpret_cast<const float4*>(src + 4 - 4 * sw);
+            r4[it][0] = sw ? b : a;
+            r4[it][1] = sw ? a : b;
           }
         }
         if (ctrl && tile == 0) bulk_wait_read_all();  // sXT (y staging) is rewritten below
@@ -255,6 +257,11 @@ __global__ void __launch_bounds__(kThreads, 2)
                           sb + OFF_BX + 16384u + ka * 8192u + swz(l, ch), v);
           }
         }
+        // is H_z already published? (then its loads overlap the first MMAs.) Probed as late as
+        // the probe's round trip still hides behind the rest of the transform: its value is
+        // stored to shared memory at the end of the transform
+        if (ctrl && tile == 0)
+          h_probe = (z == 0) ? 1u : ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
       }
       // x (hi, lo) and x~ = exp(rho_Gamma - rho_s) x, stacked over p
       const int s = tid >> 2, pg = tid & 3;
@@ -268,11 +275,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t c4 = 4u * (uint32_t)(pg & 1);
       split_store16(xtb + swz(s, c4 + 0), xtb + swz(s, c4 + 2), xt);
       split_store16(xtb + swz(s, c4 + 1), xtb + swz(s, c4 + 3), xt + 8);
-      if (ctrl) m.h_ready = (int)h_probe;
+      if (ctrl) {  // a published H_z is read by every thread after the barrier below
+        if (z > 0 && h_probe != 0u) fence_acquire_gpu();
+        m.h_ready = (int)h_probe;
+      }
     }
     fence_proxy_async_smem();
     __syncthreads();
     const bool h_early = m.h_ready != 0;
+    // not yet published at the probe: every thread looks again now (no barrier needed later: each
+    // thread orders its own H loads after its own observation of the flag)
+    uint32_t h_late = 1u;
+    if (z > 0 && !h_early) h_late = ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
 
     // ---- MMA batch 1: G = C'x B'x^T (M128 N64), S~^T = x~^T B'x (M128 N128)
     if (tid == 0) {
@@ -342,11 +356,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     // ---- H_z from the predecessor chunk (bounded wait on its release flag if not yet seen)
     if (z > 0 && !h_early) {
-      if (tid == 0) {
-        flag_wait(p.flags + (long long)bh * p.nc + z, p.err);
-        __threadfence();
-      }
-      __syncthreads();
+      if (h_late == 0u) flag_wait_relaxed(p.flags + (long long)bh * p.nc + z, p.err);
+      fence_acquire_gpu();
       const float4* src =
           reinterpret_cast<const float4*>(p.states + ((long long)bh * p.nc + z) * 64 * 128) + tid;
 #pragma unroll
@@ -437,7 +448,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_before_sync();
     __syncthreads();
     next = m.nxt;
-    // the barrier orders every thread's H stores before this gpu-scope release
+    // the barrier orders every thread's H stores before this gpu-scope release. Its fence costs
+    // the control thread's warp ~1 us wherever it is placed (measured: here, after the output
+    // epilogue, or with no loads of the warp in flight); here it also publishes H_{z+1} soonest.
     if (ctrl && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
 
     // ---- output y = Y1 + exp(rho_l) Y2 into the staging tile in sXT; the next ticket's B, C
