@@ -231,6 +231,25 @@ def run_proj_workload(args):
         y.backward(dy)
         return p.grad
 
+    dy16 = dy.to(torch.bfloat16)
+
+    def fused_bf16():  # y stored as bf16 by the kernels, its gradient read as bf16
+        p = proj.detach().requires_grad_(True)
+        a = A.detach().requires_grad_(True)
+        y = m3ssd.ssd_from_proj(p, a, H, D, N, chunk_size=CHUNK, precision=args.precision,
+                                y_dtype=torch.bfloat16)
+        y.backward(dy16)
+        return p.grad
+
+    def composed_bf16():  # the cast autocast applies in front of MIMO (models/mimo.py:27)
+        p = proj.detach().requires_grad_(True)
+        a = A.detach().requires_grad_(True)
+        x, Bt, Ct, dt = m3ssd.unpack_proj(p, H, D, N)
+        y = m3ssd.ssd_complex_chunkwise(x, a, Bt, Ct, dt, chunk_size=CHUNK,
+                                        precision=args.precision).to(torch.bfloat16)
+        y.backward(dy16)
+        return p.grad
+
     def timed(fn):
         for _ in range(args.warmup):
             fn()
@@ -249,9 +268,12 @@ def run_proj_workload(args):
     time.sleep(0.3)
     ms_fused = timed(fused)
     ms_composed = timed(composed)
+    ms_fused16 = timed(fused_bf16)
+    ms_composed16 = timed(composed_bf16)
     clocks = sampler.stop()
     os.environ["M3SSD_CHECK"] = "1"
     same = bool(torch.equal(fused(), composed()))
+    same16 = bool(torch.equal(fused_bf16(), composed_bf16()))
     torch.cuda.synchronize()
     os.environ["M3SSD_CHECK"] = "0"
     tokens = B * T
@@ -272,6 +294,15 @@ def run_proj_workload(args):
                              "autograd through the slices"},
         "speedup_vs_composed": ms_composed / ms_fused,
         "dproj_bitwise_equal": same,
+        "bf16_readout": {"what": "y in bf16 (the dtype MIMO consumes under autocast): stored as "
+                                 "bf16 by the kernels and its gradient read as bf16, vs the "
+                                 "composition followed by y.to(bfloat16)",
+                         "fused": {"value": tokens / (ms_fused16 / 1e3) / 1e6,
+                                   "ms_per_step": ms_fused16},
+                         "composed": {"value": tokens / (ms_composed16 / 1e3) / 1e6,
+                                      "ms_per_step": ms_composed16},
+                         "speedup_vs_composed": ms_composed16 / ms_fused16,
+                         "dproj_bitwise_equal": same16},
         "roofline": {"bound": "hbm", "kernel": "fwd+bwd step (fused)",
                      "achieved": step_bytes / (ms_fused / 1e3) / 1e9, "peak": peak,
                      "unit": "GB/s", "frac": step_bytes / (ms_fused / 1e3) / 1e9 / peak,

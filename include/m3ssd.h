@@ -71,6 +71,12 @@ typedef enum m3ssd_status {
 #define M3SSD_PREC_TENSOR    0x20u  /* tcgen05 tensor-core tiles where the shape has them:
                                        split-bf16 operands (hi + lo), fp32 accumulation */
 #define M3SSD_PREC_MASK      0x30u
+#define M3SSD_Y_BF16         0x100u /* y (forward output) and dy (backward input) are bfloat16
+                                       instead of float32: the output is rounded to nearest-even
+                                       once, in the store; dy is widened exactly on load. For the
+                                       block, whose next op (MIMO, models/mimo.py:27) runs in bf16
+                                       under autocast. Tensor-core path only: with any other path
+                                       the calls return M3SSD_ERR_SHAPE. */
 
 typedef struct m3ssd_problem {
   int64_t batch;      /* B */
@@ -80,7 +86,7 @@ typedef struct m3ssd_problem {
   int64_t dstate;     /* N */
   int64_t chunk;      /* chunk length C (problems the tensor-core path can take are blocked
                          at 64 internally; the result does not depend on the blocking) */
-  uint32_t flags;     /* M3SSD_X_COMPLEX | one M3SSD_PREC_* */
+  uint32_t flags;     /* M3SSD_X_COMPLEX | one M3SSD_PREC_* | M3SSD_Y_BF16 */
   uint32_t reserved;  /* must be 0 */
 } m3ssd_problem;
 
@@ -91,7 +97,8 @@ typedef struct m3ssd_fwd_args {
   const void* B;   int64_t b_strides[4];   /* (B,T,H,N) complex64 */
   const void* C;   int64_t c_strides[4];   /* (B,T,H,N) complex64 */
   const float* dt; int64_t dt_strides[3];  /* (B,T,H) float32, pre-softplus */
-  float* y;                                /* out: (B,T,H,D) float32 contiguous */
+  void* y;                                 /* out: (B,T,H,D) float32 contiguous (bfloat16 with
+                                              M3SSD_Y_BF16) */
   void* states;                            /* out: m3ssd_states_bytes() bytes; chunk-entry states
                                               kept for m3ssd_bwd (layout internal) */
   void* workspace;                         /* scratch, m3ssd_fwd_workspace_bytes() bytes */
@@ -105,7 +112,8 @@ typedef struct m3ssd_bwd_args {
   const void* B;   int64_t b_strides[4];
   const void* C;   int64_t c_strides[4];
   const float* dt; int64_t dt_strides[3];
-  const float* dy; int64_t dy_strides[4];  /* (B,T,H,D) float32: gradient of y */
+  const void* dy; int64_t dy_strides[4];   /* (B,T,H,D) float32 (bfloat16 with M3SSD_Y_BF16):
+                                              gradient of y */
   const void* states;                      /* from the matching m3ssd_fwd call */
   void* dx;                                /* out: (B,T,H,D) float32 (complex64 if X_COMPLEX) */
   void* dA;                                /* out: (H,) complex64 */
@@ -194,7 +202,8 @@ typedef struct m3ssd_proj_fwd_args {
   m3ssd_problem prob;
   const float* proj; int64_t proj_strides[2];  /* (B, T, H(D+4N+1)) fp32; strides of b, t */
   const void* A;                               /* (H,) complex64 */
-  float* y;                                    /* out: (B,T,H,D) float32 contiguous */
+  void* y;                                     /* out: (B,T,H,D) float32 (bfloat16 with
+                                                  M3SSD_Y_BF16) contiguous */
   void* states;                                /* out: as m3ssd_fwd */
   void* workspace;
   size_t workspace_bytes;
@@ -204,7 +213,8 @@ typedef struct m3ssd_proj_bwd_args {
   m3ssd_problem prob;                          /* identical to the forward call */
   const float* proj; int64_t proj_strides[2];
   const void* A;
-  const float* dy; int64_t dy_strides[4];      /* (B,T,H,D) float32: gradient of y */
+  const void* dy; int64_t dy_strides[4];       /* (B,T,H,D) float32 (bfloat16 with
+                                                  M3SSD_Y_BF16): gradient of y */
   const void* states;                          /* from the matching m3ssd_fwd_proj / m3ssd_fwd */
   float* dproj; int64_t dproj_strides[2];      /* out: (B, T, H(D+4N+1)) fp32, proj's layout */
   void* dA;                                    /* out: (H,) complex64 */

@@ -25,7 +25,7 @@ bool mul_ok(int64_t a, int64_t b, int64_t* out) {
 int check_problem(const m3ssd_problem* pr) {
   if (!pr) return M3SSD_ERR_NULL;
   if (pr->reserved != 0) return M3SSD_ERR_FLAGS;
-  const uint32_t known = M3SSD_X_COMPLEX | M3SSD_PREC_MASK;
+  const uint32_t known = M3SSD_X_COMPLEX | M3SSD_PREC_MASK | M3SSD_Y_BF16;
   if (pr->flags & ~known) return M3SSD_ERR_FLAGS;
   if ((pr->flags & M3SSD_PREC_MASK) == M3SSD_PREC_MASK) return M3SSD_ERR_FLAGS;
   if (pr->batch <= 0 || pr->seqlen <= 0 || pr->nheads <= 0 || pr->headdim <= 0 || pr->dstate <= 0)
@@ -42,6 +42,11 @@ int check_problem(const m3ssd_problem* pr) {
   if (!mul_ok(bh, nc, &t1) || !mul_ok(t1, pr->dstate * pr->headdim, &t2) || !mul_ok(t2, 8, &t2))
     return M3SSD_ERR_OVERFLOW;
   if (!mul_ok(t1, pr->chunk * pr->chunk, &t2) || !mul_ok(t2, 16, &t2)) return M3SSD_ERR_OVERFLOW;
+  // a bf16 y is written (and its gradient read) only by the tensor-core kernels
+  if ((pr->flags & M3SSD_Y_BF16) &&
+      !(pr->headdim == 64 && pr->dstate == 64 && !(pr->flags & M3SSD_X_COMPLEX) &&
+        (pr->flags & M3SSD_PREC_MASK) != M3SSD_PREC_FP32))
+    return M3SSD_ERR_SHAPE;
   return M3SSD_OK;
 }
 
@@ -64,6 +69,7 @@ Problem make_problem(const m3ssd_problem* pr) {
   p.C = (int)pr->chunk;
   p.nc = (int)((pr->seqlen + pr->chunk - 1) / pr->chunk);
   p.x_complex = (pr->flags & M3SSD_X_COMPLEX) ? 1 : 0;
+  p.y_bf16 = (pr->flags & M3SSD_Y_BF16) ? 1 : 0;
   if (tc_shape(pr)) {
     p.C = m3ssd::tc::kChunk;
     p.nc = (int)((pr->seqlen + p.C - 1) / p.C);
@@ -281,7 +287,8 @@ int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
     if (!aligned(a->y, 16)) return M3SSD_ERR_ALIGN;
     return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream));
   }
-  return m3ssd::simt::run_fwd(p, a->y, a->states, a->workspace,
+  if (p.y_bf16) return M3SSD_ERR_SHAPE;  // B / C strides the tensor-core path cannot take
+  return m3ssd::simt::run_fwd(p, static_cast<float*>(a->y), a->states, a->workspace,
                               static_cast<cudaStream_t>(stream));
 }
 
@@ -296,7 +303,8 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   if (!a->dy || !a->states || !a->dx || !a->dA || !a->dB || !a->dC || !a->ddt)
     return M3SSD_ERR_NULL;
   const size_t xa = p.x_complex ? 8 : 4;
-  if (!aligned(a->dy, 4) || !aligned(a->states, 16) || !aligned(a->dx, xa) || !aligned(a->dA, 8) ||
+  if (!aligned(a->dy, p.y_bf16 ? 2 : 4) || !aligned(a->states, 16) || !aligned(a->dx, xa) ||
+      !aligned(a->dA, 8) ||
       !aligned(a->dB, 8) || !aligned(a->dC, 8) || !aligned(a->ddt, 4))
     return M3SSD_ERR_ALIGN;
   const size_t need = bwd_ws(p);
@@ -317,7 +325,9 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
     return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
                               static_cast<cudaStream_t>(stream));
   }
-  return m3ssd::simt::run_bwd(p, a->dy, dys, a->states, a->dx, static_cast<float2*>(a->dA),
+  if (p.y_bf16) return M3SSD_ERR_SHAPE;
+  return m3ssd::simt::run_bwd(p, static_cast<const float*>(a->dy), dys, a->states, a->dx,
+                              static_cast<float2*>(a->dA),
                               static_cast<float2*>(a->dB), static_cast<float2*>(a->dC), a->ddt,
                               a->workspace, static_cast<cudaStream_t>(stream));
 }
@@ -367,7 +377,8 @@ int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* a, void* stream) {
   int rc = proj_problem(&a->prob, a->proj, a->proj_strides, a->A, &p);
   if (rc) return rc;
   if (!a->dy || !a->states || !a->dproj || !a->dA) return M3SSD_ERR_NULL;
-  if (!aligned(a->dy, 4) || !aligned(a->states, 16) || !aligned(a->dA, 8)) return M3SSD_ERR_ALIGN;
+  if (!aligned(a->dy, p.y_bf16 ? 2 : 4) || !aligned(a->states, 16) || !aligned(a->dA, 8))
+    return M3SSD_ERR_ALIGN;
   // dproj: same conditions as proj (its column blocks leave through TMA stores)
   const int64_t sb = a->dproj_strides[0], st = a->dproj_strides[1];
   if (sb <= 0 || st <= 0) return M3SSD_ERR_SHAPE;

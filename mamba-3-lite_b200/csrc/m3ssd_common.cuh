@@ -56,6 +56,8 @@ struct Problem {
   // planar fp32, real parts at Bm / Cm (read as float), imaginary parts H*N floats further;
   // bs / cs then count floats. Only the tensor-core kernels take this form.
   int bc_planar;
+  // y (forward output) and dy (backward input) in bfloat16 (M3SSD_Y_BF16); tensor-core path only
+  int y_bf16;
   __host__ __device__ __forceinline__ long long Tp() const { return (long long)nc * C; }
 };
 

@@ -79,9 +79,10 @@ struct BwdParams {
   const float* x;
   long long xs[4];
   int x_vec;
-  const float* dy;
+  const void* dy;  // float32, or bfloat16 with dy_bf16
   long long dys[4];
   int dy_vec;
+  int dy_bf16;
   const float2* A;
   const float2* Bm;
   long long bs[4];
@@ -179,6 +180,31 @@ static __device__ __noinline__ void ctl_store_tile(const CUtensorMap* map, uint8
                  hp > 0 ? 32 * (seg & 1) : 32 * seg, hp > 0 ? q.h + hp * (seg >> 1) : q.h,
                  q.z * 64, q.b);
   bulk_commit_group();
+}
+
+// 8 consecutive bfloat16 values widened to float (zeros past the end of the sequence)
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* base, long long pstride, int vec,
+                                           bool valid, int p0, float* v) {
+  if (!valid) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    return;
+  }
+  if (vec) {
+    uint4 q;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                 : "l"(base + p0));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(base[(long long)(p0 + i) * pstride]);
+  }
 }
 
 // 8 consecutive floats x[b, t, h, p0 .. p0+7] (zeros past the end of the sequence)
@@ -564,8 +590,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (tx < p.T) {
             prefetch_l2_line(p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2] +
                              (long long)xp0 * p.xs[3]);
-            prefetch_l2_line(p.dy + qx.b * p.dys[0] + (long long)tx * p.dys[1] + qx.h * p.dys[2] +
-                             (long long)xp0 * p.dys[3]);
+            const long long go = qx.b * p.dys[0] + (long long)tx * p.dys[1] +
+                                 qx.h * p.dys[2] + (long long)xp0 * p.dys[3];
+            prefetch_l2_line(static_cast<const char*>(p.dy) + go * (p.dy_bf16 ? 2 : 4));
           }
         }
       };
@@ -693,9 +720,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const int tx = t0 + xs0;
         const float* xr = p.x + q.b * p.xs[0] + (long long)tx * p.xs[1] + q.h * p.xs[2];
-        const float* gr = p.dy + q.b * p.dys[0] + (long long)tx * p.dys[1] + q.h * p.dys[2];
+        const long long go = q.b * p.dys[0] + (long long)tx * p.dys[1] + q.h * p.dys[2];
         load8(xr, p.xs[3], p.x_vec, tx < p.T, xp0, xv);
-        load8(gr, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
+        if (p.dy_bf16)
+          load8_bf16(static_cast<const __nv_bfloat16*>(p.dy) + go, p.dys[3], p.dy_vec, tx < p.T,
+                     xp0, gv);
+        else
+          load8(static_cast<const float*>(p.dy) + go, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
       }
       mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // C tile, decay record
 
@@ -949,7 +980,7 @@ BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, f
   return o;
 }
 
-int run_bwd(const Problem& p, const float* dy, const long long dys[4], const void* states,
+int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
             const BwdOut& out, void* ws, cudaStream_t st) {
   const BwdLayout L = bwd_layout(p);
   BwdParams bp{};
@@ -965,8 +996,11 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
                  ? 1
                  : 0;
   bp.dy = dy;
+  bp.dy_bf16 = p.y_bf16;
   for (int i = 0; i < 4; ++i) bp.dys[i] = dys[i];
-  bp.dy_vec = (dys[3] == 1 && dys[0] % 4 == 0 && dys[1] % 4 == 0 && dys[2] % 4 == 0 &&
+  // 8 values (32 or 16 bytes) per vector load
+  const long long dv = p.y_bf16 ? 8 : 4;
+  bp.dy_vec = (dys[3] == 1 && dys[0] % dv == 0 && dys[1] % dv == 0 && dys[2] % dv == 0 &&
                reinterpret_cast<uintptr_t>(dy) % 16 == 0)
                   ? 1
                   : 0;

@@ -70,6 +70,7 @@ struct FwdParams {
   uint32_t* flags;
   uint32_t* counter;
   uint32_t* err;
+  int y_bf16;  // y leaves as bfloat16 (one 64-column staging segment) instead of float32 (two)
 };
 
 __device__ __forceinline__ void load_x16(const FwdParams& p, int b, int t, int h, int p0,
@@ -190,9 +191,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();  // previous ticket done: its MMAs completed, its y tile staged
     int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
     if (ctrl) {
-      if (iter > 0) {  // the previous ticket's y: two 32-column segments from sXT
+      if (iter > 0) {  // the previous ticket's y: two 32-column fp32 segments (one bf16) from sXT
         tma_store_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb);
-        tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
+        if (!p.y_bf16) tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
         bulk_commit_group();
       }
       yb = b;
@@ -478,12 +479,25 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float a2 = (part ? y2[16 + c] : y2[c]) + r2;
         out[c] = a1 + el_r * a2;
       }
-      const uint32_t seg = sb + OFF_XT + (uint32_t)wg * 8192u;
+      if (p.y_bf16) {  // columns 32 wg + 16 part .. +15 = 16-byte chunks 4 wg + 2 part, +1
+        uint32_t w[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        st_shared_v4(stage_addr(seg, (uint32_t)r, (uint32_t)(4 * part + i)),
-                     make_uint4(__float_as_uint(out[4 * i]), __float_as_uint(out[4 * i + 1]),
-                                __float_as_uint(out[4 * i + 2]), __float_as_uint(out[4 * i + 3])));
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 v2 = __floats2bfloat162_rn(out[2 * i], out[2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&v2);
+        }
+        const uint32_t c0 = 4u * (uint32_t)wg + 2u * (uint32_t)part;
+        st_shared_v4(stage_addr(sb + OFF_XT, (uint32_t)r, c0), make_uint4(w[0], w[1], w[2], w[3]));
+        st_shared_v4(stage_addr(sb + OFF_XT, (uint32_t)r, c0 + 1u),
+                     make_uint4(w[4], w[5], w[6], w[7]));
+      } else {
+        const uint32_t seg = sb + OFF_XT + (uint32_t)wg * 8192u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          st_shared_v4(stage_addr(seg, (uint32_t)r, (uint32_t)(4 * part + i)),
+                       make_uint4(__float_as_uint(out[4 * i]), __float_as_uint(out[4 * i + 1]),
+                                  __float_as_uint(out[4 * i + 2]), __float_as_uint(out[4 * i + 3])));
+      }
       fence_proxy_async_smem();
     }
     tc_fence_before_sync();
@@ -494,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (ctrl) {
     if (iter > 0) {  // the last ticket's y
       tma_store_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb);
-      tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
+      if (!p.y_bf16) tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
       bulk_commit_group();
     }
     bulk_wait_all();
@@ -569,6 +583,19 @@ bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int ro
   return encode_out_map_strided(map, ptr, p, row_floats, p.H, rf, rf * p.H, rf * p.H * p.T);
 }
 
+bool encode_out_map_bf16(CUtensorMap* map, void* ptr, const Problem& p) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (!encode || (reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
+  cuuint64_t dims[4] = {64u, (cuuint64_t)p.H, (cuuint64_t)p.T, (cuuint64_t)p.Bsz};
+  cuuint64_t strides[3] = {128u, 128u * (cuuint64_t)p.H, 128u * (cuuint64_t)p.H * (cuuint64_t)p.T};
+  cuuint32_t box[4] = {64u, 1u, 64u, 1u};
+  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  const CUresult rc = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, ptr, dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return rc == CUDA_SUCCESS;
+}
+
 bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int row_floats,
                             int rows, long long s_row, long long s_t, long long s_b) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
@@ -599,7 +626,7 @@ size_t fwd_workspace_bytes(const Problem& p) {
   return 256 + 4 * (size_t)p.Bsz * p.H * nc;
 }
 
-int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st) {
+int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st) {
   FwdParams fp{};
   fp.Bsz = p.Bsz;
   fp.T = p.T;
@@ -619,9 +646,10 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   fp.err = w;
   fp.counter = w + 1;
   fp.flags = w + 64;
+  fp.y_bf16 = p.y_bf16;
   CUtensorMap tmB, tmC, tmY;
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs) ||
-      !encode_out_tensor_map(&tmY, y, p, 64))
+      !(p.y_bf16 ? encode_out_map_bf16(&tmY, y, p) : encode_out_tensor_map(&tmY, y, p, 64)))
     return M3SSD_ERR_LAUNCH;
   if (cudaMemsetAsync(ws, 0, fwd_workspace_bytes(p), st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   const int rc = run_chunk_prep(p, recs, st);

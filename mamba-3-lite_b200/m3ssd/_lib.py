@@ -15,6 +15,7 @@ M3SSD_X_COMPLEX = 0x1
 M3SSD_PREC_AUTO = 0x0
 M3SSD_PREC_FP32 = 0x10
 M3SSD_PREC_TENSOR = 0x20
+M3SSD_Y_BF16 = 0x100
 
 STATUS_NAMES = {
     0: "OK", 1: "ERR_NULL", 2: "ERR_SHAPE", 3: "ERR_CHUNK", 4: "ERR_DIM_LIMIT", 5: "ERR_ALIGN",

@@ -25,6 +25,11 @@ Differences from the reference, all deliberate:
 * ``precision`` (extra keyword) selects "auto" (default, same as "tensor"), "fp32" (CUDA cores,
   fp32 everywhere) or "tensor" (tcgen05 tensor-core tiles with split-bf16 operands and fp32
   accumulation where the shape has them: head_dim = state_dim = 64, real x).
+* ``y_dtype`` (extra keyword): torch.float32 (default, the reference's output) or torch.bfloat16,
+  for the block whose next op (MIMO, models/mimo.py:27) runs in bf16 under autocast. The
+  tensor-core kernels then round y to bf16 in their store and read its gradient as bf16, which
+  saves the cast kernels autocast would run on both sides; y is bit-identical to
+  ``y_fp32.to(torch.bfloat16)``. Other shapes compute in fp32 and cast.
 """
 from __future__ import annotations
 
@@ -39,6 +44,10 @@ ctypes_ref = ctypes.byref
 
 _PREC = {"auto": _lib.M3SSD_PREC_AUTO, "fp32": _lib.M3SSD_PREC_FP32,
          "tensor": _lib.M3SSD_PREC_TENSOR}
+
+
+def _y_dtype(flags):
+    return torch.bfloat16 if flags & _lib.M3SSD_Y_BF16 else torch.float32
 
 
 def _problem(x, B_t, chunk, flags):
@@ -113,7 +122,7 @@ def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tens
     A = A.contiguous()
     prob = _problem(x, B_t, chunk, flags)
     _lib.check(lib.m3ssd_check_problem(ctypes_ref(prob)))
-    y = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    y = torch.empty(x.shape, dtype=_y_dtype(flags), device=dev)
     states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
                          device=dev)
     ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
@@ -139,7 +148,7 @@ def _(x, A, B_t, C_t, dt, chunk, flags):
     lib = _lib.load()
     prob = _problem(x, B_t, chunk, flags)
     nbytes = int(lib.m3ssd_states_bytes(ctypes_ref(prob)))
-    return (torch.empty(x.shape, dtype=torch.float32, device=x.device),
+    return (torch.empty(x.shape, dtype=_y_dtype(flags), device=x.device),
             torch.empty(nbytes, dtype=torch.uint8, device=x.device))
 
 
@@ -151,8 +160,8 @@ def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tenso
     lib = _lib.load()
     dev = x.device
     A = A.contiguous()
-    if dy.dtype != torch.float32:
-        dy = dy.float()
+    if dy.dtype != _y_dtype(flags):
+        dy = dy.to(_y_dtype(flags))
     prob = _problem(x, B_t, chunk, flags)
     dx = torch.empty(x.shape, dtype=x.dtype, device=dev)
     dA = torch.empty(A.shape, dtype=torch.complex64, device=dev)
@@ -203,7 +212,7 @@ def _setup_context(ctx, inputs, output):
 def _backward(ctx, dy, _dstates):
     x, A, B_t, C_t, dt, states = ctx.saved_tensors
     if dy is None:
-        dy = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
+        dy = torch.zeros(x.shape, dtype=_y_dtype(ctx.flags), device=x.device)
     dx, dA, dB, dC, ddt = ssd_bwd(dy, x, A, B_t, C_t, dt, states, ctx.chunk, ctx.flags)
     return dx, dA, dB, dC, ddt, None, None
 
@@ -213,16 +222,36 @@ ssd_fwd.register_autograd(_backward, setup_context=_setup_context)
 
 def ssd_complex_chunkwise(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
                           C_t: torch.Tensor, dt: torch.Tensor, chunk_size: int = 64,
-                          ssd_dispatch: str = "cuda", precision: str = "auto") -> torch.Tensor:
+                          ssd_dispatch: str = "cuda", precision: str = "auto",
+                          y_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Complex chunkwise SSD, forward and backward on the GPU (see the module docstring)."""
     del ssd_dispatch  # every dispatch value runs the CUDA kernels
     _check_inputs(x, A, B_t, C_t, dt, chunk_size)
     if precision not in _PREC:
         raise ValueError(f"precision must be one of {sorted(_PREC)}, got {precision!r}")
+    if y_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"y_dtype must be torch.float32 or torch.bfloat16, got {y_dtype}")
     flags = _PREC[precision] | (_lib.M3SSD_X_COMPLEX if x.dtype == torch.complex64 else 0)
+    bf16_in_kernel = y_dtype == torch.bfloat16 and _bf16_store_ok(x, B_t, C_t, flags)
+    if bf16_in_kernel:
+        flags |= _lib.M3SSD_Y_BF16
     with torch.autocast("cuda", enabled=False):
         y, _ = ssd_fwd(x, A, B_t, C_t, dt, int(chunk_size), int(flags))
-    return y
+    return y.to(y_dtype) if y.dtype != y_dtype else y
+
+
+def _bf16_store_ok(x, B_t, C_t, flags):
+    """The tensor-core path runs for this call (so the kernels can store y as bf16)."""
+    Bsz, T, H, D = x.shape
+    N = B_t.shape[-1]
+    if D != 64 or N != 64 or flags & (_lib.M3SSD_X_COMPLEX | _lib.M3SSD_PREC_FP32):
+        return False
+    # B / C operands through TMA: contiguous state dim, 16-byte aligned base and strides
+    for t in (B_t, C_t):
+        s = t.stride()
+        if s[3] != 1 or any(v % 2 for v in s[:3]) or t.data_ptr() % 16:
+            return False
+    return True
 
 
 def implementation(x_shape, N, chunk_size=64, complex_x=False, precision="auto"):

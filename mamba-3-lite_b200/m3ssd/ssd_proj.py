@@ -27,7 +27,8 @@ import ctypes
 import torch
 
 from . import _lib
-from .ssd_complex import (_PREC, _check_device_status, _stream_ptr, ssd_complex_chunkwise)
+from .ssd_complex import (_PREC, _check_device_status, _stream_ptr, _y_dtype,
+                          ssd_complex_chunkwise)
 
 ctypes_ref = ctypes.byref
 
@@ -81,7 +82,7 @@ def ssd_proj_fwd(proj: torch.Tensor, A: torch.Tensor, H: int, D: int, N: int, ch
     prob = _problem(proj, H, D, N, chunk, flags)
     _lib.check(lib.m3ssd_check_problem(ctypes_ref(prob)))
     Bsz, T, _ = proj.shape
-    y = torch.empty((Bsz, T, H, D), dtype=torch.float32, device=dev)
+    y = torch.empty((Bsz, T, H, D), dtype=_y_dtype(flags), device=dev)
     states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
                          device=dev)
     ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
@@ -105,7 +106,7 @@ def _(proj, A, H, D, N, chunk, flags):
     prob = _problem(proj, H, D, N, chunk, flags)
     nbytes = int(lib.m3ssd_states_bytes(ctypes_ref(prob)))
     Bsz, T, _ = proj.shape
-    return (torch.empty((Bsz, T, H, D), dtype=torch.float32, device=proj.device),
+    return (torch.empty((Bsz, T, H, D), dtype=_y_dtype(flags), device=proj.device),
             torch.empty(nbytes, dtype=torch.uint8, device=proj.device))
 
 
@@ -116,8 +117,8 @@ def ssd_proj_bwd(dy: torch.Tensor, proj: torch.Tensor, A: torch.Tensor, states: 
     lib = _lib.load()
     dev = proj.device
     A = A.contiguous()
-    if dy.dtype != torch.float32:
-        dy = dy.float()
+    if dy.dtype != _y_dtype(flags):
+        dy = dy.to(_y_dtype(flags))
     prob = _problem(proj, H, D, N, chunk, flags)
     dproj = torch.empty(proj.shape, dtype=torch.float32, device=dev)
     dA = torch.empty(A.shape, dtype=torch.complex64, device=dev)
@@ -159,7 +160,7 @@ def _backward(ctx, dy, _dstates):
     H, D, N, chunk, flags = ctx.dims
     if dy is None:
         Bsz, T, _ = proj.shape
-        dy = torch.zeros((Bsz, T, H, D), dtype=torch.float32, device=proj.device)
+        dy = torch.zeros((Bsz, T, H, D), dtype=_y_dtype(flags), device=proj.device)
     dproj, dA = ssd_proj_bwd(dy, proj, A, states, H, D, N, chunk, flags)
     return dproj, dA, None, None, None, None, None
 
@@ -168,8 +169,11 @@ ssd_proj_fwd.register_autograd(_backward, setup_context=_setup_context)
 
 
 def ssd_from_proj(proj: torch.Tensor, A: torch.Tensor, n_heads: int, head_dim: int,
-                  state_dim: int, chunk_size: int = 64, precision: str = "auto") -> torch.Tensor:
-    """y (B, T, H, D) float32 from the block's in_proj output (see the module docstring)."""
+                  state_dim: int, chunk_size: int = 64, precision: str = "auto",
+                  y_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """y (B, T, H, D) from the block's in_proj output (see the module docstring); float32, or
+    bfloat16 stored by the kernels themselves with ``y_dtype=torch.bfloat16`` (as
+    ``ssd_complex_chunkwise``)."""
     if not isinstance(proj, torch.Tensor) or not isinstance(A, torch.Tensor):
         raise TypeError("proj and A must be torch.Tensor")
     if proj.device.type != "cuda" or A.device.type != "cuda":
@@ -191,11 +195,14 @@ def ssd_from_proj(proj: torch.Tensor, A: torch.Tensor, n_heads: int, head_dim: i
         proj = proj.float()  # the block's .float() on every slice, done once
     elif proj.dtype != torch.float32:
         raise TypeError(f"proj must be float32, bfloat16 or float16, got {proj.dtype}")
+    if y_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"y_dtype must be torch.float32 or torch.bfloat16, got {y_dtype}")
     if not fusable(proj, H, D, N, precision):
         return ssd_complex_chunkwise(*_interleave(proj, A, H, D, N), chunk_size=chunk_size,
-                                     precision=precision)
+                                     precision=precision, y_dtype=y_dtype)
+    flags = _PREC[precision] | (_lib.M3SSD_Y_BF16 if y_dtype == torch.bfloat16 else 0)
     with torch.autocast("cuda", enabled=False):
-        y, _ = ssd_proj_fwd(proj, A, H, D, N, int(chunk_size), int(_PREC[precision]))
+        y, _ = ssd_proj_fwd(proj, A, H, D, N, int(chunk_size), int(flags))
     return y
 
 

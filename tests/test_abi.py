@@ -52,7 +52,11 @@ def test_strerror_covers_all_codes(lib):
     (dict(chunk=0), 3), (dict(chunk=257), 3),
     (dict(headdim=257), 4), (dict(dstate=300), 4),
     (dict(batch=0), 2), (dict(seqlen=-1), 2), (dict(nheads=0), 2),
-    (dict(flags=0x100), 9), (dict(flags=0x30), 9), (dict(reserved=1), 9),
+    (dict(flags=0x200), 9), (dict(flags=0x30), 9), (dict(reserved=1), 9),
+    # bf16 y: tensor-core shapes only
+    (dict(flags=0x100, headdim=64, dstate=64), 0), (dict(flags=0x100, headdim=32), 2),
+    (dict(flags=0x100 | 0x10, headdim=64, dstate=64), 2),
+    (dict(flags=0x100 | 0x1, headdim=64, dstate=64), 2),
     (dict(batch=70000, nheads=1), 2),
     (dict(seqlen=64 * 70000, chunk=64), 2),
     (dict(chunk=4, seqlen=20), 0), (dict(chunk=1, seqlen=3, headdim=1, dstate=1), 0),

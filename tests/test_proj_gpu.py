@@ -157,3 +157,32 @@ def test_fused_against_fp64_block_shape(m3, cuda_device):
     assert rel(y, y64.detach()) < tol["y_normwise"]
     assert rel(gp, p64.grad) < tol["g_normwise"]
     assert rel(ga, a64.grad) < tol["g_normwise"]
+
+
+@pytest.mark.parametrize("T,fused", [(2048, True), (200, True), (200, False)])
+def test_bf16_readout(m3, cuda_device, T, fused):
+    """y_dtype=bfloat16: the kernels round y in their store and read dy as bf16. y is bit-equal to
+    the fp32 result rounded, and the gradients equal those of the fp32 path fed the same (bf16)
+    upstream gradient."""
+    B, H = 2, 4
+    proj, A, dy = _case(cuda_device, B, T, H, seed=T)
+    dy16 = dy.to(torch.bfloat16)
+
+    def run(y_dtype, g):
+        p = proj.detach().clone().requires_grad_(True)
+        a = A.detach().clone().requires_grad_(True)
+        if fused:
+            y = m3.ssd_from_proj(p, a, H, 64, 64, y_dtype=y_dtype)
+            grads = lambda: (p.grad, a.grad)  # noqa: E731
+        else:
+            x, Bt, Ct, dt = m3.unpack_proj(p, H, 64, 64)
+            y = m3.ssd_complex_chunkwise(x, a, Bt, Ct, dt, y_dtype=y_dtype)
+            grads = lambda: (p.grad, a.grad)  # noqa: E731
+        y.backward(g)
+        return (y.detach(),) + grads()
+
+    y16, gp16, ga16 = run(torch.bfloat16, dy16)
+    y32, gp32, ga32 = run(torch.float32, dy16.float())
+    assert y16.dtype == torch.bfloat16
+    assert torch.equal(y16, y32.to(torch.bfloat16))
+    assert torch.equal(gp16, gp32) and torch.equal(ga16, ga32)
