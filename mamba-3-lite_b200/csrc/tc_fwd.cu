@@ -201,69 +201,70 @@ __global__ void __launch_bounds__(kThreads, 2)
       yt0 = t0;
     }
 
-    // ---- TMA tiles of B and C land in the operand buffers; rotate and split them in place
+    // ---- TMA tiles of B and C land in the operand buffers; rotate and split them in place:
+    // B first, then x and x~, so S~ = x~^T B'x runs on the tensor core while C is converted
     mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);
-    {
-      // one tile at a time: all raw values of the tile in registers, barrier, write in place
+    // all raw values of one tile in registers (each thread: rows j/16, complex 4 (j%16) .. +3 for
+    // j = tid + 256 it); written back in place after a barrier
+    auto read_tile = [&](uint32_t base, float4 (&r4)[4][2]) {
 #pragma unroll
-      for (int tile = 0; tile < 2; ++tile) {  // 0: C -> C'x (stacked), 1: B -> B'x hi | lo
-        const uint32_t base = tile ? OFF_BX : OFF_CX;
-        float4 r4[4][2];
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-          const int j = tid + kThreads * it;
-          if constexpr (kPlanar) {  // Re and Im of complex 4q .. 4q+3 of row l, interleaved here
-            const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 64 + 4 * (j & 15);
-            const float4 re = *reinterpret_cast<const float4*>(src);
-            const float4 im = *reinterpret_cast<const float4*>(src + 4096);
-            r4[it][0] = make_float4(re.x, im.x, re.y, im.y);
-            r4[it][1] = make_float4(re.z, im.z, re.w, im.w);
-          } else {
-            // 32 bytes per thread: lanes 4-7 of each group of 8 read their second float4 first,
-            // so each 8-lane phase of a 128-bit load covers all 32 banks once
-            const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
-            const int sw = (j >> 2) & 1;
-            const float4 a = *reinterpret_cast<const float4*>(src + 4 * sw);
-            const float4 b = *reinterpret_cast<const float4*>(src + 4 - 4 * sw);
-            r4[it][0] = sw ? b : a;
-            r4[it][1] = sw ? a : b;
-          }
+      for (int it = 0; it < 4; ++it) {
+        const int j = tid + kThreads * it;
+        if constexpr (kPlanar) {  // Re and Im of complex 4q .. 4q+3 of row l, interleaved here
+          const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 64 + 4 * (j & 15);
+          const float4 re = *reinterpret_cast<const float4*>(src);
+          const float4 im = *reinterpret_cast<const float4*>(src + 4096);
+          r4[it][0] = make_float4(re.x, im.x, re.y, im.y);
+          r4[it][1] = make_float4(re.z, im.z, re.w, im.w);
+        } else {
+          // 32 bytes per thread: lanes 4-7 of each group of 8 read their second float4 first,
+          // so each 8-lane phase of a 128-bit load covers all 32 banks once
+          const float* src = reinterpret_cast<const float*>(smem + base) + (j >> 4) * 128 + 8 * (j & 15);
+          const int sw = (j >> 2) & 1;
+          const float4 a = *reinterpret_cast<const float4*>(src + 4 * sw);
+          const float4 b = *reinterpret_cast<const float4*>(src + 4 - 4 * sw);
+          r4[it][0] = sw ? b : a;
+          r4[it][1] = sw ? a : b;
         }
-        if (ctrl && tile == 0) bulk_wait_read_all();  // sXT (y staging) is rewritten below
-        __syncthreads();
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-          const int j = tid + kThreads * it;
-          const int l = j >> 4, q = j & 15;
-          const float2 cs = m.rec.cis[l];
-          const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
-          const float rv[8] = {r4[it][0].x, r4[it][0].y, r4[it][0].z, r4[it][0].w,
-                               r4[it][1].x, r4[it][1].y, r4[it][1].z, r4[it][1].w};
-          float v[8];
-          if (tile == 0) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {  // C * cis(theta_l)
-              v[2 * u] = rv[2 * u] * cs.x - rv[2 * u + 1] * cs.y;
-              v[2 * u + 1] = rv[2 * u] * cs.y + rv[2 * u + 1] * cs.x;
-            }
-            split_store16(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 0), ch),
-                          sb + OFF_CX + ka * 16384u + swz(stack_row(l, 1), ch), v);
-          } else {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {  // conj(B * conj(cis(theta_s)))
-              v[2 * u] = rv[2 * u] * cs.x + rv[2 * u + 1] * cs.y;
-              v[2 * u + 1] = rv[2 * u] * cs.y - rv[2 * u + 1] * cs.x;
-            }
-            split_store16(sb + OFF_BX + ka * 8192u + swz(l, ch),
-                          sb + OFF_BX + 16384u + ka * 8192u + swz(l, ch), v);
-          }
-        }
-        // is H_z already published? (then its loads overlap the first MMAs.) Probed as late as
-        // the probe's round trip still hides behind the rest of the transform: its value is
-        // stored to shared memory at the end of the transform
-        if (ctrl && tile == 0)
-          h_probe = (z == 0) ? 1u : ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
       }
+    };
+    // tile 0: C -> C'x (stacked); tile 1: B -> B'x hi | lo
+    auto write_tile = [&](int tile, const float4 (&r4)[4][2]) {
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int j = tid + kThreads * it;
+        const int l = j >> 4, q = j & 15;
+        const float2 cs = m.rec.cis[l];
+        const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
+        const float rv[8] = {r4[it][0].x, r4[it][0].y, r4[it][0].z, r4[it][0].w,
+                             r4[it][1].x, r4[it][1].y, r4[it][1].z, r4[it][1].w};
+        float v[8];
+        if (tile == 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {  // C * cis(theta_l)
+            v[2 * u] = rv[2 * u] * cs.x - rv[2 * u + 1] * cs.y;
+            v[2 * u + 1] = rv[2 * u] * cs.y + rv[2 * u + 1] * cs.x;
+          }
+          split_store16(sb + OFF_CX + ka * 16384u + swz(stack_row(l, 0), ch),
+                        sb + OFF_CX + ka * 16384u + swz(stack_row(l, 1), ch), v);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {  // conj(B * conj(cis(theta_s)))
+            v[2 * u] = rv[2 * u] * cs.x + rv[2 * u + 1] * cs.y;
+            v[2 * u + 1] = rv[2 * u] * cs.y - rv[2 * u + 1] * cs.x;
+          }
+          split_store16(sb + OFF_BX + ka * 8192u + swz(l, ch),
+                        sb + OFF_BX + 16384u + ka * 8192u + swz(l, ch), v);
+        }
+      }
+    };
+    float4 rc[4][2];  // the raw C tile, read once B'x and x~ are written
+    {
+      float4 rb[4][2];
+      read_tile(OFF_BX, rb);
+      if (ctrl) bulk_wait_read_all();  // sXT (y staging) is rewritten below
+      __syncthreads();
+      write_tile(1, rb);
       // x (hi, lo) and x~ = exp(rho_Gamma - rho_s) x, stacked over p
       const int s = tid >> 2, pg = tid & 3;
       split_store16(sb + OFF_XH + swz(s, 2 * pg), sb + OFF_XL + swz(s, 2 * pg), xv);
@@ -276,10 +277,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t c4 = 4u * (uint32_t)(pg & 1);
       split_store16(xtb + swz(s, c4 + 0), xtb + swz(s, c4 + 2), xt);
       split_store16(xtb + swz(s, c4 + 1), xtb + swz(s, c4 + 3), xt + 8);
-      if (ctrl) {  // a published H_z is read by every thread after the barrier below
-        if (z > 0 && h_probe != 0u) fence_acquire_gpu();
-        m.h_ready = (int)h_probe;
-      }
+      read_tile(OFF_CX, rc);
+      // is H_z already published? (then its loads overlap the first MMAs.) Probed as late as
+      // the probe's round trip still hides behind the rest of the transform: its value is
+      // stored to shared memory at the end of the transform
+      if (ctrl) h_probe = (z == 0) ? 1u : ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {  // MMA batch 1a: S~^T = x~^T B'x (M128 N128)
+      tc_fence_after_sync();
+      const uint32_t idS = idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_S, sdesc(sb + OFF_XT + j * 2048u, 8192, 1024),
+                      sdesc(sb + OFF_BX + hl * 16384u + j * 2048u, 8192, 1024), idS,
+                      (hl | j) != 0);
+    }
+    write_tile(0, rc);
+    if (ctrl) {  // a published H_z is read by every thread after the barrier below
+      if (z > 0 && h_probe != 0u) fence_acquire_gpu();
+      m.h_ready = (int)h_probe;
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -289,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint32_t h_late = 1u;
     if (z > 0 && !h_early) h_late = ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
 
-    // ---- MMA batch 1: G = C'x B'x^T (M128 N64), S~^T = x~^T B'x (M128 N128)
+    // ---- MMA batch 1b: G = C'x B'x^T (M128 N64); the commit covers S~ too
     if (tid == 0) {
       tc_fence_after_sync();
       const uint32_t idG = idesc_bf16(128, 64, 0, 0);
@@ -300,14 +320,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           mma_bf16_ss(tmem + COL_G, sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
                       sdesc(sb + OFF_BX + hl * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024),
                       idG, (hl | j) != 0);
-      const uint32_t idS = idesc_bf16(128, 128, 1, 1);
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_S, sdesc(sb + OFF_XT + j * 2048u, 8192, 1024),
-                      sdesc(sb + OFF_BX + hl * 16384u + j * 2048u, 8192, 1024), idS,
-                      (hl | j) != 0);
       mma_commit(&m.bar_mma1);
     }
     float hz[32];
