@@ -33,7 +33,9 @@ namespace tc {
 namespace {
 
 constexpr int kWorkers = 512;              // warps 0-15: operand transforms and epilogues
-constexpr int kThreads = kWorkers + 32;    // warp 16: tickets, TMA/bulk loads, flags, MMA issue
+constexpr int kCtlWarp = kWorkers / 32;    // warp 16: tickets, TMA/bulk loads and stores, MMA issue
+constexpr int kRelWarp = kCtlWarp + 1;     // warp 17: publishes each ticket's dS hand-off
+constexpr int kThreads = kWorkers + 64;
 // shared memory map
 constexpr uint32_t OFF_C = 0;        // C'x stacked [2 k-atoms][128][64]; raw C tile lands first
 constexpr uint32_t OFF_B = 32768;    // B'x (conjugate-interleaved) stacked; raw B tile lands first
@@ -45,7 +47,7 @@ constexpr uint32_t OFF_DGM = 131072; // dG' stacked over s, MN [2][64 l][64]
 constexpr uint32_t OFF_DS = 147456;  // dS_z (fp32, lands by bulk copy), then dS'x hi | lo
 constexpr uint32_t OFF_H = 180224;   // H_z (fp32, lands by bulk copy), then conj(H_z) hi | lo
 constexpr uint32_t OFF_MISC = 212992;
-constexpr uint32_t kMiscBytes = 8192;
+constexpr uint32_t kMiscBytes = 9216;
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBytes + 1024;
 constexpr uint32_t kLoadBytes = 64u * 128u * 4u + (uint32_t)sizeof(ChunkRec);  // C tile + record
 constexpr uint32_t kTmemCols = 512;
@@ -68,7 +70,8 @@ struct Misc {
   float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
   float2 rc[4][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the four 16-state column groups
   float2 rb[4][64];  // sum_n dB'_{sn} conj(B'_{sn})
-  float2 dgp[kWorkers / 32];  // per-warp partials of <dS_{z-1}, H_z>
+  float2 dgp[2][kWorkers / 32];  // per-warp partials of <dS_{z-1}, H_z>, by ticket parity
+  uint64_t bar_rel;  // hand-off warp -> control: a ticket's dS hand-off is published
   int tick[2];
   uint32_t tmem_base;
 };
@@ -381,12 +384,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int BH = p.Bsz * p.H;
 
   if (tid == 0) {
-    uint64_t* one[10] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds, &m.bar_ctl,
-                         &m.bar1,    &m.bar2,    &m.bar3, &m.bar4,  &m.bar_stfree};
+    uint64_t* one[11] = {&m.bar_tma, &m.bar_tmb, &m.bar_h, &m.bar_ds,     &m.bar_ctl, &m.bar1,
+                         &m.bar2,    &m.bar3,    &m.bar4,  &m.bar_stfree, &m.bar_rel};
     uint64_t* eight[10] = {&m.bar_opa,  &m.bar_opc, &m.bar_oph,     &m.bar_ops1, &m.bar_ops2,
                            &m.bar_ops3, &m.bar_dc,  &m.bar_colfree, &m.bar_dx,   &m.bar_db};
 #pragma unroll
-    for (int i = 0; i < 10; ++i) mbar_init(one[i], 1);
+    for (int i = 0; i < 11; ++i) mbar_init(one[i], 1);
 #pragma unroll
     for (int i = 0; i < 10; ++i) mbar_init(eight[i], kWorkers / 32);
     fence_barrier_init();
@@ -400,7 +403,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem = m.tmem_base;
 
-  if (warp == kWorkers / 32) {
+  if (warp == kRelWarp) {
+    // ============================ hand-off warp (lane 0) ============================
+    // Publishes dS_{z-1} and <dS_{z-1}, H_z> of each ticket for the chunk z-1 ticket once the
+    // workers' carries are done (bar_ops3). The release's fence holds its thread ~1 us (longer
+    // with the same thread's stores or bulk copies in flight); on this warp it delays nobody.
+    // Its waits stay on the current ticket's phases: the control publishes ticket i + 1 only
+    // after this warp has finished ticket i - 1 (bar_rel).
+    if (lane == 0) {
+      mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
+      int cur = m.tick[0];
+      uint32_t it = 0;
+      while (cur < p.total) {
+        const uint32_t ph = it & 1u;
+        const TicketPos q = ticket_pos(cur, BH, p.H, p.nc);
+        mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
+        mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
+        const int nxt = m.tick[(it + 1) & 1];
+        if (q.z > 0) {
+          float2 dg = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < kWorkers / 32; ++w) {
+            dg.x += m.dgp[ph][w].x;
+            dg.y += m.dgp[ph][w].y;
+          }
+          __stcg(p.dgring + (long long)q.bh * 4 + ((q.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
+          // the workers' ring stores happened before their bar_ops3 arrivals
+          fence_proxy_async_global();
+          st_release_gpu(p.flags + (long long)q.bh * p.nc + q.z - 1, 1u);
+        }
+        mbar_arrive(&m.bar_rel);
+        cur = nxt;
+        ++it;
+      }
+    }
+    __syncwarp();
+  } else if (warp == kCtlWarp) {
     // =============================== control warp (lane 0) ===============================
     if (lane == 0) {
       prefetch_tmap(&tmB);
@@ -455,7 +493,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int hp = 0; hp < 2; ++hp)
           mma_run4<32, 2048>(tmem + COL_DCB, sdesc(sb + OFF_DY, 16, 1024),
                              sdesc(sb + OFF_H + hp * 16384u, 8192, 1024), id128, hp == 0);
-        // publish the next ticket (workers prefetch its x and dy)
+        // publish the next ticket (workers prefetch its x and dy), once the hand-off warp is done
+        // with the ticket before this one (so no waiter ever sees a phase parity repeat)
+        if (it > 0) mbar_wait(&m.bar_rel, (it - 1) & 1u, p.err, kErrMmaWait);
         m.tick[(it + 1) & 1] = nxt;
         mbar_arrive(&m.bar_ctl);
         const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
@@ -503,20 +543,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_run4<32, 2048>(tmem + COL_DBB, sdesc(sb + OFF_X, 16, 1024),
                                sdesc(sb + OFF_DS + hp * 16384u, 8192, 1024), idbb, hp == 0);
           mma_commit(&m.bar4);
-        }
-        // hand dS_{z-1} and <dS_{z-1}, H_z> to the chunk z-1 ticket (after the MMA issue: the
-        // release waits for this thread's earlier memory operations)
-        if (qc.z > 0) {
-          float2 dg = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int w = 0; w < kWorkers / 32; ++w) {
-            dg.x += m.dgp[w].x;
-            dg.y += m.dgp[w].y;
-          }
-          __stcg(p.dgring + (long long)qc.bh * 4 + ((qc.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
-          // the workers' ring stores happened before their bar_ops3 arrivals
-          fence_proxy_async_global();
-          st_release_gpu(p.flags + (long long)qc.bh * p.nc + qc.z - 1, 1u);
         }
         // dC from its staging tile in sH; the epilogue of dC has read sC, and once dBa has too,
         // the next C tile and record (its slot was the previous ticket's, which every worker warp
@@ -901,7 +927,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
           dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
         }
-        if (lane == 0) m.dgp[warp] = dg;
+        if (lane == 0) m.dgp[ph][warp] = dg;
       }
       warp_arrive(&m.bar_ops3, lane);
       // the next ticket: its x and dy are prefetched at the top of the loop, during the epilogues
