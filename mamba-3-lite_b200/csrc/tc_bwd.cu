@@ -47,7 +47,7 @@ constexpr uint32_t OFF_DGM = 131072; // dG' stacked over s, MN [2][64 l][64]
 constexpr uint32_t OFF_DS = 147456;  // dS_z (fp32, lands by bulk copy), then dS'x hi | lo
 constexpr uint32_t OFF_H = 180224;   // H_z (fp32, lands by bulk copy), then conj(H_z) hi | lo
 constexpr uint32_t OFF_MISC = 212992;
-constexpr uint32_t kMiscBytes = 9216;
+constexpr uint32_t kMiscBytes = 13312;
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBytes + 1024;
 constexpr uint32_t kLoadBytes = 64u * 128u * 4u + (uint32_t)sizeof(ChunkRec);  // C tile + record
 constexpr uint32_t kTmemCols = 512;
@@ -67,11 +67,15 @@ struct Misc {
   // twice before its waiter looks, so a parity never repeats under a waiter.
   uint64_t bar_opa, bar_opc, bar_oph, bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx,
       bar_db;
-  float4 dgam;      // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
-  float2 rc[4][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the four 16-state column groups
-  float2 rb[4][64];  // sum_n dB'_{sn} conj(B'_{sn})
-  float2 dgp[2][kWorkers / 32];  // per-warp partials of <dS_{z-1}, H_z>, by ticket parity
-  uint64_t bar_rel;  // hand-off warp -> control: a ticket's dS hand-off is published
+  // by ticket parity, read by the hand-off warp after the workers are done with the ticket:
+  float4 dgam[2];       // <dS_z, H_{z+1}> from the chunk z+1 ticket (lands with dS_z)
+  float2 rc[2][4][64];  // sum_n dC'_{ln} conj(C'_{ln}) over the four 16-state column groups
+  float2 rb[2][4][64];  // sum_n dB'_{sn} conj(B'_{sn})
+  float2 dgp[2][kWorkers / 32];  // per-warp partials of <dS_{z-1}, H_z>
+  // hand-off warp -> control and workers: a ticket's dS hand-off is published and its d Sigma
+  // is done (the control publishes ticket i + 1 and the workers finish the carry of ticket i + 1
+  // only after ticket i - 1 is, so no wait of the hand-off warp ever sees a phase parity repeat)
+  uint64_t bar_rel;
   int tick[2];
   uint32_t tmem_base;
 };
@@ -160,7 +164,7 @@ static __device__ __noinline__ void ctl_load_h(uint8_t* smem, Misc* m, const flo
 // dS_z (and <dS_z, H_{z+1}>) from the chunk z+1 ticket once its flag is published
 static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const float* ring,
                                                 const float4* dgring, const uint32_t* flags,
-                                                uint32_t* err, int nc, TicketPos q) {
+                                                uint32_t* err, int nc, TicketPos q, int slot) {
   if (q.z == nc - 1) {
     mbar_arrive(&m->bar_ds);
     return;
@@ -170,7 +174,7 @@ static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const fl
   mbar_arrive_expect_tx(&m->bar_ds, 32768u + 16u);
   bulk_load(smem + OFF_DS, ring + ((long long)q.bh * 4 + (q.z & 3)) * 64 * 128, 32768u,
             &m->bar_ds);
-  bulk_load(&m->dgam, dgring + (long long)q.bh * 4 + (q.z & 3), 16u, &m->bar_ds);
+  bulk_load(&m->dgam[slot], dgring + (long long)q.bh * 4 + (q.z & 3), 16u, &m->bar_ds);
 }
 // TMA stores of a 64-row output tile from its 32-float staging segments (segments 0, 1 at off01,
 // 2, 3 at off23), one bulk group. hp > 0: planar complex tile, segments 0, 1 hold the real parts
@@ -404,40 +408,101 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = m.tmem_base;
 
   if (warp == kRelWarp) {
-    // ============================ hand-off warp (lane 0) ============================
-    // Publishes dS_{z-1} and <dS_{z-1}, H_z> of each ticket for the chunk z-1 ticket once the
-    // workers' carries are done (bar_ops3). The release's fence holds its thread ~1 us (longer
-    // with the same thread's stores or bulk copies in flight); on this warp it delays nobody.
-    // Its waits stay on the current ticket's phases: the control publishes ticket i + 1 only
-    // after this warp has finished ticket i - 1 (bar_rel).
-    if (lane == 0) {
-      mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
-      int cur = m.tick[0];
-      uint32_t it = 0;
-      while (cur < p.total) {
-        const uint32_t ph = it & 1u;
-        const TicketPos q = ticket_pos(cur, BH, p.H, p.nc);
-        mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
-        mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
-        const int nxt = m.tick[(it + 1) & 1];
-        if (q.z > 0) {
-          float2 dg = make_float2(0.f, 0.f);
+    // ================================ hand-off warp ================================
+    // Per ticket, off the workers' and the control's paths:
+    //  * once the workers' carries are done (bar_ops3), lane 0 publishes dS_{z-1} and
+    //    <dS_{z-1}, H_z> for the chunk z-1 ticket. The release's fence holds its thread ~1 us
+    //    (longer with the same thread's stores or bulk copies in flight).
+    //  * once the workers' dB epilogue is done (bar_db; the dC one came before), d Sigma ->
+    //    reverse cumsum -> ddt and the chunk's dA partial: lane L takes positions L and L + 32,
+    //    each half is scanned within the warp, then the upper half's total is added to the lower.
+    // Every wait is on the current ticket's phase (bar_rel back-pressure, see Misc).
+    mbar_wait(&m.bar_ctl, 0u, p.err, kErrMmaWait);
+    int cur = m.tick[0];
+    uint32_t it = 0;
+    while (cur < p.total) {
+      const uint32_t ph = it & 1u;
+      const TicketPos q = ticket_pos(cur, BH, p.H, p.nc);
+      const float2 Ah = p.A[q.h];
+      mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
+      mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
+      const int nxt = m.tick[(it + 1) & 1];
+      if (lane == 0 && q.z > 0) {
+        float2 dg = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int w = 0; w < kWorkers / 32; ++w) {
-            dg.x += m.dgp[ph][w].x;
-            dg.y += m.dgp[ph][w].y;
-          }
-          __stcg(p.dgring + (long long)q.bh * 4 + ((q.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
-          // the workers' ring stores happened before their bar_ops3 arrivals
-          fence_proxy_async_global();
-          st_release_gpu(p.flags + (long long)q.bh * p.nc + q.z - 1, 1u);
+        for (int w = 0; w < kWorkers / 32; ++w) {
+          dg.x += m.dgp[ph][w].x;
+          dg.y += m.dgp[ph][w].y;
         }
-        mbar_arrive(&m.bar_rel);
-        cur = nxt;
-        ++it;
+        __stcg(p.dgring + (long long)q.bh * 4 + ((q.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
+        // the workers' ring stores happened before their bar_ops3 arrivals
+        fence_proxy_async_global();
+        st_release_gpu(p.flags + (long long)q.bh * p.nc + q.z - 1, 1u);
       }
+      __syncwarp();
+      // the row sums of this ticket are in once every worker warp has arrived at bar_db; its
+      // record slot and <dS_z, H_{z+1}> are not reloaded before this warp's bar_rel arrival
+      mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
+      {
+        const ChunkRec& rec = m.rec[ph];
+        const float2 dgam = q.z < p.nc - 1 ? make_float2(m.dgam[ph].x, m.dgam[ph].y)
+                                           : make_float2(0.f, 0.f);
+        const int t0 = q.z * 64;
+        float2 dv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int l = lane + 32 * u;
+          dv[u] = make_float2(
+              (m.rc[ph][0][l].x + m.rc[ph][1][l].x) + (m.rc[ph][2][l].x + m.rc[ph][3][l].x) -
+                  ((m.rb[ph][0][l].x + m.rb[ph][1][l].x) + (m.rb[ph][2][l].x + m.rb[ph][3][l].x)),
+              (m.rc[ph][0][l].y + m.rc[ph][1][l].y) + (m.rc[ph][2][l].y + m.rc[ph][3][l].y) -
+                  ((m.rb[ph][0][l].y + m.rb[ph][1][l].y) + (m.rb[ph][2][l].y + m.rb[ph][3][l].y)));
+        }
+        if (lane == 31) {
+          dv[1].x += dgam.x;
+          dv[1].y += dgam.y;
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {  // suffix sums within each half
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float ux = __shfl_down_sync(0xffffffffu, dv[u].x, o);
+            const float uy = __shfl_down_sync(0xffffffffu, dv[u].y, o);
+            if (lane + o < 32) {
+              dv[u].x += ux;
+              dv[u].y += uy;
+            }
+          }
+        }
+        const float2 hi_total = make_float2(__shfl_sync(0xffffffffu, dv[1].x, 0),
+                                            __shfl_sync(0xffffffffu, dv[1].y, 0));
+        const float2 s0 = make_float2(dv[0].x + hi_total.x, dv[0].y + hi_total.y);
+        const float2 s1 = dv[1];
+        float2 dap[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int l = lane + 32 * u, t = t0 + l;
+          const float2 da = u ? s1 : s0;
+          if (t < p.T) {
+            p.ddt[q.b * p.ddt_sb + (long long)t * p.ddt_st + q.h] =
+                (da.x * Ah.x + da.y * Ah.y) * rec.dsp[l];
+            dap[u] = make_float2(da.x * rec.sp[l], da.y * rec.sp[l]);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            dap[u].x += __shfl_xor_sync(0xffffffffu, dap[u].x, o);
+            dap[u].y += __shfl_xor_sync(0xffffffffu, dap[u].y, o);
+          }
+        }
+        if (lane == 0)
+          p.dapart[(long long)q.bh * p.nc + q.z] =
+              make_float2(dap[0].x + dap[1].x, dap[0].y + dap[1].y);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&m.bar_rel);
+      cur = nxt;
+      ++it;
     }
-    __syncwarp();
   } else if (warp == kCtlWarp) {
     // =============================== control warp (lane 0) ===============================
     if (lane == 0) {
@@ -454,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qc, 0, p.hp);
         ctl_load_b(&tmB, smem, &m, qc, p.hp);
         ctl_load_h(smem, &m, p.states, p.nc, qc);
-        ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qc);
+        ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qc, 0);
       }
       uint32_t it = 0;
       while (cur < p.total) {
@@ -565,7 +630,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (nxt < p.total) ctl_load_b(&tmB, smem, &m, qn, p.hp);
         bulk_wait_read_all();
         mbar_arrive(&m.bar_stfree);
-        if (nxt < p.total) ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn);
+        if (nxt < p.total)
+          ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn, (int)((it + 1) & 1));
         cur = nxt;
         qc = qn;
         ++it;
@@ -603,8 +669,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;      // index of that ticket
     TicketPos q{};
     int t0 = 0;
-    float2 dgam = make_float2(0.f, 0.f);
-    float2 Ah = make_float2(0.f, 0.f);  // A[h] of the ticket in flight
     for (;;) {
       // x and dy rows of ticket `next`: pulled into L2 during the epilogues (a register prefetch
       // would keep 16 registers live through them and spill at this kernel's register budget);
@@ -639,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               sb + OFF_C + kat * 16384u, stack8((uint32_t)r, 0u), kch, &m.bar_colfree, lane);
           acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
           acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
-          if (part == 0) m.rc[grp][r] = acc;
+          if (part == 0) m.rc[ph][grp][r] = acc;
         }
         warp_arrive(&m.bar_dc, lane);
 
@@ -663,7 +727,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         warp_arrive(&m.bar_dx, lane);
         // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s) -> staging tiles in sDYT, sDGM
         mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
-        if (warp == 0) Ah = p.A[q.h];  // for d Sigma below (no wait in between)
         tc_fence_after_sync();
         {
           float2 acc = combine_stage<kPlanar>(
@@ -673,65 +736,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               sb + OFF_B + kat * 16384u, stack8((uint32_t)r, 0u), kch, nullptr, lane);
           acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
           acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
-          if (part == 0) m.rb[grp][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
+          if (part == 0) m.rb[ph][grp][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
         }
         warp_arrive(&m.bar_db, lane);
-        workers_sync();
-
-        // ---- d Sigma -> reverse cumsum -> ddt and the chunk's dA partial (warp 0; lane L takes
-        // positions L and L + 32: each half is scanned within the warp, then the upper half's total
-        // is added to the lower half)
-        if (warp == 0) {
-          float2 dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int l = lane + 32 * u;
-            dv[u] = make_float2(
-                (m.rc[0][l].x + m.rc[1][l].x) + (m.rc[2][l].x + m.rc[3][l].x) -
-                    ((m.rb[0][l].x + m.rb[1][l].x) + (m.rb[2][l].x + m.rb[3][l].x)),
-                (m.rc[0][l].y + m.rc[1][l].y) + (m.rc[2][l].y + m.rc[3][l].y) -
-                    ((m.rb[0][l].y + m.rb[1][l].y) + (m.rb[2][l].y + m.rb[3][l].y)));
-          }
-          if (lane == 31) {
-            dv[1].x += dgam.x;
-            dv[1].y += dgam.y;
-          }
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {  // suffix sums within each half
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const float ux = __shfl_down_sync(0xffffffffu, dv[u].x, o);
-              const float uy = __shfl_down_sync(0xffffffffu, dv[u].y, o);
-              if (lane + o < 32) {
-                dv[u].x += ux;
-                dv[u].y += uy;
-              }
-            }
-          }
-          const float2 hi_total = make_float2(__shfl_sync(0xffffffffu, dv[1].x, 0),
-                                              __shfl_sync(0xffffffffu, dv[1].y, 0));
-          const float2 s0 = make_float2(dv[0].x + hi_total.x, dv[0].y + hi_total.y);
-          const float2 s1 = dv[1];
-          float2 dap[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int l = lane + 32 * u, t = t0 + l;
-            const float2 da = u ? s1 : s0;
-            if (t < p.T) {
-              p.ddt[q.b * p.ddt_sb + (long long)t * p.ddt_st + q.h] =
-                  (da.x * Ah.x + da.y * Ah.y) * rec.dsp[l];
-              dap[u] = make_float2(da.x * rec.sp[l], da.y * rec.sp[l]);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              dap[u].x += __shfl_xor_sync(0xffffffffu, dap[u].x, o);
-              dap[u].y += __shfl_xor_sync(0xffffffffu, dap[u].y, o);
-            }
-          }
-          if (lane == 0)
-            p.dapart[(long long)q.bh * p.nc + q.z] =
-                make_float2(dap[0].x + dap[1].x, dap[0].y + dap[1].y);
-        }
         ++it;
       }
       if (next >= p.total) break;
@@ -840,7 +847,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
       float dsz[16];
-      dgam = make_float2(0.f, 0.f);
       if (q.z < p.nc - 1) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -850,7 +856,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           dsz[4 * i + 2] = v.z;
           dsz[4 * i + 3] = v.w;
         }
-        dgam = make_float2(m.dgam.x, m.dgam.y);
       } else {
 #pragma unroll
         for (int c = 0; c < 16; ++c) dsz[c] = 0.f;
@@ -929,6 +934,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) m.dgp[ph][warp] = dg;
       }
+      // (back-pressure for the hand-off warp: it has finished the ticket before this one)
+      if (it > 0) mbar_wait(&m.bar_rel, (it - 1) & 1u, p.err, kErrMmaWait);
       warp_arrive(&m.bar_ops3, lane);
       // the next ticket: its x and dy are prefetched at the top of the loop, during the epilogues
       mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
