@@ -309,65 +309,67 @@ __device__ __forceinline__ uint32_t stage_seg(uint32_t seg01, uint32_t seg23, ui
 }
 
 // ---------------------------------------------------------------- worker helpers (out of line)
-// Epilogue of dC and dB over this thread's 16 state columns (8 complex) of row `row`
-// (32-column accumulator blocks at ta, tb): v = a + w b, staged as v conj(rot) (conjugated if
-// conj_out) into 16-byte chunks schunk0 .. schunk0+3 of the staging segment, and the partial row
-// sum sum v conj(X) with X the split-bf16 operand as the tensor core saw it (hi part in chunks
-// xch0, xch0+1 of stacked row xrow of the k-atom at xop, lo part 8 rows further).
-// dC: w = e_l, rot = cis(theta_l), X = C', sum = dC' conj(C').
-// dB = conj(dBa + dec_s dBb) cis(theta_s): w = dec_s, rot = cis(theta_s), conj_out, X = conj(B'),
-// sum = conj(dB' conj(B')).
-// kPlanar: the real parts go to chunks schunk0, schunk0+1 of segment seg and the imaginary parts
-// to the same chunks of segment seg_im (the in_proj layout of dB and dC).
+// The same epilogue over a warp's 32 accumulator columns (16 complex) in the 16x256b TMEM layout:
+// the hi-row and lo-row partials of a logical row sit 8 lanes apart (stack8), which that load shape
+// hands to the same thread, so they add in registers (no shuffle, no select). Thread t of the
+// warp in lane quadrant `sub` and column group `grp` takes logical rows 16 sub + t/4 (lanes +0..15)
+// and 16 sub + 8 + t/4 (lanes +16..31), complex 16 grp + 4 k + t%4 for k = 0..3. Staging: fp32
+// interleaved in segment grp, or (kPlanar) Re in segment grp/2 and Im in 2 + grp/2. Row sums
+// sum v conj(X) with X the split operand at xop (k-atom grp/2), reduced over the quad; returns
+// them for both rows (every lane of a quad holds the quad's sums).
 template <bool kPlanar>
-__device__ __forceinline__ float2 combine_stage(uint32_t ta, uint32_t tb, int part, float w,
-                                                    float2 rot, bool conj_out, uint32_t seg,
-                                                    uint32_t seg_im,
-                                                    uint32_t row, uint32_t schunk0, uint32_t xop,
-                                                    uint32_t xrow, uint32_t xch0,
-                                                    uint64_t* colfree, int lane) {
-  float a[16], bb[16];
-  ld_exch16_lean(ta, part, a);
-  ld_exch16_lean(tb, part, bb);
-  if (colfree != nullptr) warp_arrive(colfree, lane);
-  const float2 nr = make_float2(rot.x, -rot.y);
+__device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const float* wrow,
+                                              const float2* rotrow, bool conj_out,
+                                              uint32_t seg01, uint32_t seg23, int sub, int grp,
+                                              uint32_t xop, uint64_t* colfree, int lane,
+                                              float2& acc_a, float2& acc_b) {
+  const int q4 = lane & 3, rr = lane >> 2;
   const float cj = conj_out ? -1.f : 1.f;
-  float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int jj = 0; jj < 2; ++jj) {
-    const uint32_t xa = xop + swz(xrow, xch0 + (uint32_t)jj);
-    const uint4 hi = ld_shared_u4(xa);
-    const uint4 lo = ld_shared_u4(xa + 1024u);
-    const float2 xv[4] = {unsplit2(hi.x, lo.x), unsplit2(hi.y, lo.y), unsplit2(hi.z, lo.z),
-                          unsplit2(hi.w, lo.w)};
-    float o[8];
+  for (int half = 0; half < 2; ++half) {
+    float a[16], bb[16];
+    tmem_ld16x256_x4(ta + ((uint32_t)(16 * half) << 16), a);
+    tmem_ld16x256_x4(tb + ((uint32_t)(16 * half) << 16), bb);
+    tmem_ld_wait();
+    if (half == 1 && colfree != nullptr) warp_arrive(colfree, lane);
+    const uint32_t row = (uint32_t)(16 * sub + 8 * half + rr);
+    const float w = wrow[row];
+    const float2 rot = rotrow[row];
+    const float2 nr = make_float2(rot.x, -rot.y);
+    const uint32_t xrow = stack8(row, 0u);  // its lo part is 8 stacked rows (1024 bytes) on
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int c = 8 * jj + 2 * u;
-      const float2 v = make_float2(a[c] + w * bb[c], a[c + 1] + w * bb[c + 1]);
-      acc.x += v.x * xv[u].x + v.y * xv[u].y;
-      acc.y += v.y * xv[u].x - v.x * xv[u].y;
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = make_float2((a[4 * k] + a[4 * k + 2]) + w * (bb[4 * k] + bb[4 * k + 2]),
+                                   (a[4 * k + 1] + a[4 * k + 3]) + w * (bb[4 * k + 1] + bb[4 * k + 3]));
+      // X: bf16 hi | lo pair of complex 16 grp + 4k + q4, 16-byte chunk 4 (grp mod 2) + k
+      const uint32_t xa =
+          xop + swz(xrow, 4u * ((uint32_t)grp & 1u) + (uint32_t)k) + 4u * (uint32_t)q4;
+      const float2 xv = unsplit2(ld_shared_u32(xa), ld_shared_u32(xa + 1024u));
+      acc.x += v.x * xv.x + v.y * xv.y;
+      acc.y += v.y * xv.x - v.x * xv.y;
       const float2 r2 = cmul2(v, nr);
-      o[2 * u] = r2.x;
-      o[2 * u + 1] = cj * r2.y;
+      if constexpr (kPlanar) {
+        const uint32_t ch = 4u * ((uint32_t)grp & 1u) + (uint32_t)k;
+        st_shared_f32(stage_addr(stage_seg(seg01, seg23, (uint32_t)grp >> 1), row, ch) + 4u * q4,
+                      r2.x);
+        st_shared_f32(stage_addr(stage_seg(seg01, seg23, 2u + ((uint32_t)grp >> 1)), row, ch) +
+                          4u * q4,
+                      cj * r2.y);
+      } else {
+        st_shared_f2(stage_addr(stage_seg(seg01, seg23, (uint32_t)grp), row,
+                                2u * (uint32_t)k + ((uint32_t)q4 >> 1)) +
+                         8u * ((uint32_t)q4 & 1u),
+                     r2.x, cj * r2.y);
+      }
     }
-    if constexpr (kPlanar) {
-      st_shared_v4(stage_addr(seg, row, schunk0 + (uint32_t)jj),
-                   make_uint4(__float_as_uint(o[0]), __float_as_uint(o[2]), __float_as_uint(o[4]),
-                              __float_as_uint(o[6])));
-      st_shared_v4(stage_addr(seg_im, row, schunk0 + (uint32_t)jj),
-                   make_uint4(__float_as_uint(o[1]), __float_as_uint(o[3]), __float_as_uint(o[5]),
-                              __float_as_uint(o[7])));
-    } else {
-      st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj),
-                   make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
-                              __float_as_uint(o[3])));
-      st_shared_v4(stage_addr(seg, row, schunk0 + 2u * jj + 1u),
-                   make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]),
-                              __float_as_uint(o[7])));
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+      acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
     }
+    if (half == 0) acc_a = acc; else acc_b = acc;
   }
-  return acc;
 }
 
 }  // namespace
@@ -649,13 +651,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
     const int kb = 32 * grp + 16 * part;  // this thread's 16 interleaved state columns
     const int s0c = 16 * grp + 8 * part;  // this thread's 8 columns of a 64-column accumulator
-    // staging place of its 8 complex values of dC / dB (state columns 16 grp + 8 part .. +7):
-    // interleaved, floats 32 grp + 16 part .. +15 = segment grp, chunks 4 part .. +3; planar, Re
-    // (and Im) n = 16 grp + 8 part .. +7 = segment grp / 2 (and 2 + grp / 2), chunks
-    // 4 (grp mod 2) + 2 part, +1
-    const uint32_t sseg = kPlanar ? (uint32_t)grp >> 1 : (uint32_t)grp;
-    const uint32_t schunk0 = kPlanar ? 4u * ((uint32_t)grp & 1u) + 2u * (uint32_t)part
-                                     : 4u * (uint32_t)part;
     const uint32_t kat = (uint32_t)kb >> 6;              // k-atom of its state columns
     const uint32_t kch = ((uint32_t)kb & 63u) >> 3;      // first of its two 16-byte chunks there
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
@@ -696,14 +691,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_l2();
         tc_fence_after_sync();
         {
-          float2 acc = combine_stage<kPlanar>(
-              tmem + lane_off + COL_DCA + 32u * grp, tmem + lane_off + COL_DCB + 32u * grp, part,
-              rec.el[r], rec.cis[r], false, stage_seg(sb + OFF_H, sb + OFF_H + 16384u, sseg),
-              stage_seg(sb + OFF_H, sb + OFF_H + 16384u, sseg + 2u), (uint32_t)r, schunk0,
-              sb + OFF_C + kat * 16384u, stack8((uint32_t)r, 0u), kch, &m.bar_colfree, lane);
-          acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
-          acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
-          if (part == 0) m.rc[ph][grp][r] = acc;
+          float2 acc_a, acc_b;
+          combine_rows2<kPlanar>(tmem + lane_off + COL_DCA + 32u * grp,
+                                 tmem + lane_off + COL_DCB + 32u * grp, rec.el, rec.cis, false,
+                                 sb + OFF_H, sb + OFF_H + 16384u, sub, grp,
+                                 sb + OFF_C + ((uint32_t)grp >> 1) * 16384u, &m.bar_colfree, lane,
+                                 acc_a, acc_b);
+          if ((lane & 3) == 0) {
+            m.rc[ph][grp][16 * sub + (lane >> 2)] = acc_a;
+            m.rc[ph][grp][16 * sub + 8 + (lane >> 2)] = acc_b;
+          }
         }
         warp_arrive(&m.bar_dc, lane);
 
@@ -729,14 +726,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
         {
-          float2 acc = combine_stage<kPlanar>(
-              tmem + lane_off + COL_DBA + 32u * grp, tmem + lane_off + COL_DBB + 32u * grp, part,
-              rec.dec[r], rec.cis[r], true, stage_seg(sb + OFF_DYT, sb + OFF_DGM, sseg),
-              stage_seg(sb + OFF_DYT, sb + OFF_DGM, sseg + 2u), (uint32_t)r, schunk0,
-              sb + OFF_B + kat * 16384u, stack8((uint32_t)r, 0u), kch, nullptr, lane);
-          acc.x += __shfl_xor_sync(0xffffffffu, acc.x, 8);
-          acc.y += __shfl_xor_sync(0xffffffffu, acc.y, 8);
-          if (part == 0) m.rb[ph][grp][r] = make_float2(acc.x, -acc.y);  // conj: dB' conj(B')
+          float2 acc_a, acc_b;
+          combine_rows2<kPlanar>(tmem + lane_off + COL_DBA + 32u * grp,
+                                 tmem + lane_off + COL_DBB + 32u * grp, rec.dec, rec.cis, true,
+                                 sb + OFF_DYT, sb + OFF_DGM, sub, grp,
+                                 sb + OFF_B + ((uint32_t)grp >> 1) * 16384u, nullptr, lane, acc_a,
+                                 acc_b);
+          if ((lane & 3) == 0) {  // conj: dB' conj(B')
+            m.rb[ph][grp][16 * sub + (lane >> 2)] = make_float2(acc_a.x, -acc_a.y);
+            m.rb[ph][grp][16 * sub + 8 + (lane >> 2)] = make_float2(acc_b.x, -acc_b.y);
+          }
         }
         warp_arrive(&m.bar_db, lane);
         ++it;

@@ -215,6 +215,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 16 TMEM lanes x 32 columns (shape 16x256b, 4 repeats): thread t receives, for k = 0..3,
+// v[4k], v[4k+1] = (lane t/4, columns 8k + 2 (t%4), +1) and v[4k+2], v[4k+3] = the same columns of
+// lane t/4 + 8 (lanes relative to the 16-lane base in taddr)
+__device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -330,6 +346,17 @@ namespace tc {
 // and lo partial sums of one output row sit in TMEM lanes m and m ^ 8 of the same warp.
 __device__ __forceinline__ uint32_t stack8(uint32_t r, uint32_t part) {
   return ((r >> 3) << 4) | (part << 3) | (r & 7u);
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t saddr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));
+  return v;
+}
+__device__ __forceinline__ void st_shared_f2(uint32_t saddr, float x, float y) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr), "f"(x), "f"(y) : "memory");
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t saddr, float x) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(saddr), "f"(x) : "memory");
 }
 __device__ __forceinline__ float4 ld_shared_f4(uint32_t saddr) {
   float4 v;
