@@ -707,19 +707,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- epilogue 3: dx = dXa + dec_s dXb -> staging tile in sDGK
         mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
-        {
-          float xa[8], xb[8];
-          ld_exch8(tmem + lane_off + COL_DXA + 16u * grp, part, xa);
-          ld_exch8(tmem + lane_off + COL_DXB + 16u * grp, part, xb);
-          const float d = rec.dec[r];
-          const uint32_t seg = sb + OFF_DGK + ((uint32_t)s0c >> 5) * 8192u;
+        {  // 16x256b reads as in epilogue 1; each column pair leaves as one 8-byte store
+          const int q4 = lane & 3, rr = lane >> 2;
 #pragma unroll
-          for (int i = 0; i < 2; ++i)
-            st_shared_v4(stage_addr(seg, (uint32_t)r, (((uint32_t)s0c & 31u) >> 2) + (uint32_t)i),
-                         make_uint4(__float_as_uint(xa[4 * i] + d * xb[4 * i]),
-                                    __float_as_uint(xa[4 * i + 1] + d * xb[4 * i + 1]),
-                                    __float_as_uint(xa[4 * i + 2] + d * xb[4 * i + 2]),
-                                    __float_as_uint(xa[4 * i + 3] + d * xb[4 * i + 3])));
+          for (int h = 0; h < 2; ++h) {
+            float xa[8], xb[8];
+            const uint32_t tl = tmem + lane_off + ((uint32_t)(16 * h) << 16) + 16u * grp;
+            tmem_ld16x256_x2(tl + COL_DXA, xa);
+            tmem_ld16x256_x2(tl + COL_DXB, xb);
+            tmem_ld_wait();
+            const uint32_t row = (uint32_t)(16 * sub + 8 * h + rr);
+            const float d = rec.dec[row];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const uint32_t c0 = 16u * (uint32_t)grp + 8u * (uint32_t)k + 2u * (uint32_t)q4;
+              st_shared_f2(stage_addr(sb + OFF_DGK + (c0 >> 5) * 8192u, row, (c0 & 31u) >> 2) +
+                               4u * (c0 & 3u),
+                           (xa[4 * k] + xa[4 * k + 2]) + d * (xb[4 * k] + xb[4 * k + 2]),
+                           (xa[4 * k + 1] + xa[4 * k + 3]) + d * (xb[4 * k + 1] + xb[4 * k + 3]));
+            }
+          }
         }
         warp_arrive(&m.bar_dx, lane);
         // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s) -> staging tiles in sDYT, sDGM
@@ -877,26 +884,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
       mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
       tc_fence_after_sync();
+      // 16x256b TMEM reads (hi / lo partial rows in one thread): rows 16 sub + 8 h + lane/4,
+      // columns s = 16 grp + 8 k + 2 (lane%4), +1; each pair leaves as one 4-byte bf16x2 word
+      // per split half and destination
       {
-        float gs[8], ms[8];
-        ld_exch8(tmem + lane_off + COL_G + 16u * grp, part, gs);
-        ld_exch8(tmem + lane_off + COL_DM + 16u * grp, part, ms);
-        const float rl = rec.rho[r];
-        float mrv[8], dgv[8];
+        const int q4 = lane & 3, rr = lane >> 2;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int s = s0c + c;
-          const float L = (s <= r) ? expf(rl - rec.rho[s]) : 0.f;
-          mrv[c] = L * gs[c];
-          dgv[c] = L * ms[c];
+        for (int h = 0; h < 2; ++h) {
+          float g[8], dm[8];
+          const uint32_t tl = tmem + lane_off + ((uint32_t)(16 * h) << 16) + 16u * grp;
+          tmem_ld16x256_x2(tl + COL_G, g);
+          tmem_ld16x256_x2(tl + COL_DM, dm);
+          tmem_ld_wait();
+          const int row = 16 * sub + 8 * h + rr;
+          const float rl = rec.rho[row];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int s0 = 16 * grp + 8 * k + 2 * q4;
+            float mr2[2], dg2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float L = (s0 + e <= row) ? expf(rl - rec.rho[s0 + e]) : 0.f;
+              mr2[e] = L * (g[4 * k + e] + g[4 * k + 2 + e]);
+              dg2[e] = L * (dm[4 * k + e] + dm[4 * k + 2 + e]);
+            }
+            uint32_t mrh, mrl, dgh, dgl;
+            split2(mr2[0], mr2[1], mrh, mrl);
+            split2(dg2[0], dg2[1], dgh, dgl);
+            // MN-major (stacked s): k-atom s0/32, chunks 2 ((s0/8) mod 4) (hi) and +1 (lo)
+            const uint32_t ch = 2u * (((uint32_t)s0 >> 3) & 3u), off = 4u * (uint32_t)q4;
+            const uint32_t mnh = ((uint32_t)s0 >> 5) * 8192u + swz((uint32_t)row, ch) + off;
+            const uint32_t mnl = ((uint32_t)s0 >> 5) * 8192u + swz((uint32_t)row, ch + 1u) + off;
+            st_shared_u32(sb + OFF_DYT + mnh, mrh);
+            st_shared_u32(sb + OFF_DYT + mnl, mrl);
+            st_shared_u32(sb + OFF_DGM + mnh, dgh);
+            st_shared_u32(sb + OFF_DGM + mnl, dgl);
+            // K-major (stacked rows): chunk s0/8
+            const uint32_t kc = (uint32_t)s0 >> 3;
+            st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 0u), kc) + off, dgh);
+            st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 1u), kc) + off, dgl);
+          }
         }
-        const uint32_t mh = stack8((uint32_t)s0c, 0u), ml = stack8((uint32_t)s0c, 1u);
-        split8_store(sb + OFF_DYT + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
-                     sb + OFF_DYT + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), mrv);
-        split8_store(sb + OFF_DGM + (mh >> 6) * 8192u + swz(r, (mh & 63u) >> 3),
-                     sb + OFF_DGM + (ml >> 6) * 8192u + swz(r, (ml & 63u) >> 3), dgv);
-        split8_store(sb + OFF_DGK + swz(stack8(r, 0), s0c >> 3),
-                     sb + OFF_DGK + swz(stack8(r, 1), s0c >> 3), dgv);
       }
       warp_arrive(&m.bar_ops2, lane);
       // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major), <dS_{z-1}, H_z>

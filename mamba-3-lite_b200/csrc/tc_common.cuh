@@ -231,6 +231,17 @@ __device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, float (&v)[16])
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// the same over 16 columns (2 repeats): v[4k .. 4k+3] for k = 0, 1
+__device__ __forceinline__ void tmem_ld16x256_x2(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -354,6 +365,17 @@ __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t saddr) {
 }
 __device__ __forceinline__ void st_shared_f2(uint32_t saddr, float x, float y) {
   asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr), "f"(x), "f"(y) : "memory");
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t saddr, uint32_t x) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(x) : "memory");
+}
+// splits 2 floats into a bf16x2 hi word and a bf16x2 lo word (one pair of split8)
+__device__ __forceinline__ void split2(float v0, float v1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 hp = __floats2bfloat162_rn(v0, v1);
+  const float2 hf = __bfloat1622float2(hp);
+  const __nv_bfloat162 lp = __floats2bfloat162_rn(v0 - hf.x, v1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&hp);
+  lo = *reinterpret_cast<const uint32_t*>(&lp);
 }
 __device__ __forceinline__ void st_shared_f32(uint32_t saddr, float x) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(saddr), "f"(x) : "memory");
