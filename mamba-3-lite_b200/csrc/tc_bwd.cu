@@ -250,33 +250,6 @@ __device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)
     out[c] = (part ? v[16 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
   }
 }
-// the same, with fewer registers live: each 16-column half is loaded and summed on its own (both
-// partners form both sums), then the thread keeps its half
-__device__ __forceinline__ void ld_exch16_lean(uint32_t taddr, int part, float (&out)[16]) {
-  float v[16];
-  tmem_ld16(taddr, out);
-  tmem_ld_wait();
-#pragma unroll
-  for (int c = 0; c < 16; ++c) out[c] += __shfl_xor_sync(0xffffffffu, out[c], 8);
-  tmem_ld16(taddr + 16u, v);
-  tmem_ld_wait();
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    const float t = v[c] + __shfl_xor_sync(0xffffffffu, v[c], 8);
-    out[c] = part ? t : out[c];
-  }
-}
-// the same over a 16-column block: columns [8 p, 8 p + 8)
-__device__ __forceinline__ void ld_exch8(uint32_t taddr, int part, float (&out)[8]) {
-  float v[16];
-  tmem_ld16(taddr, v);
-  tmem_ld_wait();
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const float send = part ? v[c] : v[8 + c];
-    out[c] = (part ? v[8 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-}
 __device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
   float w[8];
 #pragma unroll
@@ -650,7 +623,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
     const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
     const int kb = 32 * grp + 16 * part;  // this thread's 16 interleaved state columns
-    const int s0c = 16 * grp + 8 * part;  // this thread's 8 columns of a 64-column accumulator
     const uint32_t kat = (uint32_t)kb >> 6;              // k-atom of its state columns
     const uint32_t kch = ((uint32_t)kb & 63u) >> 3;      // first of its two 16-byte chunks there
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
