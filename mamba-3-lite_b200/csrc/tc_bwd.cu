@@ -617,8 +617,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // =============================== worker warps 0-15 ===============================
     // TMEM lane quadrant sub = warp mod 4; column group grp = warp / 4 takes 32 of the 128
-    // columns of a complex accumulator (16 of a 64-column one); the thread with `part` p keeps
-    // the full sums of half of those after the hi/lo exchange.
+    // columns of a complex accumulator (16 of a 64-column one). The epilogues read TMEM in the
+    // 16x256b shape (each thread: two logical rows, column pairs; hi and lo partials added in
+    // registers); the carry reads it in the 32x32b shape, where the thread of lane L (row r,
+    // `part` p) keeps the full sums of half of the warp's columns after the hi / lo exchange.
     const int sub = warp & 3, grp = warp >> 2;
     const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
     const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
