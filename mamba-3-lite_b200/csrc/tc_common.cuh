@@ -162,20 +162,6 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uin
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// the same with each descriptor given as (low, high) 32-bit words: the address field sits in the low
-// word, so stepping an operand along K is one 32-bit add
-__device__ __forceinline__ void mma_bf16_ss_w(uint32_t d_tmem, uint32_t alo, uint32_t ahi,
-                                              uint32_t blo, uint32_t bhi, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "mov.b64 ad, {%1, %2};\n\t"
-      "mov.b64 bd, {%3, %4};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
-      "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // mbarrier arrives once all previously issued tcgen05.mma of this thread have completed
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -269,10 +255,6 @@ __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t chunk) {
 __device__ __forceinline__ uint32_t stack_row(uint32_t r, uint32_t part) {
   return ((r >> 4) << 5) | (part << 4) | (r & 15u);
 }
-__device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
-  hi = __float2bfloat16_rn(v);
-  lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-}
 // splits 8 floats into 8 hi and 8 lo bf16 packed in two uint4 (pairwise bf16x2 conversions)
 __device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo) {
   uint32_t h[4], l[4];
@@ -291,9 +273,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
                : "memory");
-}
-__device__ __forceinline__ void st_shared_u16(uint32_t saddr, uint16_t v) {
-  asm volatile("st.shared.u16 [%0], %1;" ::"r"(saddr), "h"(v) : "memory");
 }
 
 // ----------------------------------------------------------------------------- global memory
@@ -399,13 +378,6 @@ __device__ __forceinline__ float2 unsplit2(uint32_t hi, uint32_t lo) {
   const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xFFFF0000u);
   const float l0 = __uint_as_float(lo << 16), l1 = __uint_as_float(lo & 0xFFFF0000u);
   return make_float2(h0 + l0, h1 + l1);
-}
-// the value a split-bf16 operand element represents (hi + lo of split8), computed from fp32
-__device__ __forceinline__ float2 split_round2(float2 v) {
-  const __nv_bfloat162 hp = __floats2bfloat162_rn(v.x, v.y);
-  const float2 hf = __bfloat1622float2(hp);
-  const float2 lf = __bfloat1622float2(__floats2bfloat162_rn(v.x - hf.x, v.y - hf.y));
-  return make_float2(hf.x + lf.x, hf.y + lf.y);
 }
 }  // namespace tc
 }  // namespace m3ssd
