@@ -236,20 +236,6 @@ __device__ __forceinline__ float2 cmul2(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
-// Full sums of a stacked accumulator: TMEM lanes L and L ^ 8 hold the hi-row and lo-row partials
-// of one logical row. Of a 32-column block, the thread with `part` p keeps columns [16 p, 16 p + 16)
-// and sends the other half to its partner. (tcgen05.ld takes one address for the whole warp, so
-// both halves are loaded and selected per lane.)
-__device__ __forceinline__ void ld_exch16(uint32_t taddr, int part, float (&out)[16]) {
-  float v[32];
-  tmem_ld32(taddr, v);
-  tmem_ld_wait();
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    const float send = part ? v[c] : v[16 + c];
-    out[c] = (part ? v[16 + c] : v[c]) + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-}
 __device__ __forceinline__ void split8_store(uint32_t hi_addr, uint32_t lo_addr, const float* v) {
   float w[8];
 #pragma unroll
@@ -617,16 +603,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // =============================== worker warps 0-15 ===============================
     // TMEM lane quadrant sub = warp mod 4; column group grp = warp / 4 takes 32 of the 128
-    // columns of a complex accumulator (16 of a 64-column one). The epilogues read TMEM in the
-    // 16x256b shape (each thread: two logical rows, column pairs; hi and lo partials added in
-    // registers); the carry reads it in the 32x32b shape, where the thread of lane L (row r,
-    // `part` p) keeps the full sums of half of the warp's columns after the hi / lo exchange.
+    // columns of a complex accumulator (16 of a 64-column one). Accumulators are read in the
+    // 16x256b shape: each thread gets two logical rows (16 sub + 8 h + lane/4) and column pairs
+    // 8 k + 2 (lane%4), +1 of the warp's columns, with the hi and lo partial rows (8 lanes apart
+    // in the stacking) both in its registers.
     const int sub = warp & 3, grp = warp >> 2;
-    const int r = 16 * sub + 8 * (lane >> 4) + (lane & 7);  // logical row of this TMEM lane
-    const int part = (lane >> 3) & 1;                          // 0: hi-row partial, 1: lo-row
-    const int kb = 32 * grp + 16 * part;  // this thread's 16 interleaved state columns
-    const uint32_t kat = (uint32_t)kb >> 6;              // k-atom of its state columns
-    const uint32_t kch = ((uint32_t)kb & 63u) >> 3;      // first of its two 16-byte chunks there
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
     // x / dy staging: row xs0, columns 8 (tid & 7) .. + 7 (8 lanes per row)
     const int xs0 = tid >> 3, xp0 = 8 * (tid & 7);
@@ -824,7 +805,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tile == 2) warp_arrive(&m.bar_oph, lane);   // dCb may start
       }
 
-      // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it) -> dS'x hi | lo
+      // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it: float4 i holds
+      // row p = 16 sub + 8 (i/2) + lane/4, complex n = 16 grp + 4 k + lane%4 for k = 2 (i mod 2), +1)
+      // -> dS'x hi | lo (K-major rows p: k-atom grp/2, 16-byte chunk 4 (grp mod 2) + k, 4 bytes
+      // per complex)
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
       float dsz[16];
       if (q.z < p.nc - 1) {
@@ -843,16 +827,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       workers_sync();
       {
         const float2 ct = rec.ct;
-        float w[16];
+        const uint32_t q4 = (uint32_t)lane & 3u, rr = (uint32_t)lane >> 2;
+        const uint32_t db = sb + OFF_DS + ((uint32_t)grp >> 1) * 8192u + 4u * q4;
 #pragma unroll
         for (int c = 0; c < 16; c += 2) {  // (Re, -Im) of conj(cis(theta_Gamma)) dS_z
-          w[c] = dsz[c] * ct.x + dsz[c + 1] * ct.y;
-          w[c + 1] = -(dsz[c + 1] * ct.x - dsz[c] * ct.y);
+          const uint32_t i = (uint32_t)c >> 2, k = 2u * (i & 1u) + (((uint32_t)c >> 1) & 1u);
+          const uint32_t prow = 16u * (uint32_t)sub + 8u * (i >> 1) + rr;
+          uint32_t whi, wlo;
+          split2(dsz[c] * ct.x + dsz[c + 1] * ct.y, -(dsz[c + 1] * ct.x - dsz[c] * ct.y), whi, wlo);
+          const uint32_t off = swz(prow, 4u * ((uint32_t)grp & 1u) + k);
+          st_shared_u32(db + off, whi);
+          st_shared_u32(db + 16384u + off, wlo);
         }
-#pragma unroll
-        for (int jj = 0; jj < 2; ++jj)
-          split8_store(sb + OFF_DS + kat * 8192u + swz(r, kch + jj),
-                       sb + OFF_DS + 16384u + kat * 8192u + swz(r, kch + jj), w + 8 * jj);
       }
 
       // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
@@ -901,31 +887,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       warp_arrive(&m.bar_ops2, lane);
-      // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major), <dS_{z-1}, H_z>
+      // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major, the layout above),
+      // <dS_{z-1}, H_z>. Q in the 16x256b shape: rows p = 16 sub + 8 h + lane/4, complex
+      // 16 grp + 4 k + lane%4 (k = 0..3), hi and lo partial rows added in registers.
       {
-        float qv[16];
-        ld_exch16(tmem + lane_off + COL_Q + 32u * grp, part, qv);
+        const uint32_t q4 = (uint32_t)lane & 3u, rr = (uint32_t)lane >> 2;
+        float qa[16], qb[16];
+        tmem_ld16x256_x4(tmem + lane_off + COL_Q + 32u * grp, qa);
+        tmem_ld16x256_x4(tmem + lane_off + (16u << 16) + COL_Q + 32u * grp, qb);
+        tmem_ld_wait();
         float2 dg = make_float2(0.f, 0.f);
         if (q.z > 0) {
           const float2 g = rec.g;
           float4* slot = reinterpret_cast<float4*>(p.ring + ((long long)q.bh * 4 + ((q.z - 1) & 3)) * 64 * 128);
+          const uint32_t hb = sb + OFF_H + ((uint32_t)grp >> 1) * 8192u + 4u * q4;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
+            const float* qv = (i >> 1) ? qb : qa;
+            const uint32_t prow = 16u * (uint32_t)sub + 8u * ((uint32_t)i >> 1) + rr;
             float o[4];
 #pragma unroll
-            for (int u = 0; u < 4; u += 2) {
-              const int c = 4 * i + u;
-              o[u] = qv[c] + g.x * dsz[c] + g.y * dsz[c + 1];
-              o[u + 1] = -qv[c + 1] + g.x * dsz[c + 1] - g.y * dsz[c];
+            for (int u = 0; u < 2; ++u) {
+              const int k = 2 * (i & 1) + u, c = 4 * i + 2 * u;
+              const float qre = qv[4 * k] + qv[4 * k + 2], qim = qv[4 * k + 1] + qv[4 * k + 3];
+              o[2 * u] = qre + g.x * dsz[c] + g.y * dsz[c + 1];
+              o[2 * u + 1] = -qim + g.x * dsz[c + 1] - g.y * dsz[c];
+              const uint32_t off = swz(prow, 4u * ((uint32_t)grp & 1u) + (uint32_t)k);
+              const float2 h = unsplit2(ld_shared_u32(hb + off), ld_shared_u32(hb + 16384u + off));
+              dg.x += o[2 * u] * h.x - o[2 * u + 1] * h.y;
+              dg.y += o[2 * u] * h.y + o[2 * u + 1] * h.x;
             }
             __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
-            const uint32_t hoff = kat * 8192u + swz(r, kch + (uint32_t)(i >> 1));
-            const uint4 hh = ld_shared_u4(sb + OFF_H + hoff);
-            const uint4 hl = ld_shared_u4(sb + OFF_H + 16384u + hoff);
-            const float2 h0 = unsplit2((i & 1) ? hh.z : hh.x, (i & 1) ? hl.z : hl.x);
-            const float2 h1 = unsplit2((i & 1) ? hh.w : hh.y, (i & 1) ? hl.w : hl.y);
-            dg.x += o[0] * h0.x - o[1] * h0.y + o[2] * h1.x - o[3] * h1.y;
-            dg.y += o[0] * h0.y + o[1] * h0.x + o[2] * h1.y + o[3] * h1.x;
           }
         }
 #pragma unroll
