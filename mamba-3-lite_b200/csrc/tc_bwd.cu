@@ -19,6 +19,8 @@
 // tcgen05 (kind::f16) with split-bf16 operands stacked in groups of 8 rows (stack8) so each
 // shared buffer serves as a stacked A operand and as a plain B operand. dS_z is handed from the
 // CTA that processed chunk z+1 through a 4-slot ring in global memory (L2) with release flags.
+// Warps: 16 workers (operand transforms, epilogues, carry), one control warp (tickets, every TMA
+// and bulk copy, every MMA), one hand-off warp (the dS release and d Sigma -> ddt, dA partials).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -61,10 +63,10 @@ struct Misc {
   // published, MMA commits 1..4, and the staging buffers of the previous ticket's dx / dB stores
   // read (stfree)
   uint64_t bar_tma, bar_tmb, bar_h, bar_ds, bar_ctl, bar1, bar2, bar3, bar4, bar_stfree;
-  // workers -> control (one arrival per worker warp)
-  // (opa: x, dy, e dy written; opc: C'; ops1: B'; oph: conj(H); ops2:
-  // dS' written and epilogue 1 done; ops3: carry done). Every wait is on the phase of the current ticket: no barrier can complete
-  // twice before its waiter looks, so a parity never repeats under a waiter.
+  // workers -> control (one arrival per worker warp): opa x, dy, e dy written; opc C'; ops1 B';
+  // oph conj(H); ops2 dS' written and epilogue 1 done; ops3 carry done; colfree dCa's columns
+  // read; dc / dx / db staging tiles written. Every wait is on the phase of the current ticket:
+  // no barrier can complete twice before its waiter looks, so a parity never repeats under one.
   uint64_t bar_opa, bar_opc, bar_oph, bar_ops1, bar_ops2, bar_ops3, bar_colfree, bar_dc, bar_dx,
       bar_db;
   // by ticket parity, read by the hand-off warp after the workers are done with the ticket:
