@@ -225,6 +225,25 @@ typedef struct m3ssd_proj_bwd_args {
 M3SSD_API int m3ssd_fwd_proj(const m3ssd_proj_fwd_args* args, void* stream);
 M3SSD_API int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* args, void* stream);
 
+/* ---- State carry -------------------------------------------------------------------------------
+ * The operator over one segment of a longer sequence: the reference's recurrence
+ * (models/ssd_complex.py:17-33) started from an initial state h0 instead of zero, returning the
+ * state after the segment's last position. A sequence cut into segments of multiples of 64
+ * positions, each call fed the previous call's hT, gives the same y as one call over the whole
+ * sequence, and the backward chains the same way (dhT of a segment = dh0 of the next). No
+ * counterpart in the reference's API (its operator always starts from zero and drops the state).
+ * States are (B, H, N, D) complex64, contiguous: s[n, :] of the recurrence for every (b, h).
+ *   - Tensor-core shapes only (as m3ssd_fwd_proj) and seqlen a multiple of 64; otherwise
+ *     M3SSD_ERR_SHAPE. y, dx, dB, dC: 16-byte aligned; state pointers 8-byte aligned.
+ *   - m3ssd_fwd_state: h0 NULL = zero initial state (m3ssd_fwd's result); hT NULL = not written.
+ *   - m3ssd_bwd_state: `states` from the matching m3ssd_fwd_state (it carries h0 into the
+ *     gradients). hT (the forward's final state) and dhT (its gradient) come together or both
+ *     NULL (M3SSD_ERR_NULL otherwise); dh0 NULL = the initial state's gradient is not written.
+ *     Gradients in the convention of m3ssd_bwd; dh0 = dL/dRe h0 + i dL/dIm h0. */
+M3SSD_API int m3ssd_fwd_state(const m3ssd_fwd_args* args, const void* h0, void* hT, void* stream);
+M3SSD_API int m3ssd_bwd_state(const m3ssd_bwd_args* args, const void* hT, const void* dhT,
+                              void* dh0, void* stream);
+
 /* Test aid, no counterpart in the reference: checks that the library's bounded waits end instead
  * of hanging. One thread waits on an mbarrier nobody arrives at and on a hand-off flag nobody
  * sets, with the same helpers the tensor-core kernels use; each gives up after about a second.

@@ -404,6 +404,60 @@ int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* a, void* stream) {
                             static_cast<cudaStream_t>(stream));
 }
 
+int m3ssd_fwd_state(const m3ssd_fwd_args* a, const void* h0, void* hT, void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  if (!tc_shape(&a->prob) || a->prob.seqlen % m3ssd::tc::kChunk) return M3SSD_ERR_SHAPE;
+  Problem p = make_problem(&a->prob);
+  rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
+                   a->dt_strides);
+  if (rc) return rc;
+  if (!m3ssd::tc::fwd_supported(p)) return M3SSD_ERR_SHAPE;
+  if (!a->y || !a->states) return M3SSD_ERR_NULL;
+  if (!aligned(a->y, 16) || !aligned(a->states, 16) || !aligned(h0, 8) || !aligned(hT, 8))
+    return M3SSD_ERR_ALIGN;
+  const size_t need = fwd_ws(p);
+  if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
+  rc = check_device();
+  if (rc) return rc;
+  return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream),
+                            h0, hT);
+}
+
+int m3ssd_bwd_state(const m3ssd_bwd_args* a, const void* hT, const void* dhT, void* dh0,
+                    void* stream) {
+  if (!a) return M3SSD_ERR_NULL;
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  if (!tc_shape(&a->prob) || a->prob.seqlen % m3ssd::tc::kChunk) return M3SSD_ERR_SHAPE;
+  Problem p = make_problem(&a->prob);
+  rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
+                   a->dt_strides);
+  if (rc) return rc;
+  if (!m3ssd::tc::bwd_supported(p)) return M3SSD_ERR_SHAPE;
+  if (!a->dy || !a->states || !a->dx || !a->dA || !a->dB || !a->dC || !a->ddt)
+    return M3SSD_ERR_NULL;
+  if ((hT != nullptr) != (dhT != nullptr)) return M3SSD_ERR_NULL;
+  if (!aligned(a->dy, p.y_bf16 ? 2 : 4) || !aligned(a->states, 16) || !aligned(a->dx, 16) ||
+      !aligned(a->dA, 8) || !aligned(a->dB, 16) || !aligned(a->dC, 16) || !aligned(a->ddt, 4) ||
+      !aligned(hT, 8) || !aligned(dhT, 8) || !aligned(dh0, 8))
+    return M3SSD_ERR_ALIGN;
+  const size_t need = bwd_ws(p);
+  if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
+  rc = check_device();
+  if (rc) return rc;
+  long long dys[4];
+  for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
+  const m3ssd::tc::BwdOut out = m3ssd::tc::contiguous_bwd_out(
+      p, static_cast<float*>(a->dx), static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
+      static_cast<float2*>(a->dC), a->ddt);
+  return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
+                            static_cast<cudaStream_t>(stream), hT, dhT, dh0);
+}
+
 int m3ssd_selftest_bounded_waits(void* workspace, size_t workspace_bytes, void* stream) {
   if (!workspace || workspace_bytes < 256) return M3SSD_ERR_WORKSPACE;
   if (!aligned(workspace, 256)) return M3SSD_ERR_ALIGN;

@@ -108,6 +108,12 @@ struct BwdParams {
   uint32_t* flags;
   uint32_t* counter;
   uint32_t* err;
+  // state carry (optional): gradient of the final state in, of the initial state out, both
+  // (B, H, N, D) complex64 = the transpose of a state tile; <dhT, hT> per sequence (the
+  // [l = 63] d Sigma term of the last chunk)
+  const float2* dhT;
+  float2* dh0;
+  const float2* dgam_last;
 };
 
 // (sequence, chunk) of a ticket: tickets run over sequences fastest, chunks in reverse order
@@ -409,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const ChunkRec& rec = m.rec[ph];
         const float2 dgam = q.z < p.nc - 1 ? make_float2(m.dgam[ph].x, m.dgam[ph].y)
-                                           : make_float2(0.f, 0.f);
+                            : p.dgam_last != nullptr ? p.dgam_last[q.bh]
+                                                     : make_float2(0.f, 0.f);
         const int t0 = q.z * 64;
         float2 dv[2];
 #pragma unroll
@@ -528,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&m.bar_ctl);
         const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
         // Each remaining contraction as soon as its operands are written and its TMEM columns
-        // read        // after epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
+        // read.
+        // After epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
         // dXb = conj(B') dS' into the columns of G and dM
         mbar_wait(&m.bar_ops2, ph, p.err, kErrMmaWait);
         tc_fence_after_sync();
@@ -822,6 +830,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           dsz[4 * i + 2] = v.z;
           dsz[4 * i + 3] = v.w;
         }
+      } else if (p.dhT != nullptr) {  // last chunk: dS = the final state's gradient, transposed
+        const float2* src = p.dhT + (long long)q.bh * 64 * 64 + 16 * sub + (lane >> 2);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int n = 16 * grp + 4 * (2 * (i & 1) + u) + (lane & 3);
+            const float2 v = __ldcg(src + n * 64 + 8 * (i >> 1));
+            dsz[4 * i + 2 * u] = v.x;
+            dsz[4 * i + 2 * u + 1] = v.y;
+          }
       } else {
 #pragma unroll
         for (int c = 0; c < 16; ++c) dsz[c] = 0.f;
@@ -921,6 +940,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
           }
+        } else if (p.dh0 != nullptr) {  // first chunk: dS_{-1} is the initial state's gradient
+          const float2 g = rec.g;
+          float2* dst = p.dh0 + (long long)q.bh * 64 * 64 + 16 * sub + rr;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* qv = (i >> 1) ? qb : qa;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int k = 2 * (i & 1) + u, c = 4 * i + 2 * u;
+              const float qre = qv[4 * k] + qv[4 * k + 2], qim = qv[4 * k + 1] + qv[4 * k + 3];
+              const int n = 16 * grp + 4 * k + (int)q4;
+              __stcg(dst + n * 64 + 8 * (i >> 1),
+                     make_float2(qre + g.x * dsz[c] + g.y * dsz[c + 1],
+                                 -qim + g.x * dsz[c + 1] - g.y * dsz[c]));
+            }
+          }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -968,13 +1003,44 @@ __global__ void __launch_bounds__(256) k_bwd_tc_dA(const float2* __restrict__ da
   if (threadIdx.x == 0) dA[h] = red[0];
 }
 
+// <dS_{nc-1}, conj(H_{nc})> of a sequence with a final-state gradient: the d Sigma term the last
+// chunk's position 63 gets from its exit state (the other chunks take it from the chunk after
+// them). One block per (b, h), (N, D) complex64 tiles of the final state and its gradient.
+__global__ void __launch_bounds__(256) k_bwd_tc_dgam_last(const float2* __restrict__ hT,
+                                                          const float2* __restrict__ dhT,
+                                                          float2* __restrict__ out) {
+  __shared__ float2 red[8];
+  const long long base = (long long)blockIdx.x * 64 * 64;
+  float2 acc = make_float2(0.f, 0.f);
+  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+    const float2 g = dhT[base + i], h = hT[base + i];
+    acc.x += g.x * h.x + g.y * h.y;
+    acc.y += g.y * h.x - g.x * h.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float2 t = red[0];
+    for (int w = 1; w < 8; ++w) {
+      t.x += red[w].x;
+      t.y += red[w].y;
+    }
+    out[blockIdx.x] = t;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 namespace {
 
 struct BwdLayout {
-  size_t flags, ring, dgring, dapart, total;
+  size_t flags, ring, dgring, dapart, dglast, total;
 };
 
 BwdLayout bwd_layout(const Problem& p) {
@@ -985,7 +1051,8 @@ BwdLayout bwd_layout(const Problem& p) {
   L.ring = al(L.flags + 4 * bh * nc);
   L.dgring = al(L.ring + bh * 4 * 64 * 128 * sizeof(float));
   L.dapart = al(L.dgring + bh * 4 * sizeof(float4));
-  L.total = al(L.dapart + bh * nc * sizeof(float2));
+  L.dglast = al(L.dapart + bh * nc * sizeof(float2));
+  L.total = al(L.dglast + bh * sizeof(float2));
   return L;
 }
 
@@ -1009,7 +1076,8 @@ BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, f
 }
 
 int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
-            const BwdOut& out, void* ws, cudaStream_t st) {
+            const BwdOut& out, void* ws, cudaStream_t st, const void* hT, const void* dhT,
+            void* dh0) {
   const BwdLayout L = bwd_layout(p);
   BwdParams bp{};
   bp.Bsz = p.Bsz;
@@ -1054,6 +1122,12 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
   bp.ring = reinterpret_cast<float*>(base + L.ring);
   bp.dgring = reinterpret_cast<float4*>(base + L.dgring);
   bp.dapart = reinterpret_cast<float2*>(base + L.dapart);
+  // state carry: with a final-state gradient the final state must come too (the last chunk's
+  // d Sigma term); the initial state's gradient is written whenever asked for
+  if ((dhT != nullptr) != (hT != nullptr)) return M3SSD_ERR_NULL;
+  bp.dhT = static_cast<const float2*>(dhT);
+  bp.dh0 = static_cast<float2*>(dh0);
+  bp.dgam_last = dhT != nullptr ? reinterpret_cast<const float2*>(base + L.dglast) : nullptr;
   CUtensorMap tmB, tmC, tmDX, tmDB, tmDC;
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
     return M3SSD_ERR_LAUNCH;
@@ -1077,6 +1151,9 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
       cudaSuccess)
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
+  if (dhT != nullptr)
+    k_bwd_tc_dgam_last<<<p.Bsz * p.H, 256, 0, st>>>(static_cast<const float2*>(hT),
+                                                    bp.dhT, reinterpret_cast<float2*>(base + L.dglast));
   kern<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmDX, tmDB, tmDC, bp);
   k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, out.dA);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;

@@ -71,6 +71,10 @@ struct FwdParams {
   uint32_t* counter;
   uint32_t* err;
   int y_bf16;  // y leaves as bfloat16 (one 64-column staging segment) instead of float32 (two)
+  // state carry (optional): initial state h0 and final state hT, (B, H, N, D) complex64
+  // contiguous = s[n][p] of the reference's recurrence, the transpose of a state tile H[p][n]
+  const float2* h0;
+  float2* hT;
 };
 
 __device__ __forceinline__ void load_x16(const FwdParams& p, int b, int t, int h, int p0,
@@ -323,9 +327,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       mma_commit(&m.bar_mma1);
     }
     float hz[32];
-    if (z == 0) {
+    if (z == 0) {  // H_0: zero, or the initial state (row p = r, complex n = 32 wg + 16 part + c/2)
+      if (p.h0 != nullptr) {
+        const float2* src = p.h0 + ((long long)bh * 64 + 32 * wg + 16 * part) * 64 + r;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) hz[c] = 0.f;
+        for (int c = 0; c < 16; ++c) {
+          const float2 v = __ldcg(src + c * 64);
+          hz[2 * c] = v.x;
+          hz[2 * c + 1] = v.y;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) hz[c] = 0.f;
+      }
     } else if (h_early) {  // H_z already published: load it while the MMAs run
       const float4* src =
           reinterpret_cast<const float4*>(p.states + ((long long)bh * p.nc + z) * 64 * 128) + tid;
@@ -444,10 +458,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           hn[c] = hv.x + sv.x;
           hn[c + 1] = hv.y + sv.y;
         }
-        if (z == 0) {
+        if (z == 0) {  // the chunk-0 state tile the backward reads: H_0
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            __stcg(tile0 + (4 * hh + i) * kThreads, make_float4(0.f, 0.f, 0.f, 0.f));
+            __stcg(tile0 + (4 * hh + i) * kThreads,
+                   make_float4(hz[16 * hh + 4 * i], hz[16 * hh + 4 * i + 1],
+                               hz[16 * hh + 4 * i + 2], hz[16 * hh + 4 * i + 3]));
         }
         if (z + 1 < p.nc) {
           float4* dst = tile0 + (long long)(z + 1) * 64 * 32;
@@ -455,6 +471,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int i = 0; i < 4; ++i)
             __stcg(dst + (4 * hh + i) * kThreads,
                    make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
+        } else if (p.hT != nullptr) {  // the final state H_nc, transposed to (n, p)
+          float2* dst = p.hT + ((long long)bh * 64 + 32 * wg + 16 * part + 8 * hh) * 64 + r;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) __stcg(dst + c * 64, make_float2(hn[2 * c], hn[2 * c + 1]));
         }
       }
     }
@@ -638,7 +658,8 @@ size_t fwd_workspace_bytes(const Problem& p) {
   return 256 + 4 * (size_t)p.Bsz * p.H * nc;
 }
 
-int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st) {
+int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, const void* h0,
+            void* hT) {
   FwdParams fp{};
   fp.Bsz = p.Bsz;
   fp.T = p.T;
@@ -659,6 +680,8 @@ int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st) 
   fp.counter = w + 1;
   fp.flags = w + 64;
   fp.y_bf16 = p.y_bf16;
+  fp.h0 = static_cast<const float2*>(h0);
+  fp.hT = static_cast<float2*>(hT);
   CUtensorMap tmB, tmC, tmY;
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs) ||
       !(p.y_bf16 ? encode_out_map_bf16(&tmY, y, p) : encode_out_tensor_map(&tmY, y, p, 64)))

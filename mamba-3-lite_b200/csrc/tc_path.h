@@ -39,18 +39,20 @@ bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
 // 32-float (128-byte) column segments, 128-byte swizzled in shared memory. False if the pointer
 // is not 16-byte aligned.
 bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int row_floats);
-// the same over a strided (B, T, rows, row_floats) fp32 output: strides of a row, a time step and
-// a batch entry in floats, each a multiple of 4. False for a misaligned pointer or stride.
 // 4D map over a contiguous (B, T, H, 64) bfloat16 output, box of 64 rows x 64 values (128-byte
 // rows, 128-byte swizzled in shared memory)
 bool encode_out_map_bf16(CUtensorMap* map, void* ptr, const Problem& p);
+// the same over a strided (B, T, rows, row_floats) fp32 output: strides of a row, a time step and
+// a batch entry in floats, each a multiple of 4. False for a misaligned pointer or stride.
 bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int row_floats,
                             int rows, long long s_row, long long s_t, long long s_b);
 
 // head_dim = state_dim = 64, real x, B/C with contiguous state dim and 16-byte aligned strides
 bool fwd_supported(const Problem& p);
 size_t fwd_workspace_bytes(const Problem& p);
-int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st);
+// h0 / hT (optional): initial and final state, (B, H, N, D) complex64 contiguous
+int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st,
+            const void* h0 = nullptr, void* hT = nullptr);
 
 bool bwd_supported(const Problem& p);
 
@@ -72,9 +74,12 @@ struct BwdOut {
 };
 BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, float2* dC,
                           float* ddt);
-// dy: float32, or bfloat16 with p.y_bf16; strides in elements
+// dy: float32, or bfloat16 with p.y_bf16; strides in elements. State carry (optional, all
+// (B, H, N, D) complex64 contiguous): hT the forward's final state and dhT its gradient (both or
+// neither), dh0 receives the gradient of the initial state.
 int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
-            const BwdOut& out, void* ws, cudaStream_t st);
+            const BwdOut& out, void* ws, cudaStream_t st, const void* hT = nullptr,
+            const void* dhT = nullptr, void* dh0 = nullptr);
 
 }  // namespace tc
 }  // namespace m3ssd

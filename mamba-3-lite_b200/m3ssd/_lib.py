@@ -99,6 +99,10 @@ SIGNATURES = {
     "m3ssd_fwd_static_scratch": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
     "m3ssd_fwd_proj": (ctypes.c_int, [ctypes.POINTER(ProjFwdArgs), ctypes.c_void_p]),
     "m3ssd_bwd_proj": (ctypes.c_int, [ctypes.POINTER(ProjBwdArgs), ctypes.c_void_p]),
+    "m3ssd_fwd_state": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p]),
+    "m3ssd_bwd_state": (ctypes.c_int, [ctypes.POINTER(BwdArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p]),
     "m3ssd_selftest_bounded_waits": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t,
                                                     ctypes.c_void_p]),
 }

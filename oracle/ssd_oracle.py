@@ -18,7 +18,9 @@ Reference: models/ssd_complex.py in atandra2000/Mamba-3-Lite.
 * ``ssd_naive_grads``   - the adjoint of that recurrence: gradients of ``sum(dy * Re(y))`` for
                            x, A, B_t, C_t, dt in PyTorch's convention for complex leaves
                            (grad = dL/dRe + i dL/dIm). This is an independent derivation of what
-                           torch.autograd returns through models/ssd_complex.py:58-119.
+                           torch.autograd returns through models/ssd_complex.py:58-119. Both take
+                           an optional initial state (and final-state gradient) for the state
+                           carry of segmented calls.
 
 Shapes follow the reference: x (B,T,H,D) real or complex, A (H,) complex, B_t/C_t (B,T,H,N)
 complex, dt (B,T,H) real and pre-softplus.
@@ -119,11 +121,13 @@ def ssd_chunkwise(x, A, B_t, C_t, dt, chunk_size=64):
     return Y.reshape(Bsz, T + pad, H, D)[:, :T]
 
 
-def ssd_naive(x, A, B_t, C_t, dt, dtype=np.complex128):
+def ssd_naive(x, A, B_t, C_t, dt, dtype=np.complex128, s0=None, return_state=False):
     """The O(T) recurrence of models/ssd_complex.py:17-33; returns complex (B,T,H,D).
 
     With ``dtype=np.complex64`` it follows the reference's precision; the default complex128 is
-    the ground truth used for error reports.
+    the ground truth used for error reports. ``s0`` (B,H,N,D) is an initial state (zero in the
+    reference); with ``return_state`` the final state s_T is returned as well (the state carry
+    of an operator call split into segments: no counterpart in the reference's code).
     """
     real_t = np.float64 if dtype == np.complex128 else np.float32
     sp = softplus_f64(dt) if real_t is np.float64 else softplus_f32(dt)
@@ -133,16 +137,19 @@ def ssd_naive(x, A, B_t, C_t, dt, dtype=np.complex128):
     Ct = np.asarray(C_t).astype(dtype)
     Bsz, T, H, D = x.shape
     N = Bt.shape[-1]
-    s = np.zeros((Bsz, H, N, D), dtype=dtype)
+    s = np.zeros((Bsz, H, N, D), dtype=dtype) if s0 is None else np.asarray(s0).astype(dtype)
     ys = np.empty((Bsz, T, H, D), dtype=dtype)
     for t in range(T):
         s = Abar[:, t, :, None, None] * s + Bt[:, t, :, :, None] * x[:, t, :, None, :]
         ys[:, t] = np.einsum("bhn,bhnd->bhd", Ct[:, t], s)
-    return ys
+    return (ys, s) if return_state else ys
 
 
-def ssd_naive_grads(x, A, B_t, C_t, dt, dy):
+def ssd_naive_grads(x, A, B_t, C_t, dt, dy, s0=None, dsT=None):
     """Gradients of L = sum(dy * Re(ssd_naive(...))) in complex128, PyTorch's convention.
+
+    With an initial state ``s0`` and/or an upstream gradient ``dsT`` of the final state
+    (L += Re(sum conj(dsT) s_T)), a sixth result is returned: ds0, the gradient of s0.
 
     Returns ``(dx, dA, dB, dC, ddt)``: dx real when x is real, complex otherwise; dA (H,) complex;
     dB/dC (B,T,H,N) complex; ddt (B,T,H) real. The adjoint state runs backwards in time:
@@ -163,7 +170,9 @@ def ssd_naive_grads(x, A, B_t, C_t, dt, dy):
     N = Bt.shape[-1]
 
     states = np.empty((Bsz, T, H, N, D), dtype=np.complex128)
-    s = np.zeros((Bsz, H, N, D), dtype=np.complex128)
+    s0c = (np.zeros((Bsz, H, N, D), dtype=np.complex128) if s0 is None
+           else np.asarray(s0).astype(np.complex128))
+    s = s0c
     for t in range(T):
         s = Abar[:, t, :, None, None] * s + Bt[:, t, :, :, None] * X[:, t, :, None, :]
         states[:, t] = s
@@ -172,13 +181,14 @@ def ssd_naive_grads(x, A, B_t, C_t, dt, dy):
     dB = np.empty_like(Bt)
     dC = np.empty_like(Ct)
     da = np.empty((Bsz, T, H), dtype=np.complex128)
-    g = np.zeros((Bsz, H, N, D), dtype=np.complex128)
+    g = (np.zeros((Bsz, H, N, D), dtype=np.complex128) if dsT is None
+         else np.asarray(dsT).astype(np.complex128))
     for t in range(T - 1, -1, -1):
         g = g + np.conj(Ct[:, t])[..., None] * dy[:, t, :, None, :]
         dC[:, t] = np.einsum("bhd,bhnd->bhn", dy[:, t], np.conj(states[:, t]))
         dB[:, t] = np.einsum("bhnd,bhd->bhn", g, np.conj(X[:, t]))
         dX[:, t] = np.einsum("bhnd,bhn->bhd", g, np.conj(Bt[:, t]))
-        prev = states[:, t - 1] if t > 0 else np.zeros_like(g)
+        prev = states[:, t - 1] if t > 0 else s0c
         dAbar = np.einsum("bhnd,bhnd->bh", g, np.conj(prev))
         da[:, t] = dAbar * np.conj(Abar[:, t])
         g = np.conj(Abar[:, t])[..., None, None] * g
@@ -186,4 +196,6 @@ def ssd_naive_grads(x, A, B_t, C_t, dt, dy):
     dA = np.einsum("bth,bth->h", da, sp)
     ddt = np.real(da * np.conj(A)[None, None, :]) * dsp
     dx = dX if x_is_complex else dX.real
+    if s0 is not None or dsT is not None:
+        return dx, dA, dB, dC, ddt, g
     return dx, dA, dB, dC, ddt

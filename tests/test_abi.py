@@ -92,6 +92,68 @@ def test_null_arguments_rejected_before_any_device_work(lib):
     assert lib.m3ssd_bwd(ctypes.byref(b), None) == 1
 
 
+def _fake_fwd_args(p, ptr=0x10000):
+    """Args whose device pointers are non-null and aligned but never dereferenced: every case
+    below is rejected by host-side validation before the library looks at the device."""
+    a = _lib.FwdArgs()
+    a.prob = p
+    a.x = a.A = a.B = a.C = a.dt = a.y = a.states = a.workspace = ptr
+    a.workspace_bytes = 1 << 30
+    _contiguous_strides(a, p)
+    return a
+
+
+def _fake_bwd_args(p, ptr=0x10000):
+    b = _lib.BwdArgs()
+    b.prob = p
+    b.x = b.A = b.B = b.C = b.dt = b.dy = b.states = ptr
+    b.dx = b.dA = b.dB = b.dC = b.ddt = b.workspace = ptr
+    b.workspace_bytes = 1 << 30
+    _contiguous_strides(b, p)
+    b.dy_strides = _lib.I64x4(*b.x_strides)
+    return b
+
+
+def _contiguous_strides(a, p):
+    T, H, D, N = p.seqlen, p.nheads, p.headdim, p.dstate
+    a.x_strides = _lib.I64x4(T * H * D, H * D, D, 1)
+    a.b_strides = _lib.I64x4(T * H * N, H * N, N, 1)
+    a.c_strides = _lib.I64x4(T * H * N, H * N, N, 1)
+    a.dt_strides = _lib.I64x3(T * H, H, 1)
+
+
+def test_state_carry_entry_points_validate_on_the_host(lib):
+    assert lib.m3ssd_fwd_state(None, None, None, None) == 1
+    assert lib.m3ssd_bwd_state(None, None, None, None, None) == 1
+    # tensor-core shapes with T a multiple of 64 only
+    for kw in (dict(headdim=32), dict(seqlen=100), dict(flags=0x1), dict(flags=0x10)):
+        assert lib.m3ssd_fwd_state(ctypes.byref(_fake_fwd_args(prob(**kw))), None, None,
+                                   None) == 2, kw
+        assert lib.m3ssd_bwd_state(ctypes.byref(_fake_bwd_args(prob(**kw))), None, None, None,
+                                   None) == 2, kw
+    a = _lib.FwdArgs()
+    a.prob = prob()
+    assert lib.m3ssd_fwd_state(ctypes.byref(a), None, None, None) == 1
+    # a final state without its gradient (or the reverse) is rejected
+    b = _fake_bwd_args(prob())
+    assert lib.m3ssd_bwd_state(ctypes.byref(b), 0x20000, None, None, None) == 1
+    assert lib.m3ssd_bwd_state(ctypes.byref(b), None, 0x20000, None, None) == 1
+    # state pointers are complex64: 8-byte aligned
+    assert lib.m3ssd_fwd_state(ctypes.byref(_fake_fwd_args(prob())), 0x20004, None, None) == 5
+    assert lib.m3ssd_bwd_state(ctypes.byref(b), None, None, 0x20004, None) == 5
+
+
+def test_state_carry_cpu_tensors_raise_no_fallback():
+    import torch
+    from m3ssd import ssd_complex_chunkwise_state
+    x = torch.randn(1, 64, 2, 64)
+    A = torch.randn(2, dtype=torch.complex64)
+    B = torch.randn(1, 64, 2, 64, dtype=torch.complex64)
+    dt = torch.randn(1, 64, 2)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ssd_complex_chunkwise_state(x, A, B, B, dt)
+
+
 def test_error_maps_to_runtime_error():
     with pytest.raises(RuntimeError, match="chunk_size"):
         _lib.check(3)

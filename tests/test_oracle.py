@@ -113,3 +113,55 @@ def test_metrics_floor():
     assert metrics.normwise(got, ref) == pytest.approx(5e-7)
     # second entry is judged against the floor 1e-3 * max|ref| = 2e-3
     assert metrics.floored(got, ref) == pytest.approx(1e-6 / 2e-3)
+
+
+def _small_state_case(seed=5, B=1, T=12, H=2, D=3, N=2):
+    rng = np.random.default_rng(seed)
+    inp = cases.ref_style_inputs(seed, B, T, H, D, N, complex_x=False)
+    cshape = (B, H, N, D)
+    s0 = rng.standard_normal(cshape) + 1j * rng.standard_normal(cshape)
+    dsT = rng.standard_normal(cshape) + 1j * rng.standard_normal(cshape)
+    dy = rng.standard_normal((B, T, H, D))
+    return inp, s0, dsT, dy
+
+
+def test_naive_state_carry_chains_segments():
+    """The recurrence cut at t = 5 and restarted from the carried state is the same recurrence."""
+    inp, s0, _, _ = _small_state_case()
+    y, sT = O.ssd_naive(**inp, s0=s0, return_state=True)
+    first = {k: (v if k == "A" else v[:, :5]) for k, v in inp.items()}
+    rest = {k: (v if k == "A" else v[:, 5:]) for k, v in inp.items()}
+    y1, s1 = O.ssd_naive(**first, s0=s0, return_state=True)
+    y2, s2 = O.ssd_naive(**rest, s0=s1, return_state=True)
+    np.testing.assert_allclose(np.concatenate([y1, y2], axis=1), y, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(s2, sT, rtol=1e-12, atol=1e-12)
+
+
+def test_adjoint_state_gradients_match_finite_differences():
+    """ds0 and the other gradients of L = sum(dy Re y) + Re sum(conj(dsT) s_T), checked by
+    central differences of the fp64 recurrence (PyTorch's convention: dL/dRe + i dL/dIm)."""
+    inp, s0, dsT, dy = _small_state_case()
+
+    def loss(inp_, s0_):
+        y, sT = O.ssd_naive(**inp_, s0=s0_, return_state=True)
+        return float(np.sum(dy * y.real) + np.sum((np.conj(dsT) * sT).real))
+
+    g = O.ssd_naive_grads(**inp, dy=dy, s0=s0, dsT=dsT)
+    assert len(g) == 6
+    eps = 1e-6
+    idx = (0, 1, 1, 2)
+    for part, unit in ((0, 1.0), (1, 1j)):
+        sp, sm = s0.copy(), s0.copy()
+        sp[idx] += eps * unit
+        sm[idx] -= eps * unit
+        fd = (loss(inp, sp) - loss(inp, sm)) / (2 * eps)
+        got = g[5][idx].real if part == 0 else g[5][idx].imag
+        assert abs(fd - got) < 1e-6 * max(1.0, abs(fd)), (part, fd, got)
+    # dt at one position (real input), through the carried state as well
+    dtp, dtm = dict(inp), dict(inp)
+    dtp["dt"] = inp["dt"].astype(np.float64).copy()
+    dtm["dt"] = inp["dt"].astype(np.float64).copy()
+    dtp["dt"][0, 3, 1] += eps
+    dtm["dt"][0, 3, 1] -= eps
+    fd = (loss(dtp, s0) - loss(dtm, s0)) / (2 * eps)
+    assert abs(fd - g[4][0, 3, 1]) < 1e-6 * max(1.0, abs(fd))
