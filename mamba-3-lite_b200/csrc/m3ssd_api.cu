@@ -77,14 +77,43 @@ Problem make_problem(const m3ssd_problem* pr) {
   return p;
 }
 
-size_t bwd_ws(const Problem& p) {
-  const size_t a = m3ssd::simt::bwd_workspace_bytes(p), b = m3ssd::tc::bwd_workspace_bytes(p);
+
+// Scratch of a forward / backward call: the larger of the two paths' needs; the tensor-core path
+// adds the chained-pass buffers when the shape runs as several chains per sequence.
+size_t bwd_ws(const m3ssd_problem* pr, const Problem& p) {
+  size_t a = m3ssd::simt::bwd_workspace_bytes(p), b = m3ssd::tc::bwd_workspace_bytes(p);
+  if (tc_shape(pr)) {
+    const int G = m3ssd::tc::chains_for(p, true);
+    if (G > 1) b = m3ssd::tc::bwd_chains_workspace_bytes(p, G);
+  }
   return a > b ? a : b;
 }
 
-size_t fwd_ws(const Problem& p) {
-  const size_t a = m3ssd::simt::fwd_workspace_bytes(p), b = m3ssd::tc::fwd_workspace_bytes(p);
+size_t fwd_ws(const m3ssd_problem* pr, const Problem& p) {
+  size_t a = m3ssd::simt::fwd_workspace_bytes(p), b = m3ssd::tc::fwd_workspace_bytes(p);
+  if (tc_shape(pr)) {
+    const int G = m3ssd::tc::chains_for(p, false);
+    if (G > 1) b = m3ssd::tc::fwd_chains_workspace_bytes(p, G);
+  }
   return a > b ? a : b;
+}
+
+// The tensor-core forward / backward, in one pass or as chains (m3ssd::tc::chains_for)
+int tc_fwd(const Problem& p, void* y, void* states, void* ws, void* stream, const void* h0,
+           void* hT) {
+  const auto st = static_cast<cudaStream_t>(stream);
+  const int G = m3ssd::tc::chains_for(p, false);
+  if (G > 1) return m3ssd::tc::run_fwd_chains(p, y, states, ws, st, h0, hT, G);
+  return m3ssd::tc::run_fwd(p, y, states, ws, st, h0, hT);
+}
+
+int tc_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
+           const m3ssd::tc::BwdOut& out, void* ws, void* stream, const void* hT, const void* dhT,
+           void* dh0) {
+  const auto st = static_cast<cudaStream_t>(stream);
+  const int G = m3ssd::tc::chains_for(p, true);
+  if (G > 1) return m3ssd::tc::run_bwd_chains(p, dy, dys, states, out, ws, st, hT, dhT, dh0, G);
+  return m3ssd::tc::run_bwd(p, dy, dys, states, out, ws, st, hT, dhT, dh0);
 }
 
 bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
@@ -243,12 +272,12 @@ size_t m3ssd_states_bytes(const m3ssd_problem* prob) {
 
 size_t m3ssd_fwd_workspace_bytes(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  return fwd_ws(make_problem(prob));
+  return fwd_ws(prob, make_problem(prob));
 }
 
 size_t m3ssd_bwd_workspace_bytes(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  return bwd_ws(make_problem(prob));
+  return bwd_ws(prob, make_problem(prob));
 }
 
 const char* m3ssd_fwd_path(const m3ssd_problem* prob) {
@@ -263,8 +292,12 @@ const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
 
 int m3ssd_launch_count(const m3ssd_problem* prob, int backward) {
   if (check_problem(prob) != M3SSD_OK) return 0;
-  if (backward) return tc_shape(prob) ? m3ssd::tc::kBwdLaunches : m3ssd::simt::kBwdLaunches;
-  return tc_shape(prob) ? m3ssd::tc::kFwdLaunches : m3ssd::simt::kFwdLaunches;
+  if (!tc_shape(prob)) return backward ? m3ssd::simt::kBwdLaunches : m3ssd::simt::kFwdLaunches;
+  // the chained form: two passes (the records once) plus the segment chain (and, backward, the
+  // segments' end-state terms)
+  const bool chained = m3ssd::tc::chains_for(make_problem(prob), backward != 0) > 1;
+  if (backward) return chained ? 2 * m3ssd::tc::kBwdLaunches + 2 : m3ssd::tc::kBwdLaunches;
+  return chained ? 2 * m3ssd::tc::kFwdLaunches : m3ssd::tc::kFwdLaunches;
 }
 
 int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
@@ -277,7 +310,7 @@ int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
   if (rc) return rc;
   if (!a->y || !a->states) return M3SSD_ERR_NULL;
   if (!aligned(a->y, 4) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
-  const size_t need = fwd_ws(p);
+  const size_t need = fwd_ws(&a->prob, p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
@@ -285,7 +318,7 @@ int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
   if (tc_shape(&a->prob) && m3ssd::tc::fwd_supported(p)) {
     // y leaves the tensor-core forward through TMA stores
     if (!aligned(a->y, 16)) return M3SSD_ERR_ALIGN;
-    return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream));
+    return tc_fwd(p, a->y, a->states, a->workspace, stream, nullptr, nullptr);
   }
   if (p.y_bf16) return M3SSD_ERR_SHAPE;  // B / C strides the tensor-core path cannot take
   return m3ssd::simt::run_fwd(p, static_cast<float*>(a->y), a->states, a->workspace,
@@ -307,7 +340,7 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
       !aligned(a->dA, 8) ||
       !aligned(a->dB, 8) || !aligned(a->dC, 8) || !aligned(a->ddt, 4))
     return M3SSD_ERR_ALIGN;
-  const size_t need = bwd_ws(p);
+  const size_t need = bwd_ws(&a->prob, p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
@@ -322,8 +355,7 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
     const m3ssd::tc::BwdOut out = m3ssd::tc::contiguous_bwd_out(
         p, static_cast<float*>(a->dx), static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
         static_cast<float2*>(a->dC), a->ddt);
-    return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
-                              static_cast<cudaStream_t>(stream));
+    return tc_bwd(p, a->dy, dys, a->states, out, a->workspace, stream, nullptr, nullptr, nullptr);
   }
   if (p.y_bf16) return M3SSD_ERR_SHAPE;
   return m3ssd::simt::run_bwd(p, static_cast<const float*>(a->dy), dys, a->states, a->dx,
@@ -363,12 +395,12 @@ int m3ssd_fwd_proj(const m3ssd_proj_fwd_args* a, void* stream) {
   if (rc) return rc;
   if (!a->y || !a->states) return M3SSD_ERR_NULL;
   if (!aligned(a->y, 16) || !aligned(a->states, 16)) return M3SSD_ERR_ALIGN;
-  const size_t need = fwd_ws(p);
+  const size_t need = fwd_ws(&a->prob, p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
   if (rc) return rc;
-  return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream));
+  return tc_fwd(p, a->y, a->states, a->workspace, stream, nullptr, nullptr);
 }
 
 int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* a, void* stream) {
@@ -383,7 +415,7 @@ int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* a, void* stream) {
   const int64_t sb = a->dproj_strides[0], st = a->dproj_strides[1];
   if (sb <= 0 || st <= 0) return M3SSD_ERR_SHAPE;
   if (!aligned(a->dproj, 16) || sb % 4 || st % 4) return M3SSD_ERR_ALIGN;
-  const size_t need = bwd_ws(p);
+  const size_t need = bwd_ws(&a->prob, p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
@@ -400,8 +432,7 @@ int m3ssd_bwd_proj(const m3ssd_proj_bwd_args* a, void* stream) {
   out.planar = 1;
   out.s_b = sb;
   out.s_t = st;
-  return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
-                            static_cast<cudaStream_t>(stream));
+  return tc_bwd(p, a->dy, dys, a->states, out, a->workspace, stream, nullptr, nullptr, nullptr);
 }
 
 int m3ssd_fwd_state(const m3ssd_fwd_args* a, const void* h0, void* hT, void* stream) {
@@ -417,13 +448,12 @@ int m3ssd_fwd_state(const m3ssd_fwd_args* a, const void* h0, void* hT, void* str
   if (!a->y || !a->states) return M3SSD_ERR_NULL;
   if (!aligned(a->y, 16) || !aligned(a->states, 16) || !aligned(h0, 8) || !aligned(hT, 8))
     return M3SSD_ERR_ALIGN;
-  const size_t need = fwd_ws(p);
+  const size_t need = fwd_ws(&a->prob, p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
   if (rc) return rc;
-  return m3ssd::tc::run_fwd(p, a->y, a->states, a->workspace, static_cast<cudaStream_t>(stream),
-                            h0, hT);
+  return tc_fwd(p, a->y, a->states, a->workspace, stream, h0, hT);
 }
 
 int m3ssd_bwd_state(const m3ssd_bwd_args* a, const void* hT, const void* dhT, void* dh0,
@@ -444,7 +474,7 @@ int m3ssd_bwd_state(const m3ssd_bwd_args* a, const void* hT, const void* dhT, vo
       !aligned(a->dA, 8) || !aligned(a->dB, 16) || !aligned(a->dC, 16) || !aligned(a->ddt, 4) ||
       !aligned(hT, 8) || !aligned(dhT, 8) || !aligned(dh0, 8))
     return M3SSD_ERR_ALIGN;
-  const size_t need = bwd_ws(p);
+  const size_t need = bwd_ws(&a->prob, p);
   if (!a->workspace || a->workspace_bytes < need) return M3SSD_ERR_WORKSPACE;
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
@@ -454,8 +484,7 @@ int m3ssd_bwd_state(const m3ssd_bwd_args* a, const void* hT, const void* dhT, vo
   const m3ssd::tc::BwdOut out = m3ssd::tc::contiguous_bwd_out(
       p, static_cast<float*>(a->dx), static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
       static_cast<float2*>(a->dC), a->ddt);
-  return m3ssd::tc::run_bwd(p, a->dy, dys, a->states, out, a->workspace,
-                            static_cast<cudaStream_t>(stream), hT, dhT, dh0);
+  return tc_bwd(p, a->dy, dys, a->states, out, a->workspace, stream, hT, dhT, dh0);
 }
 
 int m3ssd_selftest_bounded_waits(void* workspace, size_t workspace_bytes, void* stream) {

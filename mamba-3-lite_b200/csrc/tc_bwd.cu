@@ -114,17 +114,39 @@ struct BwdParams {
   const float2* dhT;
   float2* dh0;
   const float2* dgam_last;
+  int G, seg;  // chains per sequence and chunks per chain (see TicketPos)
 };
 
-// (sequence, chunk) of a ticket: tickets run over sequences fastest, chunks in reverse order
+// (sequence, chunk) of a ticket: tickets run over sequences (then segments) fastest, chunks
+// within a segment in reverse order. Each sequence's chunks form G chains of seg = nc / G chunks
+// (G = 1: one chain); a chain's last chunk takes dS from dhT (or zero) and its first chunk's
+// carry is the chain's entry-state gradient. sg = bh * G + segment indexes per-chain data.
 struct TicketPos {
-  int bh, z, b, h;
+  int bh, z, b, h, sg;
+  bool first, last;
 };
-__device__ __forceinline__ TicketPos ticket_pos(int tk, int BH, int H, int nc) {
+template <bool kChains>
+__device__ __forceinline__ TicketPos ticket_pos(int tk, int BH, int H, int G, int seg) {
   TicketPos q;
-  const int zr = tk / BH;
-  q.bh = tk - zr * BH;
-  q.z = nc - 1 - zr;
+  if constexpr (!kChains) {  // one chain per sequence (seg = nc)
+    const int zr = tk / BH;
+    q.bh = q.sg = tk - zr * BH;
+    q.z = seg - 1 - zr;
+    q.first = q.z == 0;
+    q.last = zr == 0;
+    q.b = q.bh / H;
+    q.h = q.bh - q.b * H;
+    return q;
+  }
+  const int zr = tk / (BH * G);
+  const int rest = tk - zr * BH * G;
+  const int sgm = rest / BH;
+  q.bh = rest - sgm * BH;
+  const int j = seg - 1 - zr;
+  q.z = sgm * seg + j;
+  q.sg = q.bh * G + sgm;
+  q.first = j == 0;
+  q.last = j == seg - 1;
   q.b = q.bh / H;
   q.h = q.bh - q.b * H;
   return q;
@@ -173,16 +195,16 @@ static __device__ __noinline__ void ctl_load_h(uint8_t* smem, Misc* m, const flo
 static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const float* ring,
                                                 const float4* dgring, const uint32_t* flags,
                                                 uint32_t* err, int nc, TicketPos q, int slot) {
-  if (q.z == nc - 1) {
+  if (q.last) {
     mbar_arrive(&m->bar_ds);
     return;
   }
   flag_wait(flags + (long long)q.bh * nc + q.z, err);
   fence_proxy_async_global();  // the ring was written with plain stores by another CTA
   mbar_arrive_expect_tx(&m->bar_ds, 32768u + 16u);
-  bulk_load(smem + OFF_DS, ring + ((long long)q.bh * 4 + (q.z & 3)) * 64 * 128, 32768u,
+  bulk_load(smem + OFF_DS, ring + ((long long)q.sg * 4 + (q.z & 3)) * 64 * 128, 32768u,
             &m->bar_ds);
-  bulk_load(&m->dgam[slot], dgring + (long long)q.bh * 4 + (q.z & 3), 16u, &m->bar_ds);
+  bulk_load(&m->dgam[slot], dgring + (long long)q.sg * 4 + (q.z & 3), 16u, &m->bar_ds);
 }
 // TMA stores of a 64-row output tile from its 32-float staging segments (segments 0, 1 at off01,
 // 2, 3 at off23), one bulk group. hp > 0: planar complex tile, segments 0, 1 hold the real parts
@@ -343,7 +365,7 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
 
 // kPlanar: B and C arrive, and dB and dC leave, as separate real and imaginary tiles (the in_proj
 // column layout); everything else is shared
-template <bool kPlanar>
+template <bool kPlanar, bool kChains>
 __global__ void __launch_bounds__(kThreads, 1)
     k_bwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDB,
@@ -391,19 +413,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;
     while (cur < p.total) {
       const uint32_t ph = it & 1u;
-      const TicketPos q = ticket_pos(cur, BH, p.H, p.nc);
+      const TicketPos q = ticket_pos<kChains>(cur, BH, p.H, p.G, p.seg);
       const float2 Ah = p.A[q.h];
       mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
       mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
       const int nxt = m.tick[(it + 1) & 1];
-      if (lane == 0 && q.z > 0) {
+      if (lane == 0 && !q.first) {
         float2 dg = make_float2(0.f, 0.f);
 #pragma unroll
         for (int w = 0; w < kWorkers / 32; ++w) {
           dg.x += m.dgp[ph][w].x;
           dg.y += m.dgp[ph][w].y;
         }
-        __stcg(p.dgring + (long long)q.bh * 4 + ((q.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
+        __stcg(p.dgring + (long long)q.sg * 4 + ((q.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
         // the workers' ring stores happened before their bar_ops3 arrivals
         fence_proxy_async_global();
         st_release_gpu(p.flags + (long long)q.bh * p.nc + q.z - 1, 1u);
@@ -414,8 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
       {
         const ChunkRec& rec = m.rec[ph];
-        const float2 dgam = q.z < p.nc - 1 ? make_float2(m.dgam[ph].x, m.dgam[ph].y)
-                            : p.dgam_last != nullptr ? p.dgam_last[q.bh]
+        const float2 dgam = !q.last ? make_float2(m.dgam[ph].x, m.dgam[ph].y)
+                            : p.dgam_last != nullptr ? p.dgam_last[q.sg]
                                                      : make_float2(0.f, 0.f);
         const int t0 = q.z * 64;
         float2 dv[2];
@@ -484,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int cur = (int)atomicAdd(p.counter, 1u);
       m.tick[0] = cur;
       mbar_arrive(&m.bar_ctl);
-      TicketPos qc = ticket_pos(cur, BH, p.H, p.nc);
+      TicketPos qc = ticket_pos<kChains>(cur, BH, p.H, p.G, p.seg);
       if (cur < p.total) {
         ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qc, 0, p.hp);
         ctl_load_b(&tmB, smem, &m, qc, p.hp);
@@ -533,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it > 0) mbar_wait(&m.bar_rel, (it - 1) & 1u, p.err, kErrMmaWait);
         m.tick[(it + 1) & 1] = nxt;
         mbar_arrive(&m.bar_ctl);
-        const TicketPos qn = ticket_pos(nxt, BH, p.H, p.nc);
+        const TicketPos qn = ticket_pos<kChains>(nxt, BH, p.H, p.G, p.seg);
         // Each remaining contraction as soon as its operands are written and its TMEM columns
         // read.
         // After epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
@@ -635,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the register loads follow at the start of that ticket
       auto prefetch_l2 = [&]() {
         if (next < p.total) {
-          const TicketPos qx = ticket_pos(next, BH, p.H, p.nc);
+          const TicketPos qx = ticket_pos<kChains>(next, BH, p.H, p.G, p.seg);
           const int tx = qx.z * 64 + xs0;
           if (tx < p.T) {
             prefetch_l2_line(p.x + qx.b * p.xs[0] + (long long)tx * p.xs[1] + qx.h * p.xs[2] +
@@ -716,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // =================== ticket `next` starts ===================
       active = true;
-      q = ticket_pos(next, BH, p.H, p.nc);
+      q = ticket_pos<kChains>(next, BH, p.H, p.G, p.seg);
       t0 = q.z * 64;
       const uint32_t ph = it & 1u;
       const ChunkRec& rec = m.rec[ph];
@@ -821,7 +843,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // per complex)
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
       float dsz[16];
-      if (q.z < p.nc - 1) {
+      if (!q.last) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float4 v = ld_shared_f4(sb + OFF_DS + (uint32_t)(i * kWorkers + tid) * 16u);
@@ -830,8 +852,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           dsz[4 * i + 2] = v.z;
           dsz[4 * i + 3] = v.w;
         }
-      } else if (p.dhT != nullptr) {  // last chunk: dS = the final state's gradient, transposed
-        const float2* src = p.dhT + (long long)q.bh * 64 * 64 + 16 * sub + (lane >> 2);
+      } else if (p.dhT != nullptr) {  // a chain's last chunk: dS = its end state's gradient, transposed
+        const float2* src = p.dhT + (long long)q.sg * 64 * 64 + 16 * sub + (lane >> 2);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -918,9 +940,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16x256_x4(tmem + lane_off + (16u << 16) + COL_Q + 32u * grp, qb);
         tmem_ld_wait();
         float2 dg = make_float2(0.f, 0.f);
-        if (q.z > 0) {
+        if (!q.first) {
           const float2 g = rec.g;
-          float4* slot = reinterpret_cast<float4*>(p.ring + ((long long)q.bh * 4 + ((q.z - 1) & 3)) * 64 * 128);
+          float4* slot = reinterpret_cast<float4*>(p.ring + ((long long)q.sg * 4 + ((q.z - 1) & 3)) * 64 * 128);
           const uint32_t hb = sb + OFF_H + ((uint32_t)grp >> 1) * 8192u + 4u * q4;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -940,9 +962,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
           }
-        } else if (p.dh0 != nullptr) {  // first chunk: dS_{-1} is the initial state's gradient
+        } else if (p.dh0 != nullptr) {  // a chain's first chunk: dS_{z-1} is its entry state's gradient
           const float2 g = rec.g;
-          float2* dst = p.dh0 + (long long)q.bh * 64 * 64 + 16 * sub + rr;
+          float2* dst = p.dh0 + (long long)q.sg * 64 * 64 + 16 * sub + rr;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float* qv = (i >> 1) ? qb : qa;
@@ -1043,16 +1065,17 @@ struct BwdLayout {
   size_t flags, ring, dgring, dapart, dglast, total;
 };
 
-BwdLayout bwd_layout(const Problem& p) {
-  const size_t bh = (size_t)p.Bsz * p.H, nc = (size_t)((p.T + 63) / 64);
+// the ring, its <dS, H> slots and the end-state d Sigma terms are per chain (G per sequence)
+BwdLayout bwd_layout(const Problem& p, int G) {
+  const size_t bh = (size_t)p.Bsz * p.H, nc = (size_t)((p.T + 63) / 64), chains = bh * G;
   auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
   BwdLayout L;
   L.flags = 256;
   L.ring = al(L.flags + 4 * bh * nc);
-  L.dgring = al(L.ring + bh * 4 * 64 * 128 * sizeof(float));
-  L.dapart = al(L.dgring + bh * 4 * sizeof(float4));
+  L.dgring = al(L.ring + chains * 4 * 64 * 128 * sizeof(float));
+  L.dapart = al(L.dgring + chains * 4 * sizeof(float4));
   L.dglast = al(L.dapart + bh * nc * sizeof(float2));
-  L.total = al(L.dglast + bh * sizeof(float2));
+  L.total = al(L.dglast + chains * sizeof(float2));
   return L;
 }
 
@@ -1060,7 +1083,7 @@ BwdLayout bwd_layout(const Problem& p) {
 
 bool bwd_supported(const Problem& p) { return fwd_supported(p); }
 
-size_t bwd_workspace_bytes(const Problem& p) { return bwd_layout(p).total; }
+size_t bwd_workspace_bytes(const Problem& p, int G) { return bwd_layout(p, G).total; }
 
 BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, float2* dC,
                           float* ddt) {
@@ -1077,14 +1100,17 @@ BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, f
 
 int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
             const BwdOut& out, void* ws, cudaStream_t st, const void* hT, const void* dhT,
-            void* dh0) {
-  const BwdLayout L = bwd_layout(p);
+            void* dh0, int G, const void* dgam, bool clear_status) {
+  const BwdLayout L = bwd_layout(p, G);
   BwdParams bp{};
   bp.Bsz = p.Bsz;
   bp.T = p.T;
   bp.H = p.H;
   bp.nc = (p.T + 63) / 64;
   bp.total = p.Bsz * p.H * bp.nc;
+  if (G < 1 || bp.nc % G != 0) return M3SSD_ERR_SHAPE;
+  bp.G = G;
+  bp.seg = bp.nc / G;
   bp.x = static_cast<const float*>(p.x);
   for (int i = 0; i < 4; ++i) bp.xs[i] = p.xs[i];
   bp.x_vec = (p.xs[3] == 1 && p.xs[0] % 4 == 0 && p.xs[1] % 4 == 0 && p.xs[2] % 4 == 0 &&
@@ -1122,12 +1148,15 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
   bp.ring = reinterpret_cast<float*>(base + L.ring);
   bp.dgring = reinterpret_cast<float4*>(base + L.dgring);
   bp.dapart = reinterpret_cast<float2*>(base + L.dapart);
-  // state carry: with a final-state gradient the final state must come too (the last chunk's
-  // d Sigma term); the initial state's gradient is written whenever asked for
-  if ((dhT != nullptr) != (hT != nullptr)) return M3SSD_ERR_NULL;
+  // state carry: with an end-state gradient the end state must come too (the chain's last chunk's
+  // d Sigma term), unless that term is given ready-made; the entry-state gradient is written
+  // whenever asked for
+  if (dgam == nullptr && (dhT != nullptr) != (hT != nullptr)) return M3SSD_ERR_NULL;
   bp.dhT = static_cast<const float2*>(dhT);
   bp.dh0 = static_cast<float2*>(dh0);
-  bp.dgam_last = dhT != nullptr ? reinterpret_cast<const float2*>(base + L.dglast) : nullptr;
+  bp.dgam_last = dgam != nullptr  ? static_cast<const float2*>(dgam)
+                 : dhT != nullptr ? reinterpret_cast<const float2*>(base + L.dglast)
+                                  : nullptr;
   CUtensorMap tmB, tmC, tmDX, tmDB, tmDC;
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs))
     return M3SSD_ERR_LAUNCH;
@@ -1142,17 +1171,19 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
              !encode_out_tensor_map(&tmDC, out.dC, p, 128)) {
     return M3SSD_ERR_LAUNCH;
   }
-  if (cudaMemsetAsync(ws, 0, L.ring, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  const size_t keep = clear_status ? 0 : 4;  // an earlier pass of the same call reported here
+  if (cudaMemsetAsync(base + keep, 0, L.ring - keep, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  auto kern = out.planar ? k_bwd_tc<true> : k_bwd_tc<false>;
+  auto kern = out.planar ? (G > 1 ? k_bwd_tc<true, true> : k_bwd_tc<true, false>)
+                         : (G > 1 ? k_bwd_tc<false, true> : k_bwd_tc<false, false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
       cudaSuccess)
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
-  if (dhT != nullptr)
-    k_bwd_tc_dgam_last<<<p.Bsz * p.H, 256, 0, st>>>(static_cast<const float2*>(hT),
+  if (dhT != nullptr && dgam == nullptr)
+    k_bwd_tc_dgam_last<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float2*>(hT),
                                                     bp.dhT, reinterpret_cast<float2*>(base + L.dglast));
   kern<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmDX, tmDB, tmDC, bp);
   k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, out.dA);

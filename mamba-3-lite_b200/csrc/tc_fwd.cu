@@ -75,7 +75,32 @@ struct FwdParams {
   // contiguous = s[n][p] of the reference's recurrence, the transpose of a state tile H[p][n]
   const float2* h0;
   float2* hT;
+  // segments: each sequence's chunks run as G chains of seg = nc / G chunks (G = 1: one chain).
+  // A chain starts from h0 (per (sequence, segment), or zero) and its end state goes to hT.
+  int G, seg;
 };
+
+// (chunk, sequence, segment) of a ticket: chunk-within-segment major, so every chain's first
+// chunk comes before any second chunk and a ticket only waits on smaller ones
+struct FwdPos {
+  int z, bh, j, sg;  // chunk, sequence, chunk within its segment, bh * G + segment
+};
+template <bool kChains>
+__device__ __forceinline__ FwdPos fwd_pos(int tk, int BH, int G, int seg) {
+  FwdPos q;
+  if constexpr (!kChains) {  // one chain per sequence
+    q.z = q.j = tk / BH;
+    q.bh = q.sg = tk - q.z * BH;
+    return q;
+  }
+  q.j = tk / (BH * G);
+  const int rest = tk - q.j * BH * G;
+  const int sgm = rest / BH;
+  q.bh = rest - sgm * BH;
+  q.z = sgm * seg + q.j;
+  q.sg = q.bh * G + sgm;
+  return q;
+}
 
 __device__ __forceinline__ void load_x16(const FwdParams& p, int b, int t, int h, int p0,
                                          float (&xv)[16]) {
@@ -124,7 +149,7 @@ __device__ __forceinline__ void split_store16(uint32_t hi_addr, uint32_t lo_addr
 
 // kPlanar: B and C tiles arrive as separate real and imaginary 64 x 64 fp32 tiles (the in_proj
 // column layout) instead of one interleaved 64 x 128 tile; everything after the transform is shared
-template <bool kPlanar>
+template <bool kPlanar, bool kChains>
 __global__ void __launch_bounds__(kThreads, 2)
     k_fwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmY, const FwdParams p) {
@@ -165,14 +190,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   int ticket = m.first;
   float xv[16];
   auto prefetch_regs = [&](int tk) {
-    const int z = tk / BH, bh = tk - (tk / BH) * BH;
+    const FwdPos q = fwd_pos<kChains>(tk, BH, p.G, p.seg);
+    const int z = q.z, bh = q.bh;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
     load_x16(p, b, t0 + (tid >> 2), h, 16 * (tid & 3), xv);
   };
   if (ticket < p.total) prefetch_regs(ticket);
   // B, C tiles and the decay record of a ticket (issued once the previous ticket's MMAs are done)
   auto issue_tma = [&](int tk) {
-    const int z = tk / BH, bh = tk - z * BH;
+    const FwdPos q = fwd_pos<kChains>(tk, BH, p.G, p.seg);
+    const int z = q.z, bh = q.bh;
     const int b = bh / p.H, h = bh - b * p.H;
     mbar_arrive_expect_tx(&m.bar_tma, kTmaBytes + (uint32_t)sizeof(ChunkRec));
     tma_load_4d(smem + OFF_BX, &tmB, &m.bar_tma, 0, h, z * 64, b);
@@ -190,7 +217,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t iter = 0;
   while (ticket < p.total) {
     const uint32_t ph = iter & 1u;
-    const int z = ticket / BH, bh = ticket - z * BH;
+    const FwdPos q = fwd_pos<kChains>(ticket, BH, p.G, p.seg);
+    const int z = q.z, bh = q.bh, j = q.j;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
     __syncthreads();  // previous ticket done: its MMAs completed, its y tile staged
     int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
@@ -285,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // is H_z already published? (then its loads overlap the first MMAs.) Probed as late as
       // the probe's round trip still hides behind the rest of the transform: its value is
       // stored to shared memory at the end of the transform
-      if (ctrl) h_probe = (z == 0) ? 1u : ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
+      if (ctrl) h_probe = (j == 0) ? 1u : ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -302,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     write_tile(0, rc);
     if (ctrl) {  // a published H_z is read by every thread after the barrier below
-      if (z > 0 && h_probe != 0u) fence_acquire_gpu();
+      if (j > 0 && h_probe != 0u) fence_acquire_gpu();
       m.h_ready = (int)h_probe;
     }
     fence_proxy_async_smem();
@@ -311,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // not yet published at the probe: every thread looks again now (no barrier needed later: each
     // thread orders its own H loads after its own observation of the flag)
     uint32_t h_late = 1u;
-    if (z > 0 && !h_early) h_late = ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
+    if (j > 0 && !h_early) h_late = ld_relaxed_gpu(p.flags + (long long)bh * p.nc + z);
 
     // ---- MMA batch 1b: G = C'x B'x^T (M128 N64); the commit covers S~ too
     if (tid == 0) {
@@ -327,9 +355,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mma_commit(&m.bar_mma1);
     }
     float hz[32];
-    if (z == 0) {  // H_0: zero, or the initial state (row p = r, complex n = 32 wg + 16 part + c/2)
+    if (j == 0) {  // a chain's entry state: zero, or h0 (row p = r, complex n = 32 wg + 16 part + c/2)
       if (p.h0 != nullptr) {
-        const float2* src = p.h0 + ((long long)bh * 64 + 32 * wg + 16 * part) * 64 + r;
+        const float2* src = p.h0 + ((long long)q.sg * 64 + 32 * wg + 16 * part) * 64 + r;
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const float2 v = __ldcg(src + c * 64);
@@ -382,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (ctrl) nn = (int)atomicAdd(p.counter, 1u);  // next ticket; stored at the state update
 
     // ---- H_z from the predecessor chunk (bounded wait on its release flag if not yet seen)
-    if (z > 0 && !h_early) {
+    if (j > 0 && !h_early) {
       if (h_late == 0u) flag_wait_relaxed(p.flags + (long long)bh * p.nc + z, p.err);
       fence_acquire_gpu();
       const float4* src =
@@ -458,21 +486,21 @@ __global__ void __launch_bounds__(kThreads, 2)
           hn[c] = hv.x + sv.x;
           hn[c + 1] = hv.y + sv.y;
         }
-        if (z == 0) {  // the chunk-0 state tile the backward reads: H_0
+        if (j == 0) {  // a chain's first chunk stores its own entry state tile (the backward reads it)
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            __stcg(tile0 + (4 * hh + i) * kThreads,
+            __stcg(tile0 + (long long)z * 64 * 32 + (4 * hh + i) * kThreads,
                    make_float4(hz[16 * hh + 4 * i], hz[16 * hh + 4 * i + 1],
                                hz[16 * hh + 4 * i + 2], hz[16 * hh + 4 * i + 3]));
         }
-        if (z + 1 < p.nc) {
+        if (j + 1 < (kChains ? p.seg : p.nc)) {
           float4* dst = tile0 + (long long)(z + 1) * 64 * 32;
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             __stcg(dst + (4 * hh + i) * kThreads,
                    make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
-        } else if (p.hT != nullptr) {  // the final state H_nc, transposed to (n, p)
-          float2* dst = p.hT + ((long long)bh * 64 + 32 * wg + 16 * part + 8 * hh) * 64 + r;
+        } else if (p.hT != nullptr) {  // the chain's end state, transposed to (n, p)
+          float2* dst = p.hT + ((long long)q.sg * 64 + 32 * wg + 16 * part + 8 * hh) * 64 + r;
 #pragma unroll
           for (int c = 0; c < 8; ++c) __stcg(dst + c * 64, make_float2(hn[2 * c], hn[2 * c + 1]));
         }
@@ -484,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // the barrier orders every thread's H stores before this gpu-scope release. Its fence costs
     // the control thread's warp ~1 us wherever it is placed (measured: here, after the output
     // epilogue, or with no loads of the warp in flight); here it also publishes H_{z+1} soonest.
-    if (ctrl && z + 1 < p.nc) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+    if (ctrl && j + 1 < (kChains ? p.seg : p.nc)) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
 
     // ---- output y = Y1 + exp(rho_l) Y2 into the staging tile in sXT; the next ticket's B, C
     // tiles and record load as soon as the last MMA has read sCX / sBX
@@ -659,7 +687,7 @@ size_t fwd_workspace_bytes(const Problem& p) {
 }
 
 int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, const void* h0,
-            void* hT) {
+            void* hT, int G, bool prep, bool clear_status) {
   FwdParams fp{};
   fp.Bsz = p.Bsz;
   fp.T = p.T;
@@ -682,17 +710,28 @@ int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, 
   fp.y_bf16 = p.y_bf16;
   fp.h0 = static_cast<const float2*>(h0);
   fp.hT = static_cast<float2*>(hT);
+  if (G < 1 || fp.nc % G != 0) return M3SSD_ERR_SHAPE;
+  fp.G = G;
+  fp.seg = fp.nc / G;
   CUtensorMap tmB, tmC, tmY;
   if (!encode_bc_tensor_map(&tmB, p.Bm, p, p.bs) || !encode_bc_tensor_map(&tmC, p.Cm, p, p.cs) ||
       !(p.y_bf16 ? encode_out_map_bf16(&tmY, y, p) : encode_out_tensor_map(&tmY, y, p, 64)))
     return M3SSD_ERR_LAUNCH;
-  if (cudaMemsetAsync(ws, 0, fwd_workspace_bytes(p), st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
-  const int rc = run_chunk_prep(p, recs, st);
-  if (rc != M3SSD_OK) return rc;
+  // status word (unless an earlier pass of the same call already reported into it), ticket
+  // counter and hand-off flags start at zero
+  const size_t keep = clear_status ? 0 : 4;
+  if (cudaMemsetAsync(static_cast<char*>(ws) + keep, 0, fwd_workspace_bytes(p) - keep, st) !=
+      cudaSuccess)
+    return M3SSD_ERR_LAUNCH;
+  if (prep) {
+    const int rc = run_chunk_prep(p, recs, st);
+    if (rc != M3SSD_OK) return rc;
+  }
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  auto kern = p.bc_planar ? k_fwd_tc<true> : k_fwd_tc<false>;
+  auto kern = p.bc_planar ? (G > 1 ? k_fwd_tc<true, true> : k_fwd_tc<true, false>)
+                          : (G > 1 ? k_fwd_tc<false, true> : k_fwd_tc<false, false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
       cudaSuccess)
     return M3SSD_ERR_LAUNCH;

@@ -1,0 +1,223 @@
+// Long sequences, few of them: the tensor-core path run as G chains per sequence.
+//
+// The one-pass kernels hand the state from chunk to chunk of a sequence (forward: H_z -> H_{z+1};
+// backward: dS_z -> dS_{z-1}); each hand-off costs a few microseconds of latency, so a sequence of
+// nc chunks takes at least nc hand-offs whatever the work. At B4 L16384 with two heads per GPU
+// (8 sequences of 256 chunks) that chain, not HBM, sets the time. Here each sequence's chunks run
+// as G chains of nc / G chunks in the same kernels, in two passes:
+//
+//   forward   pass 1: every chain from a zero entry state; its end state L_s goes to scratch
+//             chain:  S_0 = h0 (or 0), S_{s+1} = D_s S_s + L_s over the segments (D_s = the
+//                     segment's total decay, the product of its chunks' e^Gamma), S_G = final state
+//             pass 2: every chain from its true entry state S_s: y and the chunk-entry states
+//   backward  pass 1: every chain from a zero end-state gradient; its entry-state gradient P_s
+//             chain:  dS_G = dhT (or 0), dS_s = P_{s+1} + conj(D_{s+1}) dS_{s+1} going back, and
+//                     each segment's last-chunk d Sigma term <dS_s, conj(S_{s+1})>
+//             pass 2: every chain from its true end-state gradient: all gradients
+//
+// Every chain's algebra is the reference's recurrence split at segment boundaries
+// (s_t = e^{a_t} s_{t-1} + B_t x_t^T is linear in s), so the result equals the one-pass path's
+// up to rounding. Pass 1 writes y (forward) or the gradients (backward) that pass 2 overwrites.
+#include <cuda_runtime.h>
+
+#include "tc_path.h"
+
+namespace m3ssd {
+namespace tc {
+
+namespace {
+
+constexpr int kMaxChains = 64;     // chains per sequence
+constexpr int kStateElems = 64 * 64;  // complex elements of one state
+
+size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// scratch after the one-pass workspace: two per-chain state arrays (B*H*G states each)
+size_t chain_states_bytes(const Problem& p, int G) {
+  return (size_t)p.Bsz * p.H * G * kStateElems * sizeof(float2);
+}
+
+// D_s for s = 0..G-1 of sequence bh into shared memory (threads s < G)
+__device__ __forceinline__ void segment_decays(const ChunkRec* recs, int bh, int nc, int G,
+                                               float2* D) {
+  const int seg = nc / G;
+  for (int s = threadIdx.x; s < G; s += blockDim.x) {
+    float2 d = make_float2(1.f, 0.f);
+    const ChunkRec* r = recs + (long long)bh * nc + (long long)s * seg;
+    for (int j = 0; j < seg; ++j) {
+      const float2 g = r[j].g;
+      d = make_float2(d.x * g.x - d.y * g.y, d.x * g.y + d.y * g.x);
+    }
+    D[s] = d;
+  }
+  __syncthreads();
+}
+
+// forward chain over the segments of one sequence, one complex element per thread
+__global__ void __launch_bounds__(256) k_chain_fwd(const ChunkRec* __restrict__ recs, int nc, int G,
+                                                   const float2* __restrict__ h0,
+                                                   const float2* __restrict__ L,
+                                                   float2* __restrict__ S, float2* __restrict__ hT) {
+  __shared__ float2 D[kMaxChains];
+  const int bh = blockIdx.x;
+  segment_decays(recs, bh, nc, G, D);
+  const int e = blockIdx.y * 256 + threadIdx.x;
+  float2 s = h0 != nullptr ? h0[(long long)bh * kStateElems + e] : make_float2(0.f, 0.f);
+  for (int k = 0; k < G; ++k) {
+    const long long i = ((long long)bh * G + k) * kStateElems + e;
+    S[i] = s;
+    const float2 l = L[i], d = D[k];
+    s = make_float2(d.x * s.x - d.y * s.y + l.x, d.x * s.y + d.y * s.x + l.y);
+  }
+  if (hT != nullptr) hT[(long long)bh * kStateElems + e] = s;
+}
+
+// backward chain: end-state gradients of every segment from the entry-state gradients of pass 1
+__global__ void __launch_bounds__(256) k_chain_bwd(const ChunkRec* __restrict__ recs, int nc, int G,
+                                                   const float2* __restrict__ dhT,
+                                                   const float2* __restrict__ P,
+                                                   float2* __restrict__ dE, float2* __restrict__ dh0) {
+  __shared__ float2 D[kMaxChains];
+  const int bh = blockIdx.x;
+  segment_decays(recs, bh, nc, G, D);
+  const int e = blockIdx.y * 256 + threadIdx.x;
+  float2 g = dhT != nullptr ? dhT[(long long)bh * kStateElems + e] : make_float2(0.f, 0.f);
+  for (int k = G - 1; k >= 0; --k) {
+    const long long i = ((long long)bh * G + k) * kStateElems + e;
+    dE[i] = g;
+    const float2 q = P[i], d = D[k];  // dS at the entry of segment k = P_k + conj(D_k) dS_end
+    g = make_float2(q.x + d.x * g.x + d.y * g.y, q.y + d.x * g.y - d.y * g.x);
+  }
+  if (dh0 != nullptr) dh0[(long long)bh * kStateElems + e] = g;
+}
+
+// <dE_s, conj(S_{s+1})> per chain: the d Sigma term of a segment's last position from its end
+// state. S_{s+1} is the chunk-entry state tile of chunk (s + 1) * seg in `states` (the forward's
+// thread-major layout: float4 f holds, of row p = 16 (w mod 4) + (l mod 16), the complex columns
+// n0, n0 + 1 with n0 = 32 (w / 4) + 16 (l / 16) + 8 (f / 1024) + 2 ((f / 256) mod 4), where
+// t = f mod 256, w = t / 32, l = t mod 32); the last segment's end state is the final state hT
+// ((n, p) layout), or absent when no end-state gradient comes in (then its dE is zero).
+__global__ void __launch_bounds__(256) k_chain_dgam(const float* __restrict__ states, int nc, int G,
+                                                    const float2* __restrict__ dE,
+                                                    const float2* __restrict__ hT,
+                                                    float2* __restrict__ dgam) {
+  __shared__ float2 red[8];
+  const int sg = blockIdx.x, bh = sg / G, s = sg - bh * G, seg = nc / G;
+  const float2* de = dE + (long long)sg * kStateElems;
+  float2 acc = make_float2(0.f, 0.f);
+  if (s + 1 < G) {
+    const float4* tile =
+        reinterpret_cast<const float4*>(states + ((long long)bh * nc + (long long)(s + 1) * seg) * 64 * 128);
+    for (int f = threadIdx.x; f < 2048; f += 256) {
+      const int t = f & 255, w = t >> 5, l = t & 31;
+      const int prow = 16 * (w & 3) + (l & 15);
+      const int n0 = 32 * (w >> 2) + 16 * (l >> 4) + 8 * (f >> 10) + 2 * ((f >> 8) & 3);
+      const float4 h = tile[f];
+      const float2 a = de[n0 * 64 + prow], b = de[(n0 + 1) * 64 + prow];
+      acc.x += a.x * h.x + a.y * h.y + b.x * h.z + b.y * h.w;
+      acc.y += a.y * h.x - a.x * h.y + b.y * h.z - b.x * h.w;
+    }
+  } else if (hT != nullptr) {
+    const float2* hh = hT + (long long)bh * kStateElems;
+    for (int e = threadIdx.x; e < kStateElems; e += 256) {
+      const float2 a = de[e], h = hh[e];
+      acc.x += a.x * h.x + a.y * h.y;
+      acc.y += a.y * h.x - a.x * h.y;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float2 t = red[0];
+    for (int w = 1; w < 8; ++w) {
+      t.x += red[w].x;
+      t.y += red[w].y;
+    }
+    dgam[sg] = t;
+  }
+}
+
+}  // namespace
+
+// Time model of one pass (microseconds, fitted to one-pass runs on B200): a ticket (one chunk of
+// one sequence) costs `ticket` of throughput with the GPU full, a hand-off `hop` of latency on its
+// chain, and a pass takes about the larger of the two plus a fifth of the smaller (B16 L2048 H16:
+// work-bound; B4 L16384 with 2 or 16 heads: chain-bound). The chained form runs two passes over
+// chains of nc / G chunks plus the segment chain. G = 1 unless chains are clearly faster.
+int chains_for(const Problem& p, bool backward) {
+  const int nc = (p.T + 63) / 64;
+  const double bh = (double)p.Bsz * p.H;
+  const double ticket = backward ? 0.070 : 0.039, hop = backward ? 5.2 : 4.3;
+  const double work = bh * nc * ticket;
+  auto pass = [&](double chain) {
+    return work > chain ? work + 0.2 * chain : chain + 0.2 * work;
+  };
+  const double one_pass = pass(nc * hop);
+  double best = one_pass;
+  int best_g = 1;
+  for (int G = 2; G <= kMaxChains && nc / G >= 2; G *= 2) {
+    if (nc % G != 0) break;  // a larger power of two does not divide nc either
+    const double est = 2.0 * pass((double)(nc / G) * hop) + 10.0 + 0.5 * G;
+    if (est < best) {
+      best = est;
+      best_g = G;
+    }
+  }
+  return best < 0.8 * one_pass ? best_g : 1;
+}
+
+size_t fwd_chains_workspace_bytes(const Problem& p, int G) {
+  return al256(fwd_workspace_bytes(p)) + 2 * chain_states_bytes(p, G);
+}
+
+size_t bwd_chains_workspace_bytes(const Problem& p, int G) {
+  return al256(bwd_workspace_bytes(p, G)) + 2 * chain_states_bytes(p, G) +
+         al256((size_t)p.Bsz * p.H * G * sizeof(float2));
+}
+
+int run_fwd_chains(const Problem& p, void* y, void* states, void* ws, cudaStream_t st,
+                   const void* h0, void* hT, int G) {
+  const int nc = (p.T + 63) / 64;
+  if (G < 2 || G > kMaxChains || nc % G != 0) return M3SSD_ERR_SHAPE;
+  char* base = static_cast<char*>(ws);
+  float2* L = reinterpret_cast<float2*>(base + al256(fwd_workspace_bytes(p)));
+  float2* S = L + (size_t)p.Bsz * p.H * G * kStateElems;
+  int rc = run_fwd(p, y, states, ws, st, nullptr, L, G, true, true);
+  if (rc != M3SSD_OK) return rc;
+  const ChunkRec* recs =
+      reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
+  k_chain_fwd<<<dim3(p.Bsz * p.H, kStateElems / 256), 256, 0, st>>>(
+      recs, nc, G, static_cast<const float2*>(h0), L, S, static_cast<float2*>(hT));
+  if (cudaGetLastError() != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  return run_fwd(p, y, states, ws, st, S, nullptr, G, false, false);
+}
+
+int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], const void* states,
+                   const BwdOut& out, void* ws, cudaStream_t st, const void* hT, const void* dhT,
+                   void* dh0, int G) {
+  const int nc = (p.T + 63) / 64;
+  if (G < 2 || G > kMaxChains || nc % G != 0) return M3SSD_ERR_SHAPE;
+  if ((dhT != nullptr) != (hT != nullptr)) return M3SSD_ERR_NULL;
+  char* base = static_cast<char*>(ws);
+  float2* P = reinterpret_cast<float2*>(base + al256(bwd_workspace_bytes(p, G)));
+  float2* dE = P + (size_t)p.Bsz * p.H * G * kStateElems;
+  float2* dgam = dE + (size_t)p.Bsz * p.H * G * kStateElems;
+  int rc = run_bwd(p, dy, dys, states, out, ws, st, nullptr, nullptr, P, G, nullptr, true);
+  if (rc != M3SSD_OK) return rc;
+  const ChunkRec* recs =
+      reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
+  k_chain_bwd<<<dim3(p.Bsz * p.H, kStateElems / 256), 256, 0, st>>>(
+      recs, nc, G, static_cast<const float2*>(dhT), P, dE, static_cast<float2*>(dh0));
+  k_chain_dgam<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float*>(states), nc, G, dE,
+                                                static_cast<const float2*>(hT), dgam);
+  if (cudaGetLastError() != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  return run_bwd(p, dy, dys, states, out, ws, st, nullptr, dE, nullptr, G, dgam, false);
+}
+
+}  // namespace tc
+}  // namespace m3ssd

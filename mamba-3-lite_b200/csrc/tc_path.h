@@ -50,15 +50,20 @@ bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int r
 // head_dim = state_dim = 64, real x, B/C with contiguous state dim and 16-byte aligned strides
 bool fwd_supported(const Problem& p);
 size_t fwd_workspace_bytes(const Problem& p);
-// h0 / hT (optional): initial and final state, (B, H, N, D) complex64 contiguous
+// h0 / hT (optional): initial and final state, (B, H, N, D) complex64 contiguous. With G > 1
+// (a divisor of the chunk count) every sequence runs as G independent chains of nc / G chunks,
+// h0 / hT then hold one state per (sequence, segment) ((b * H + h) * G + segment). `prep` = false
+// reuses the chunk records a previous call left in `states`; `clear_status` = false keeps what an
+// earlier pass of the same call reported in the status word.
 int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st,
-            const void* h0 = nullptr, void* hT = nullptr);
+            const void* h0 = nullptr, void* hT = nullptr, int G = 1, bool prep = true,
+            bool clear_status = true);
 
 bool bwd_supported(const Problem& p);
 
 // tc_selftest.cu: the bounded waits give up and report (status word in the first 256 bytes of ws)
 int run_selftest_waits(void* ws, cudaStream_t st);
-size_t bwd_workspace_bytes(const Problem& p);
+size_t bwd_workspace_bytes(const Problem& p, int G = 1);
 
 // Where the backward writes its gradients. Contiguous (B, T, H, ...) tensors by default; the
 // in_proj form (planar = 1) writes dx, dB, dC, ddt into one (B, T, H(D + 4N + 1)) fp32 gradient of
@@ -76,10 +81,31 @@ BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, f
                           float* ddt);
 // dy: float32, or bfloat16 with p.y_bf16; strides in elements. State carry (optional, all
 // (B, H, N, D) complex64 contiguous): hT the forward's final state and dhT its gradient (both or
-// neither), dh0 receives the gradient of the initial state.
+// neither), dh0 receives the gradient of the initial state. With G > 1 (a divisor of the chunk
+// count) every sequence runs as G independent chains (run_fwd): dhT / dh0 (and hT) then hold one
+// state per chain, and `dgam` (one complex per chain: <dhT, conj(end state)>, the chain's last
+// chunk's d Sigma term) may be passed ready-made instead of hT.
 int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
             const BwdOut& out, void* ws, cudaStream_t st, const void* hT = nullptr,
-            const void* dhT = nullptr, void* dh0 = nullptr);
+            const void* dhT = nullptr, void* dh0 = nullptr, int G = 1,
+            const void* dgam = nullptr, bool clear_status = true);
+
+// Long sequences with few of them: the hand-off chain from chunk to chunk (a few microseconds per
+// chunk) bounds the time, not the work. tc_long.cu then runs every sequence as G chains in two
+// passes with a short chain over segments in between (forward: local end states, then the true
+// entry states; backward: local entry-state gradients, then the true end-state gradients).
+// chains_for picks G from the problem's shape alone (1 = the one-pass path), so a forward and a
+// backward may pick differently: `states` is the same either way.
+int chains_for(const Problem& p, bool backward);
+size_t fwd_chains_workspace_bytes(const Problem& p, int G);
+size_t bwd_chains_workspace_bytes(const Problem& p, int G);
+// the forward / backward with G chains per sequence; h0, hT, dhT, dh0 as for run_fwd / run_bwd
+// with G = 1 (one state per sequence, optional)
+int run_fwd_chains(const Problem& p, void* y, void* states, void* ws, cudaStream_t st,
+                   const void* h0, void* hT, int G);
+int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], const void* states,
+                   const BwdOut& out, void* ws, cudaStream_t st, const void* hT, const void* dhT,
+                   void* dh0, int G);
 
 }  // namespace tc
 }  // namespace m3ssd

@@ -46,14 +46,26 @@ def _state_loss(hT, dhT):
     return (torch.view_as_real(hT) * torch.view_as_real(dhT)).sum()
 
 
-@pytest.mark.parametrize("T", [64, 256])
-def test_state_carry_vs_fp64_recurrence(m3, cuda_device, T):
+def _chained(B, T, H):
+    """Whether the library runs this shape as several chains per sequence (two passes)."""
+    import ctypes
+    from m3ssd import _lib
+    p = _lib.Problem(B, T, H, 64, 64, 64, 0, 0)
+    lib = _lib.load()
+    return (lib.m3ssd_launch_count(ctypes.byref(p), 0) > 2,
+            lib.m3ssd_launch_count(ctypes.byref(p), 1) > 2)
+
+
+# (2, 64, 3): first and last chunk in one ticket; (1, 1024, 2): few long sequences, run as chains
+@pytest.mark.parametrize("B,T,H", [(2, 64, 3), (2, 256, 3), (1, 1024, 2)])
+def test_state_carry_vs_fp64_recurrence(m3, cuda_device, B, T, H):
     tol = TOL["tensor"]
-    inp, dy, h0, dhT = _case(2, T, 3, seed=T)
+    assert _chained(B, T, H) == ((True, True) if T == 1024 else (False, False))
+    inp, dy, h0, dhT = _case(B, T, H, seed=T)
     xs = [_dev(inp[k], cuda_device, True) for k in KEYS]
     h0_t = _dev(h0, cuda_device, True)
     y, hT = m3.ssd_complex_chunkwise_state(*xs, initial_state=h0_t)
-    assert hT.shape == (2, 3, 64, 64) and hT.dtype == torch.complex64
+    assert hT.shape == (B, H, 64, 64) and hT.dtype == torch.complex64
     loss = (y * _dev(dy, cuda_device)).sum() + _state_loss(hT, _dev(dhT, cuda_device))
     loss.backward()
 
@@ -105,10 +117,12 @@ def test_segments_chain_like_one_call(m3, cuda_device):
         assert rel < 1e-5, (k, rel)
 
 
-def test_zero_state_is_the_plain_operator(m3, cuda_device):
+@pytest.mark.parametrize("B,T,H", [(2, 256, 2), (1, 2048, 2)])
+def test_zero_state_is_the_plain_operator(m3, cuda_device, B, T, H):
     """No initial state and no final-state gradient: the same kernels and results as
-    ssd_complex_chunkwise, bit for bit; an explicit zero initial state gives the same y."""
-    inp, dy, _, _ = _case(2, 256, 2, seed=3)
+    ssd_complex_chunkwise, bit for bit (one pass, and as chains); an explicit zero initial state
+    gives the same y."""
+    inp, dy, _, _ = _case(B, T, H, seed=3)
     dy_t = _dev(dy, cuda_device)
     a = [_dev(inp[k], cuda_device, True) for k in KEYS]
     b = [_dev(inp[k], cuda_device, True) for k in KEYS]
