@@ -121,8 +121,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sms)}
 
 
-def make_inputs(dev, seed, B, T, H, D, N, pin=False):
-    """Block-shape distributions, generated on the device (or on the host when pin=True)."""
+def make_inputs(dev, seed, B, T, H, D, N, pin=False, slow_decay=False):
+    """Block-shape distributions, generated on the device (or on the host when pin=True);
+    slow_decay draws Re A from -exp(U(log 0.01, log 1)) (the long-sequence stress case)."""
     import torch
     gdev = "cpu" if pin else dev
     g = torch.Generator(device=gdev).manual_seed(seed)
@@ -133,8 +134,9 @@ def make_inputs(dev, seed, B, T, H, D, N, pin=False):
         return torch.complex(re, im)
 
     x = torch.randn(B, T, H, D, generator=g, device=gdev)
-    a_re = -torch.exp(torch.empty(H, device=gdev).uniform_(0.0, float(torch.log(torch.tensor(16.0))),
-                                                           generator=g))
+    lo, hi = ((float(torch.log(torch.tensor(0.01))), 0.0) if slow_decay
+              else (0.0, float(torch.log(torch.tensor(16.0)))))
+    a_re = -torch.exp(torch.empty(H, device=gdev).uniform_(lo, hi, generator=g))
     a_im = torch.empty(H, device=gdev).uniform_(-3.141592653589793, 3.141592653589793, generator=g)
     A = torch.complex(a_re, a_im)
     s = (1.0 / (2 * N)) ** 0.5
@@ -194,6 +196,110 @@ def run_reference_arm(args):
                          "sample": f"B={sample_batch} T=2048 H=16 fwd+bwd per step "
                                    "(torch CPU restatement of models/ssd_complex.py:58-119)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+LONG = dict(B=4, T=16384, H=16)  # the long-sequence stress shape, heads sharded over the GPUs
+
+
+def run_long_workload(args):
+    """Few long sequences: B4 L16384 H16 with slow decays, its 16 heads sharded over the job's
+    GPUs (one process per GPU, no collective in the op; strong scaling). `--long-shard K` runs one
+    GPU's share of a K-GPU job (16 / K heads) on each rank instead. `value` is the job's tokens
+    (all heads of a token) per second; `per_gpu` the SURVEY-style B * L * H_local / H / time."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+    import m3ssd
+    from m3ssd import _lib
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from m3ssd import dist as mdist
+    if world > 1:
+        mdist.init_process_group("nccl", timeout_s=120.0, device=dev)
+    lib = m3ssd.load()
+    shard = args.long_shard or world
+    if LONG["H"] % shard:
+        raise SystemExit(f"--long-shard {shard} does not divide {LONG['H']} heads")
+    B, T, H, D, N = LONG["B"], LONG["T"], LONG["H"] // shard, SHAPE["D"], SHAPE["N"]
+    d = make_inputs(dev, 3000 + rank, B, T, H, D, N, slow_decay=True)
+    prob = _lib.Problem(B, T, H, D, N, CHUNK, 0, 0)
+    launches = (lib.m3ssd_launch_count(ctypes.byref(prob), 0),
+                lib.m3ssd_launch_count(ctypes.byref(prob), 1))
+    stream = torch.cuda.current_stream(dev)
+    fwd_ev, bwd_ev = [], []
+
+    def step(timed=False):
+        xs = [d[k].detach().requires_grad_(True) for k in ("x", "A", "B_t", "C_t", "dt")]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if timed else None
+        if timed:
+            ev[0].record(stream)
+        y = m3ssd.ssd_complex_chunkwise(*xs, chunk_size=CHUNK, precision=args.precision)
+        if timed:
+            ev[1].record(stream)
+        y.backward(d["dy"])
+        if timed:
+            ev[2].record(stream)
+            fwd_ev.append((ev[0], ev[1]))
+            bwd_ev.append((ev[1], ev[2]))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(timed=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    os.environ["M3SSD_CHECK"] = "1"
+    step()
+    torch.cuda.synchronize()
+    os.environ["M3SSD_CHECK"] = "0"
+    ms = t0.elapsed_time(t1) / args.steps
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_ev)
+    ms, fwd_ms, bwd_ms = mdist.max_over_ranks([ms, fwd_ms, bwd_ms], device=dev)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    per_gpu = B * T * H / LONG["H"] / (ms / 1e3) / 1e6
+    peak, peak_kind = measured_peaks()
+    step_bytes = (FWD_BYTES_PER_TOKHEAD + BWD_BYTES_PER_TOKHEAD) * B * T * H
+    line = {
+        "metric": "SSD fwd+bwd Mtokens/s @B4 L16384 H16 D64 N64, heads sharded over the GPUs",
+        "value": per_gpu * world, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong" if shard == world else "weak",
+        "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded; Re A from -exp(U(log 0.01, log 1)))",
+        "per_gpu": per_gpu,
+        "config": {"workload": f"B4 L16384 H16, {H} heads per GPU ({shard}-GPU share): "
+                               f"{B * H} sequences of {T // 64} chunks per GPU",
+                   "chunk": CHUNK, "precision": args.precision,
+                   "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                   "launches_fwd_bwd": list(launches), "chained": launches != (2, 2),
+                   "l2": "inputs > 126 MB L2 per GPU (no flush needed)"},
+        "roofline": {"bound": "hbm", "kernel": "fwd+bwd step", "peak_kind": peak_kind,
+                     "achieved": step_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": step_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None},
+        "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -325,9 +431,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
     ap.add_argument("--batch", type=int, default=SHAPE["B"],
                     help="batch per rank (a smaller batch is only for profiling captures)")
-    ap.add_argument("--workload", choices=["op", "proj"], default="op",
+    ap.add_argument("--long-shard", type=int, default=0,
+                    help="with --workload long: run one GPU's share of a job on this many GPUs "
+                         "(default: the job's own GPU count)")
+    ap.add_argument("--workload", choices=["op", "proj", "long"], default="op",
                     help="op: the operator on unpacked inputs (default); proj: the block's SSD "
-                         "input path from its in_proj output, fused vs composed")
+                         "input path from its in_proj output, fused vs composed; long: one "
+                         "GPU's share of B4 L16384 H16 (few long sequences)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -335,6 +445,8 @@ def main():
         return run_reference_arm(args)
     if args.workload == "proj":
         return run_proj_workload(args)
+    if args.workload == "long":
+        return run_long_workload(args)
 
     import torch
     import torch.distributed as dist
