@@ -305,6 +305,116 @@ def run_long_workload(args):
     return 0
 
 
+def run_model_workload(args):
+    """The whole-model data-parallel training step (the reference's 28-layer model, d_model 1024,
+    vocab 50257, micro-batch 16 x 2048 per GPU, tokens uniform) with this operator in every block:
+    m3ssd.lm under DistributedDataParallel (NCCL all-reduce of bf16-autocast gradients in 64 MB
+    buckets, overlapped with the backward), AdamW. `value`: tokens per second of the whole job
+    with the batch resident on the device; `e2e`: the same step fed from pinned host memory and
+    reading the loss back every step, as the reference's trainer does (training/pretrain.py:
+    136-171 calls loss.item() per micro-step)."""
+    import torch
+    import torch.distributed as dist
+    import m3ssd
+    from m3ssd import lm
+    from m3ssd import dist as mdist
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        mdist.init_process_group("nccl", timeout_s=300.0, device=dev)
+    m3ssd.load()
+    cfg = lm.ModelConfig(n_layers=args.model_layers)
+    torch.manual_seed(1234)  # same initial weights on every rank (DDP also broadcasts them)
+    model = lm.Mamba3Transformer(cfg).to(dev)
+    n_params = sum(p.numel() for p in model.parameters())
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(
+            model, device_ids=[local], bucket_cap_mb=64, gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1)
+    B, T = args.batch, cfg.max_seq_len
+    g = torch.Generator(device="cpu").manual_seed(5000 + rank)
+    tok_h = torch.randint(0, cfg.vocab_size, (B, T + 1), generator=g).pin_memory()
+    tokens = tok_h[:, :-1].to(dev)
+    targets = tok_h[:, 1:].to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(k, from_host):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        loss = None
+        for _ in range(k):
+            if from_host:
+                x = tok_h[:, :-1].to(dev, non_blocking=True)
+                y = tok_h[:, 1:].to(dev, non_blocking=True)
+                loss = lm.train_step(net, opt, x, y).item()
+            else:
+                loss = lm.train_step(net, opt, tokens, targets)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return e0.elapsed_time(e1) / k, float(loss)
+
+    for _ in range(args.warmup):
+        lm.train_step(net, opt, tokens, targets)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ms, loss = timed(args.steps, False)
+    clocks = sampler.stop()
+    e2e_ms, _ = timed(max(1, args.e2e_steps), True)
+    ms, e2e_ms = mdist.max_over_ranks([ms, e2e_ms], device=dev)
+    mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    tokens_job = world * B * T
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tf_peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    # GEMM flops: 6 per parameter per token (forward + backward); the tied embedding counts once,
+    # as the head (its lookup has no flops). The SSD's own flops (~2% of these) are left out.
+    flops = 6.0 * n_params * B * T
+    line = {
+        "metric": "whole-model DP train step tokens/s @28L d1024 vocab 50257, 16 x 2048 per GPU",
+        "value": tokens_job / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 autocast (SSD in fp32 / split-bf16 tensor cores)",
+        "data": "synthetic (tokens uniform in [0, 50257), seeded per rank)",
+        "config": {"workload": f"Mamba-3-Lite {cfg.n_layers} layers, {n_params / 1e6:.0f}M "
+                               f"parameters, micro-batch {B} x {T} per GPU, AdamW, grad clip 1.0",
+                   "parallelism": f"dp{world}" + (" (DDP, NCCL, 64 MB buckets)" if world > 1
+                                                  else ""),
+                   "loss_last": loss, "max_memory_gb": mem_gb,
+                   "l2": "activations >> 126 MB L2 (no flush needed)"},
+        "e2e": {"value": tokens_job / (e2e_ms / 1e3), "unit": "tokens/s",
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": 2 * B * T * 8,
+                "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "tensor", "kernel": "whole step (GEMM flops 6 x params x tokens)",
+                     "achieved": flops / (ms / 1e3) / 1e12, "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": flops / (ms / 1e3) / 1e12 / tf_peak,
+                     "peak_kind": "measured sustained bf16" if peaks else "fallback",
+                     "traffic": None},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_proj_workload(args):
     """The block's SSD input path (in_proj output -> y -> d(proj), dA), fused vs composed."""
     import torch
@@ -434,10 +544,13 @@ def main():
     ap.add_argument("--long-shard", type=int, default=0,
                     help="with --workload long: run one GPU's share of a job on this many GPUs "
                          "(default: the job's own GPU count)")
-    ap.add_argument("--workload", choices=["op", "proj", "long"], default="op",
+    ap.add_argument("--model-layers", type=int, default=28,
+                    help="with --workload model: number of blocks (28 = the reference model)")
+    ap.add_argument("--workload", choices=["op", "proj", "long", "model"], default="op",
                     help="op: the operator on unpacked inputs (default); proj: the block's SSD "
                          "input path from its in_proj output, fused vs composed; long: one "
-                         "GPU's share of B4 L16384 H16 (few long sequences)")
+                         "GPU's share of B4 L16384 H16 (few long sequences); model: the whole "
+                         "28-layer model's data-parallel train step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -447,6 +560,8 @@ def main():
         return run_proj_workload(args)
     if args.workload == "long":
         return run_long_workload(args)
+    if args.workload == "model":
+        return run_model_workload(args)
 
     import torch
     import torch.distributed as dist

@@ -4,6 +4,9 @@ Run from the repository root in a container where the reference checkout is pres
 
     python tests/golden/make_golden.py --reference /root/reference
 
+``lm_tiny.npz``: a two-layer reference ``Mamba3Transformer`` (models/transformer.py) on CPU, its
+parameters, logits, loss and parameter gradients for one batch (see ``make_lm_fixture``).
+
 For every in_proj case (``PROJ_CASES`` in ``oracle/cases.py``) it runs the reference block's own
 unpacking of its in_proj output and the operator call inside it (models/mamba_block.py:73-104), and
 records the unpacked operands, y, and the gradients of proj and A (see ``run_reference_block``).
@@ -96,6 +99,44 @@ def run_reference_block(proj_np, A_np, dy, chunk, dims):
     return out, unpacked
 
 
+LM_TINY = dict(vocab_size=50, d_model=16, n_layers=2, n_heads=2, head_dim=64, state_dim=64,
+               chunk_size=64, ffn_dim=32, max_seq_len=128)
+
+
+def make_lm_fixture():
+    """A tiny reference Mamba3Transformer (models/transformer.py) on CPU in fp32: its parameters
+    (A set to seeded complex decays), one batch of tokens and targets, the logits, the
+    cross-entropy loss and the gradient of every parameter. Pins the model around the operator
+    (m3ssd.lm) to the reference's layers, names and initialisation-independent wiring."""
+    from models.transformer import Mamba3Transformer  # the reference itself
+
+    torch.manual_seed(11)
+    model = Mamba3Transformer(dict(LM_TINY))
+    rng = np.random.Generator(np.random.PCG64(77))
+    H = LM_TINY["n_heads"]
+    with torch.no_grad():
+        for layer in model.layers:
+            # slow decays: the reference's exp-then-mask stays finite over a 64-chunk
+            a = -np.exp(rng.uniform(np.log(0.01), 0.0, H)) + 1j * rng.uniform(-np.pi, np.pi, H)
+            layer.A.copy_(torch.from_numpy(a.astype(np.complex64)))
+    T = 128
+    tokens = torch.from_numpy(rng.integers(0, LM_TINY["vocab_size"], (2, T)).astype(np.int64))
+    targets = torch.from_numpy(rng.integers(0, LM_TINY["vocab_size"], (2, T)).astype(np.int64))
+    logits = model(tokens)
+    loss = torch.nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)),
+                                             targets.reshape(-1))
+    loss.backward()
+    rec = {"tokens": tokens.numpy(), "targets": targets.numpy(),
+           "logits": logits.detach().numpy(), "loss": np.float64(loss.item())}
+    for name, prm in model.state_dict().items():
+        rec["param::" + name] = prm.numpy()
+    for name, prm in model.named_parameters():
+        rec["grad::" + name] = prm.grad.numpy()
+    path = os.path.join(HERE, "lm_tiny.npz")
+    np.savez_compressed(path, **rec)
+    print(f"lm_tiny loss={loss.item():.5f} -> {os.path.getsize(path) / 1024:.1f} KiB")
+
+
 def make_proj_fixtures(only):
     for name in PROJ_CASES:
         if only and name not in only:
@@ -137,6 +178,8 @@ def main():
     from models.ssd_complex import ssd_complex_chunkwise  # the reference itself
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if not args.only or "lm_tiny" in args.only:
+        make_lm_fixture()
     make_proj_fixtures(args.only)
     for name in CASES:
         if args.only and name not in args.only:

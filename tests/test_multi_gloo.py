@@ -46,9 +46,37 @@ def _worker(rank, world, port, mode, q):
             xs = mdist.shard_inputs(*t, world=world, rank=rank)
             y = O.ssd_chunkwise(*[v.numpy() for v in xs], chunk_size=chunk)
             q.put((rank, "ok", (mdist.head_shard(inp["A"].shape[0], world, rank), y)))
+        elif mode == "ddp":
+            q.put((rank, "ok", _ddp_step(rank)))
         dist.destroy_process_group()
     except Exception as e:
         q.put((rank, "raised", f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+def _tiny_lm_step(tokens, targets, ddp=False):
+    """One train_step of the two-layer model of tests/golden/lm_tiny.npz (CPU SSD restatement,
+    fp32) from the fixture's parameters; returns the parameters after the step."""
+    import torch
+    from m3ssd import lm
+    from test_lm_cpu import LM_TINY, _fixture, _ssd_cpu
+    _, params, _ = _fixture()
+    model = lm.Mamba3Transformer(dict(LM_TINY), ssd_fn=_ssd_cpu)
+    model.load_state_dict(params, strict=True)
+    net = torch.nn.parallel.DistributedDataParallel(model) if ddp else model
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+    lm.train_step(net, opt, tokens, targets, amp_dtype=None)
+    return {k: v.detach().numpy().copy() for k, v in model.named_parameters()}
+
+
+def _ddp_step(rank):
+    """Rank r takes row r of the fixture's batch; DDP averages the gradients (complex A
+    included), so every rank ends where one process stepping on the whole batch ends."""
+    import torch
+    from test_lm_cpu import _fixture
+    g, _, _ = _fixture()
+    tok = torch.from_numpy(g["tokens"][rank:rank + 1])
+    tgt = torch.from_numpy(g["targets"][rank:rank + 1])
+    return _tiny_lm_step(tok, tgt, ddp=True)
 
 
 def _run(mode, world=2, timeout=120):
@@ -106,3 +134,19 @@ def test_sharded_problem_recombines():
         assert out[r][0] == "ok", out[r]
         (h0, h1), y = out[r][1]
         np.testing.assert_array_equal(y, y_full[:, :, h0:h1])
+
+
+def test_ddp_train_step_matches_one_process_on_the_whole_batch():
+    """The whole-model data-parallel step (m3ssd.lm under DistributedDataParallel, gloo, two
+    ranks, one row of the batch each) ends with the parameters one process reaches on both rows."""
+    import torch
+    from test_lm_cpu import _fixture
+    out = _run("ddp", timeout=300)
+    g, _, _ = _fixture()
+    want = _tiny_lm_step(torch.from_numpy(g["tokens"]), torch.from_numpy(g["targets"]))
+    for r in range(2):
+        assert out[r][0] == "ok", out[r]
+        got = out[r][1]
+        assert sorted(got) == sorted(want)
+        for k in want:
+            np.testing.assert_allclose(got[k], want[k], rtol=2e-5, atol=2e-6, err_msg=k)
