@@ -146,11 +146,24 @@ class Mamba3Transformer(nn.Module):
         if isinstance(module, (nn.Linear, nn.Embedding)):
             nn.init.normal_(module.weight, mean=0.0, std=self.cfg.init_std)
 
+    def _logits(self, h: torch.Tensor) -> torch.Tensor:
+        """lm_head(h). On the GPU the head's rows are padded to a multiple of 64: with the
+        reference's 50257-entry vocabulary the logits' row stride is not 16-byte aligned and
+        cuBLAS falls back to an old unaligned tensor-op kernel (~7x slower on the head's three
+        GEMMs); the padded GEMM writes aligned rows, and its first `vocab_size` columns are the
+        logits (a strided view)."""
+        V = self.cfg.vocab_size
+        pad = (-V) % 64
+        if pad == 0 or h.device.type != "cuda":
+            return self.lm_head(h)
+        w = F.pad(self.lm_head.weight, (0, 0, 0, pad))
+        return F.linear(h, w)[..., :V]
+
     def forward(self, tokens: torch.Tensor) -> torch.Tensor:
         x = self.embed(tokens)
         for layer in self.layers:
             x = layer(x)
-        return self.lm_head(self.norm_f(x))
+        return self._logits(self.norm_f(x))
 
 
 def train_step(model: nn.Module, optimizer: torch.optim.Optimizer, tokens: torch.Tensor,
