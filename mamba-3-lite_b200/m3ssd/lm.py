@@ -146,24 +146,31 @@ class Mamba3Transformer(nn.Module):
         if isinstance(module, (nn.Linear, nn.Embedding)):
             nn.init.normal_(module.weight, mean=0.0, std=self.cfg.init_std)
 
-    def _logits(self, h: torch.Tensor) -> torch.Tensor:
-        """lm_head(h). On the GPU the head's rows are padded to a multiple of 64: with the
+    def _padded_logits(self, h: torch.Tensor) -> torch.Tensor:
+        """lm_head(h) with the head's rows padded to a multiple of 64 on the GPU: with the
         reference's 50257-entry vocabulary the logits' row stride is not 16-byte aligned and
         cuBLAS falls back to an old unaligned tensor-op kernel (~7x slower on the head's three
-        GEMMs); the padded GEMM writes aligned rows, and its first `vocab_size` columns are the
-        logits (a strided view)."""
-        V = self.cfg.vocab_size
-        pad = (-V) % 64
+        GEMMs). The first `vocab_size` columns are the logits."""
+        pad = (-self.cfg.vocab_size) % 64
         if pad == 0 or h.device.type != "cuda":
             return self.lm_head(h)
-        w = F.pad(self.lm_head.weight, (0, 0, 0, pad))
-        return F.linear(h, w)[..., :V]
+        return F.linear(h, F.pad(self.lm_head.weight, (0, 0, 0, pad)))
 
-    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, targets: torch.Tensor | None = None) -> torch.Tensor:
+        """Logits (B, T, vocab) as the reference's model returns them; with ``targets`` the mean
+        cross-entropy instead (ignore_index -100), computed on the padded logits with the pad
+        columns at -inf (the same loss, without copying the logits out of their padded rows)."""
         x = self.embed(tokens)
         for layer in self.layers:
             x = layer(x)
-        return self._logits(self.norm_f(x))
+        logits = self._padded_logits(self.norm_f(x))
+        V = self.cfg.vocab_size
+        if targets is None:
+            return logits[..., :V]
+        if logits.size(-1) > V:
+            logits[..., V:] = float("-inf")  # exp(-inf) = 0: the pad columns add nothing
+        return F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1),
+                               ignore_index=-100)
 
 
 def train_step(model: nn.Module, optimizer: torch.optim.Optimizer, tokens: torch.Tensor,
@@ -175,9 +182,7 @@ def train_step(model: nn.Module, optimizer: torch.optim.Optimizer, tokens: torch
     ctx = (torch.autocast(device_type, dtype=amp_dtype) if amp_dtype is not None
            else torch.autocast(device_type, enabled=False))
     with ctx:
-        logits = model(tokens)
-        loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1),
-                               ignore_index=-100)
+        loss = model(tokens, targets)  # the reference's cross-entropy over model(tokens)
     loss.backward()
     nn.utils.clip_grad_norm_(model.parameters(), max_grad_norm)
     optimizer.step()

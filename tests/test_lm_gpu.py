@@ -45,6 +45,10 @@ def test_lm_with_cuda_operator_matches_reference_model(cuda_device):
     loss.backward()
     for k, p in model.named_parameters():
         assert _rel(p.grad.cpu().numpy(), grads[k]) < tol["g_normwise"], k
+    # the training form: cross-entropy on the padded logits (pad columns at -inf)
+    with torch.no_grad():
+        fused_loss = model(tokens, targets)
+    assert abs(fused_loss.item() - loss.item()) < 1e-6 * abs(loss.item())
 
 
 def test_bf16_autocast_fused_equals_block_composition(cuda_device):
