@@ -293,10 +293,10 @@ const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
 int m3ssd_launch_count(const m3ssd_problem* prob, int backward) {
   if (check_problem(prob) != M3SSD_OK) return 0;
   if (!tc_shape(prob)) return backward ? m3ssd::simt::kBwdLaunches : m3ssd::simt::kFwdLaunches;
-  // the chained form: two passes (the records once) plus the segment chain (and, backward, the
-  // segments' end-state terms)
+  // the chained forms: forward two passes (the records once) plus the segment chain; backward the
+  // carry pass, the segment chain, the segments' end-state terms and the tensor-core pass
   const bool chained = m3ssd::tc::chains_for(make_problem(prob), backward != 0) > 1;
-  if (backward) return chained ? 2 * m3ssd::tc::kBwdLaunches + 2 : m3ssd::tc::kBwdLaunches;
+  if (backward) return chained ? m3ssd::tc::kBwdLaunches + 3 : m3ssd::tc::kBwdLaunches;
   return chained ? 2 * m3ssd::tc::kFwdLaunches : m3ssd::tc::kFwdLaunches;
 }
 

@@ -4,20 +4,23 @@
 // backward: dS_z -> dS_{z-1}); each hand-off costs a few microseconds of latency, so a sequence of
 // nc chunks takes at least nc hand-offs whatever the work. At B4 L16384 with two heads per GPU
 // (8 sequences of 256 chunks) that chain, not HBM, sets the time. Here each sequence's chunks run
-// as G chains of nc / G chunks in the same kernels, in two passes:
+// as G chains of nc / G chunks, in two passes:
 //
-//   forward   pass 1: every chain from a zero entry state; its end state L_s goes to scratch
+//   forward   pass 1: the tensor-core forward, every chain from a zero entry state; its end state
+//                     L_s goes to scratch (its y is overwritten by pass 2)
 //             chain:  S_0 = h0 (or 0), S_{s+1} = D_s S_s + L_s over the segments (D_s = the
 //                     segment's total decay, the product of its chunks' e^Gamma), S_G = final state
-//             pass 2: every chain from its true entry state S_s: y and the chunk-entry states
-//   backward  pass 1: every chain from a zero end-state gradient; its entry-state gradient P_s
+//             pass 2: the tensor-core forward, every chain from its true entry state S_s: y and
+//                     the chunk-entry states
+//   backward  pass 1: every chain's entry-state gradient P_s from a zero end-state gradient
+//                     (k_chain_bwd_pass1, CUDA cores, one CTA per chain: only the carry)
 //             chain:  dS_G = dhT (or 0), dS_s = P_{s+1} + conj(D_{s+1}) dS_{s+1} going back, and
 //                     each segment's last-chunk d Sigma term <dS_s, conj(S_{s+1})>
-//             pass 2: every chain from its true end-state gradient: all gradients
+//             pass 2: the tensor-core backward, every chain from its true end-state gradient
 //
 // Every chain's algebra is the reference's recurrence split at segment boundaries
 // (s_t = e^{a_t} s_{t-1} + B_t x_t^T is linear in s), so the result equals the one-pass path's
-// up to rounding. Pass 1 writes y (forward) or the gradients (backward) that pass 2 overwrites.
+// up to rounding.
 #include <cuda_runtime.h>
 
 #include "tc_path.h"
@@ -142,6 +145,120 @@ __global__ void __launch_bounds__(256) k_chain_dgam(const float* __restrict__ st
   }
 }
 
+// First backward pass of the chained form on CUDA cores, one CTA per chain, its chunks in reverse,
+// the chain's carry in registers: G <- conj(e^Gamma) G + sum_l w_l[n] dy_l[p] with
+// w_l = conj(C_l e^{Sigma_l}), from zero; the chain's entry-state gradient goes to
+// out[bh * G + segment] in the (n, p) layout of the state arguments. Only the carry of a chunk is
+// needed, not its gradients, so this replaces a full tensor-core backward pass (~80 ns per chunk
+// of throughput) by one 64 x 64 x 64 complex-by-real product per chunk (~35 ns). Each thread owns
+// a 4 n x 4 p block of the carry. (The same form for the forward's end states measured slower
+// than the tensor-core forward pass, whose chunks cost ~43 ns: along a chain each chunk here
+// takes ~8 us.)
+struct Pass1Args {
+  const float2* bc;  // C, interleaved complex or planar (see Problem)
+  long long bcs[4];
+  int planar;
+  const void* dy;
+  long long dys[4];
+  int dy_bf16;
+  const ChunkRec* recs;
+  int T, H, nc, G;
+};
+
+__global__ void __launch_bounds__(256) k_chain_bwd_pass1(const Pass1Args a, float2* __restrict__ out) {
+  __shared__ __align__(16) float2 sW[64][64];
+  __shared__ __align__(16) float sR[64][64];
+  const int tid = threadIdx.x;
+  const int sg = blockIdx.x, bh = sg / a.G, sgm = sg - bh * a.G, seg = a.nc / a.G;
+  const int b = bh / a.H, h = bh - b * a.H;
+  const int n0 = 4 * (tid >> 4), p0 = 4 * (tid & 15);
+  float2 st[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) st[i][k] = cz();
+  for (int it = 0; it < seg; ++it) {
+    const int z = sgm * seg + seg - 1 - it;
+    const ChunkRec* rec = a.recs + (long long)bh * a.nc + z;
+    __syncthreads();  // the previous chunk's tiles are no longer read
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int e = tid + 256 * i, l = e >> 6, c = e & 63, t = z * 64 + l;
+      float2 v = cz();
+      float r = 0.f;
+      if (t < a.T) {
+        if (a.planar) {
+          const float* f = reinterpret_cast<const float*>(a.bc) + b * a.bcs[0] + t * a.bcs[1] +
+                           h * a.bcs[2] + c * a.bcs[3];
+          v = make_float2(f[0], f[(long long)a.H * 64]);
+        } else {
+          v = a.bc[b * a.bcs[0] + t * a.bcs[1] + h * a.bcs[2] + c * a.bcs[3]];
+        }
+        const long long o = b * a.dys[0] + t * a.dys[1] + h * a.dys[2] + c * a.dys[3];
+        r = a.dy_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.dy)[o])
+                      : static_cast<const float*>(a.dy)[o];
+      }
+      // conj(C e^{Sigma_l}) = conj(C) el conj(cis)
+      const float2 cs = rec->cis[l];
+      sW[l][c] = cmul(cconj(v), make_float2(rec->el[l] * cs.x, -rec->el[l] * cs.y));
+      sR[l][c] = r;
+    }
+    __syncthreads();
+    float2 acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[i][k] = cz();
+#pragma unroll 4
+    for (int l = 0; l < 64; ++l) {
+      const float4 w01 = *reinterpret_cast<const float4*>(&sW[l][n0]);
+      const float4 w23 = *reinterpret_cast<const float4*>(&sW[l][n0 + 2]);
+      const float4 r4 = *reinterpret_cast<const float4*>(&sR[l][p0]);
+      const float2 w[4] = {make_float2(w01.x, w01.y), make_float2(w01.z, w01.w),
+                           make_float2(w23.x, w23.y), make_float2(w23.z, w23.w)};
+      const float r[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[i][k].x = fmaf(w[i].x, r[k], acc[i][k].x);
+          acc[i][k].y = fmaf(w[i].y, r[k], acc[i][k].y);
+        }
+    }
+    const float2 f = cconj(rec->g);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) st[i][k] = cadd(cmul(f, st[i][k]), acc[i][k]);
+  }
+  float2* dst = out + (long long)sg * kStateElems;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4* row = reinterpret_cast<float4*>(dst + (n0 + i) * 64 + p0);
+    row[0] = make_float4(st[i][0].x, st[i][0].y, st[i][1].x, st[i][1].y);
+    row[1] = make_float4(st[i][2].x, st[i][2].y, st[i][3].x, st[i][3].y);
+  }
+}
+
+Pass1Args pass1_args(const Problem& p, const void* dy, const long long dys[4],
+                     const ChunkRec* recs, int G) {
+  Pass1Args a{};
+  a.bc = p.Cm;
+  for (int i = 0; i < 4; ++i) {
+    a.bcs[i] = p.cs[i];
+    a.dys[i] = dys[i];
+  }
+  a.planar = p.bc_planar;
+  a.dy = dy;
+  a.dy_bf16 = p.y_bf16;
+  a.recs = recs;
+  a.T = p.T;
+  a.H = p.H;
+  a.nc = (p.T + 63) / 64;
+  a.G = G;
+  return a;
+}
+
 }  // namespace
 
 // Time model of one pass (microseconds, fitted to one-pass runs on B200): a ticket (one chunk of
@@ -162,7 +279,11 @@ int chains_for(const Problem& p, bool backward) {
   int best_g = 1;
   for (int G = 2; G <= kMaxChains && nc / G >= 2; G *= 2) {
     if (nc % G != 0) break;  // a larger power of two does not divide nc either
-    const double est = 2.0 * pass((double)(nc / G) * hop) + 10.0 + 0.5 * G;
+    // first pass (forward: the tensor-core pass; backward: the CUDA-core carry pass, ~35 ns of
+    // throughput per chunk, ~8 us per chunk along a chain), the tensor-core pass, the chains
+    const double first = backward ? fmax(bh * nc * 0.035, (double)(nc / G) * 8.0) + 3.0
+                                  : pass((double)(nc / G) * hop);
+    const double est = first + pass((double)(nc / G) * hop) + 10.0 + 0.5 * G;
     if (est < best) {
       best = est;
       best_g = G;
@@ -207,16 +328,15 @@ int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], con
   float2* P = reinterpret_cast<float2*>(base + al256(bwd_workspace_bytes(p, G)));
   float2* dE = P + (size_t)p.Bsz * p.H * G * kStateElems;
   float2* dgam = dE + (size_t)p.Bsz * p.H * G * kStateElems;
-  int rc = run_bwd(p, dy, dys, states, out, ws, st, nullptr, nullptr, P, G, nullptr, true);
-  if (rc != M3SSD_OK) return rc;
   const ChunkRec* recs =
       reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
+  k_chain_bwd_pass1<<<p.Bsz * p.H * G, 256, 0, st>>>(pass1_args(p, dy, dys, recs, G), P);
   k_chain_bwd<<<dim3(p.Bsz * p.H, kStateElems / 256), 256, 0, st>>>(
       recs, nc, G, static_cast<const float2*>(dhT), P, dE, static_cast<float2*>(dh0));
   k_chain_dgam<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float*>(states), nc, G, dE,
                                                 static_cast<const float2*>(hT), dgam);
   if (cudaGetLastError() != cudaSuccess) return M3SSD_ERR_LAUNCH;
-  return run_bwd(p, dy, dys, states, out, ws, st, nullptr, dE, nullptr, G, dgam, false);
+  return run_bwd(p, dy, dys, states, out, ws, st, nullptr, dE, nullptr, G, dgam, true);
 }
 
 }  // namespace tc
