@@ -91,6 +91,11 @@ def test_long_few_sequences_run_as_chains(lib):
     assert lib.m3ssd_launch_count(ctypes.byref(long_), 1) == 5
     one_pass = 256 + 4 * 4 * 2 * 256  # status word, counter, one flag per chunk
     assert lib.m3ssd_fwd_workspace_bytes(ctypes.byref(long_)) > one_pass
+    # the chained shapes of tests/test_proj_gpu.py
+    for kw in (dict(batch=1, seqlen=4096, nheads=2), dict(batch=2, seqlen=4096, nheads=4)):
+        p = prob(**kw)
+        assert lib.m3ssd_launch_count(ctypes.byref(p), 0) == 4, kw
+        assert lib.m3ssd_launch_count(ctypes.byref(p), 1) == 5, kw
     # the fp32 path has no chained form
     assert lib.m3ssd_launch_count(ctypes.byref(prob(batch=4, seqlen=16384, nheads=2, flags=0x1)),
                                   0) == lib.m3ssd_launch_count(ctypes.byref(prob(headdim=32)), 0)

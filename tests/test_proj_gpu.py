@@ -64,6 +64,7 @@ def _composed(m3, proj, A, dy, H, chunk=64):
     (3, 200, 4, 64),     # T not a multiple of the chunk
     (1, 64, 4, 128),     # chunk 128 (the kernels block at 64; the result does not depend on it)
     (2, 1000, 8, 64),
+    (1, 4096, 2, 64),    # few long sequences: both directions run as chains (planar C in the carry pass)
 ])
 def test_fused_equals_composition_bitwise(m3, cuda_device, B, T, H, chunk):
     proj, A, dy = _case(cuda_device, B, T, H, seed=B * 1000 + T)
@@ -159,7 +160,8 @@ def test_fused_against_fp64_block_shape(m3, cuda_device):
     assert rel(ga, a64.grad) < tol["g_normwise"]
 
 
-@pytest.mark.parametrize("T,fused", [(2048, True), (200, True), (200, False)])
+# T = 4096 (8 sequences of 64 chunks) runs as chains: the carry pass reads dy as bf16 there too
+@pytest.mark.parametrize("T,fused", [(2048, True), (200, True), (200, False), (4096, True)])
 def test_bf16_readout(m3, cuda_device, T, fused):
     """y_dtype=bfloat16: the kernels round y in their store and read dy as bf16. y is bit-equal to
     the fp32 result rounded, and the gradients equal those of the fp32 path fed the same (bf16)
