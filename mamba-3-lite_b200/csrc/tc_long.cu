@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(256) k_chain_dgam(const float* __restrict__ st
 // a 4 n x 4 p block of the carry. (The same form for the forward's end states measured slower
 // than the tensor-core forward pass, whose chunks cost ~43 ns: along a chain each chunk here
 // takes ~8 us.)
-struct Pass1Args {
+struct CarryPassArgs {
   const float2* bc;  // C, interleaved complex or planar (see Problem)
   long long bcs[4];
   int planar;
@@ -165,7 +165,8 @@ struct Pass1Args {
   int T, H, nc, G;
 };
 
-__global__ void __launch_bounds__(256) k_chain_bwd_pass1(const Pass1Args a, float2* __restrict__ out) {
+__global__ void __launch_bounds__(256) k_chain_bwd_pass1(const CarryPassArgs a,
+                                                         float2* __restrict__ out) {
   __shared__ __align__(16) float2 sW[64][64];
   __shared__ __align__(16) float sR[64][64];
   const int tid = threadIdx.x;
@@ -240,9 +241,9 @@ __global__ void __launch_bounds__(256) k_chain_bwd_pass1(const Pass1Args a, floa
   }
 }
 
-Pass1Args pass1_args(const Problem& p, const void* dy, const long long dys[4],
-                     const ChunkRec* recs, int G) {
-  Pass1Args a{};
+CarryPassArgs carry_pass_args(const Problem& p, const void* dy, const long long dys[4],
+                              const ChunkRec* recs, int G) {
+  CarryPassArgs a{};
   a.bc = p.Cm;
   for (int i = 0; i < 4; ++i) {
     a.bcs[i] = p.cs[i];
@@ -330,7 +331,7 @@ int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], con
   float2* dgam = dE + (size_t)p.Bsz * p.H * G * kStateElems;
   const ChunkRec* recs =
       reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
-  k_chain_bwd_pass1<<<p.Bsz * p.H * G, 256, 0, st>>>(pass1_args(p, dy, dys, recs, G), P);
+  k_chain_bwd_pass1<<<p.Bsz * p.H * G, 256, 0, st>>>(carry_pass_args(p, dy, dys, recs, G), P);
   k_chain_bwd<<<dim3(p.Bsz * p.H, kStateElems / 256), 256, 0, st>>>(
       recs, nc, G, static_cast<const float2*>(dhT), P, dE, static_cast<float2*>(dh0));
   k_chain_dgam<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float*>(states), nc, G, dE,
