@@ -208,7 +208,7 @@ def run_long_workload(args):
     """Few long sequences: B4 L16384 H16 with slow decays, its 16 heads sharded over the job's
     GPUs (one process per GPU, no collective in the op; strong scaling). `--long-shard K` runs one
     GPU's share of a K-GPU job (16 / K heads) on each rank instead. `value` is the job's tokens
-    (all heads of a token) per second; `per_gpu` the SURVEY-style B * L * H_local / H / time."""
+    (all heads of a token) per second; `per_gpu` is B * L * H_local / H / time."""
     import ctypes
 
     import torch
