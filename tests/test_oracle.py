@@ -165,3 +165,48 @@ def test_adjoint_state_gradients_match_finite_differences():
     dtm["dt"][0, 3, 1] -= eps
     fd = (loss(dtp, s0) - loss(dtm, s0)) / (2 * eps)
     assert abs(fd - g[4][0, 3, 1]) < 1e-6 * max(1.0, abs(fd))
+
+
+def test_chained_segments_algebra_matches_the_whole_sequence():
+    """The decomposition the chained kernels run (tc_long.cu), on the fp64 recurrence: each
+    segment from a zero state gives its end state L_s; S_{s+1} = D_s S_s + L_s with D_s the
+    segment's total decay; every segment rerun from S_s gives the whole sequence's y. Backward:
+    each segment's entry-state gradient P_s with a zero end gradient; dE_{s-1} = P_s +
+    conj(D_s) dE_s; every segment rerun with its end gradient dE_s and entry state S_s gives the
+    whole sequence's gradients (dA summed over segments)."""
+    B, T, H, D, N, G = 1, 24, 2, 3, 2, 4
+    inp = cases.ref_style_inputs(9, B, T, H, D, N, complex_x=False)
+    rng = np.random.default_rng(9)
+    dy = rng.standard_normal((B, T, H, D))
+    seg = T // G
+
+    def part(k):
+        return {n: (v if n == "A" else v[:, k * seg:(k + 1) * seg]) for n, v in inp.items()}
+
+    sp = O.softplus_f64(inp["dt"])
+    A = np.asarray(inp["A"]).astype(np.complex128)
+    Dk = [np.exp(np.sum(sp[:, k * seg:(k + 1) * seg] * A, axis=1))[:, :, None, None]
+          for k in range(G)]                                              # (B, H, 1, 1)
+    L = [O.ssd_naive(**part(k), return_state=True)[1] for k in range(G)]
+    S = [np.zeros_like(L[0])]
+    for k in range(G):
+        S.append(Dk[k] * S[k] + L[k])
+    y_full, s_full = O.ssd_naive(**inp, return_state=True)
+    y_seg = np.concatenate([O.ssd_naive(**part(k), s0=S[k]) for k in range(G)], axis=1)
+    np.testing.assert_allclose(y_seg, y_full, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(S[G], s_full, rtol=1e-12, atol=1e-12)
+
+    full = O.ssd_naive_grads(**inp, dy=dy)
+    zero = np.zeros_like(L[0])
+    P = [O.ssd_naive_grads(**part(k), dy=dy[:, k * seg:(k + 1) * seg], s0=zero, dsT=zero)[5]
+         for k in range(G)]
+    dE = [None] * G
+    dE[G - 1] = zero
+    for k in range(G - 1, 0, -1):
+        dE[k - 1] = P[k] + np.conj(Dk[k]) * dE[k]
+    parts = [O.ssd_naive_grads(**part(k), dy=dy[:, k * seg:(k + 1) * seg], s0=S[k], dsT=dE[k])
+             for k in range(G)]
+    for i, name in enumerate(("dx", "dA", "dB", "dC", "ddt")):
+        got = (sum(p[i] for p in parts) if name == "dA"
+               else np.concatenate([p[i] for p in parts], axis=1))
+        np.testing.assert_allclose(got, full[i], rtol=1e-10, atol=1e-12, err_msg=name)
