@@ -241,6 +241,125 @@ __global__ void __launch_bounds__(256) k_chain_bwd_pass1(const CarryPassArgs a,
   }
 }
 
+// The same carry pass with the next chunk's C and dy tiles copied into shared memory (cp.async,
+// 16 bytes per copy) while the current chunk is multiplied, and the decay applied to the landed C
+// tile in place. For interleaved C with a contiguous state dimension and fp32 dy with a contiguous
+// head dimension, rows 16-byte aligned (carry_tiled_ok); other layouts take k_chain_bwd_pass1.
+constexpr int kCarryTiledSmem = 2 * 64 * 64 * ((int)sizeof(float2) + (int)sizeof(float));
+
+__device__ __forceinline__ void cp_async16(float* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(256) k_chain_bwd_pass1_tiled(const CarryPassArgs a,
+                                                               float2* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float2* sC = reinterpret_cast<float2*>(smem);                      // [2][64 l][64 n]
+  float* sD = reinterpret_cast<float*>(smem + 2 * 64 * 64 * sizeof(float2));  // [2][64 l][64 p]
+  const int tid = threadIdx.x;
+  const int sg = blockIdx.x, bh = sg / a.G, sgm = sg - bh * a.G, seg = a.nc / a.G;
+  const int b = bh / a.H, h = bh - b * a.H;
+  const int n0 = 4 * (tid >> 4), p0 = 4 * (tid & 15);
+  const float* dyf = static_cast<const float*>(a.dy);
+  // copies of chunk `it` (chunks in reverse) into buffer `buf`; rows past T are zero-filled
+  auto issue = [&](int it, int buf) {
+    const int z = sgm * seg + seg - 1 - it;
+    float* cdst = reinterpret_cast<float*>(sC + buf * 4096);
+    float* ddst = sD + buf * 4096;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // C: 64 rows x 32 copies of 2 complex
+      const int e = tid + 256 * i, l = e >> 5, q = e & 31, t = z * 64 + l;
+      float* d = cdst + l * 128 + 4 * q;
+      if (t < a.T)
+        cp_async16(d, a.bc + b * a.bcs[0] + t * a.bcs[1] + h * a.bcs[2] + 2 * q);
+      else
+        *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // dy: 64 rows x 16 copies of 4 floats
+      const int e = tid + 256 * i, l = e >> 4, q = e & 15, t = z * 64 + l;
+      float* d = ddst + l * 64 + 4 * q;
+      if (t < a.T)
+        cp_async16(d, dyf + b * a.dys[0] + t * a.dys[1] + h * a.dys[2] + 4 * q);
+      else
+        *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float2 st[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) st[i][k] = cz();
+  issue(0, 0);
+  for (int it = 0; it < seg; ++it) {
+    const int buf = it & 1;
+    if (it + 1 < seg) {
+      issue(it + 1, buf ^ 1);  // that buffer was last read before the previous iteration's barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // every thread's copies of this chunk have landed
+    const int z = sgm * seg + seg - 1 - it;
+    const ChunkRec* rec = a.recs + (long long)bh * a.nc + z;
+    float2* cb = sC + buf * 4096;
+    const float* db = sD + buf * 4096;
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {  // conj(C e^{Sigma_l}) = conj(C) el conj(cis), in place
+      const int e = tid + 256 * i, l = e >> 6;
+      const float2 cs = rec->cis[l];
+      const float el = rec->el[l];
+      cb[e] = cmul(cconj(cb[e]), make_float2(el * cs.x, -el * cs.y));
+    }
+    __syncthreads();
+    float2 acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[i][k] = cz();
+#pragma unroll 4
+    for (int l = 0; l < 64; ++l) {
+      const float4 w01 = *reinterpret_cast<const float4*>(cb + l * 64 + n0);
+      const float4 w23 = *reinterpret_cast<const float4*>(cb + l * 64 + n0 + 2);
+      const float4 r4 = *reinterpret_cast<const float4*>(db + l * 64 + p0);
+      const float2 w[4] = {make_float2(w01.x, w01.y), make_float2(w01.z, w01.w),
+                           make_float2(w23.x, w23.y), make_float2(w23.z, w23.w)};
+      const float r[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[i][k].x = fmaf(w[i].x, r[k], acc[i][k].x);
+          acc[i][k].y = fmaf(w[i].y, r[k], acc[i][k].y);
+        }
+    }
+    const float2 f = cconj(rec->g);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) st[i][k] = cadd(cmul(f, st[i][k]), acc[i][k]);
+    __syncthreads();  // this buffer is refilled by the next iteration's copies
+  }
+  float2* dst = out + (long long)sg * kStateElems;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float4* row = reinterpret_cast<float4*>(dst + (n0 + i) * 64 + p0);
+    row[0] = make_float4(st[i][0].x, st[i][0].y, st[i][1].x, st[i][1].y);
+    row[1] = make_float4(st[i][2].x, st[i][2].y, st[i][3].x, st[i][3].y);
+  }
+}
+
+// 16-byte copies of whole rows: interleaved C with a contiguous state dimension, fp32 dy with a
+// contiguous head dimension, every row start 16-byte aligned
+bool carry_tiled_ok(const Problem& p, const void* dy, const long long dys[4]) {
+  if (p.bc_planar || p.y_bf16) return false;
+  if (p.cs[3] != 1 || p.cs[0] % 2 || p.cs[1] % 2 || p.cs[2] % 2) return false;
+  if (reinterpret_cast<uintptr_t>(p.Cm) % 16 || reinterpret_cast<uintptr_t>(dy) % 16) return false;
+  return dys[3] == 1 && dys[0] % 4 == 0 && dys[1] % 4 == 0 && dys[2] % 4 == 0;
+}
+
 CarryPassArgs carry_pass_args(const Problem& p, const void* dy, const long long dys[4],
                               const ChunkRec* recs, int G) {
   CarryPassArgs a{};
@@ -331,7 +450,15 @@ int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], con
   float2* dgam = dE + (size_t)p.Bsz * p.H * G * kStateElems;
   const ChunkRec* recs =
       reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
-  k_chain_bwd_pass1<<<p.Bsz * p.H * G, 256, 0, st>>>(carry_pass_args(p, dy, dys, recs, G), P);
+  const CarryPassArgs ca = carry_pass_args(p, dy, dys, recs, G);
+  if (carry_tiled_ok(p, dy, dys)) {
+    if (cudaFuncSetAttribute(k_chain_bwd_pass1_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kCarryTiledSmem) != cudaSuccess)
+      return M3SSD_ERR_LAUNCH;
+    k_chain_bwd_pass1_tiled<<<p.Bsz * p.H * G, 256, kCarryTiledSmem, st>>>(ca, P);
+  } else {
+    k_chain_bwd_pass1<<<p.Bsz * p.H * G, 256, 0, st>>>(ca, P);
+  }
   k_chain_bwd<<<dim3(p.Bsz * p.H, kStateElems / 256), 256, 0, st>>>(
       recs, nc, G, static_cast<const float2*>(dhT), P, dE, static_cast<float2*>(dh0));
   k_chain_dgam<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float*>(states), nc, G, dE,
