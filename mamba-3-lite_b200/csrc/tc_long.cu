@@ -13,7 +13,8 @@
 //             pass 2: the tensor-core forward, every chain from its true entry state S_s: y and
 //                     the chunk-entry states
 //   backward  pass 1: every chain's entry-state gradient P_s from a zero end-state gradient
-//                     (k_chain_bwd_pass1, CUDA cores, one CTA per chain: only the carry)
+//                     (k_chain_bwd_pass1_tiled / k_chain_bwd_pass1, CUDA cores, one CTA per
+//                     chain: only the carry)
 //             chain:  dS_G = dhT (or 0), dS_s = P_{s+1} + conj(D_{s+1}) dS_{s+1} going back, and
 //                     each segment's last-chunk d Sigma term <dS_s, conj(S_{s+1})>
 //             pass 2: the tensor-core backward, every chain from its true end-state gradient
