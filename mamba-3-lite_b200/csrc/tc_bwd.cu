@@ -28,9 +28,12 @@
 #include "m3ssd_common.cuh"
 #include "tc_common.cuh"
 #include "tc_path.h"
+#include "tc_trace.cuh"
 
 namespace m3ssd {
 namespace tc {
+
+M3_TRACE_DEFINE(m3ssd_trace_set_bwd)
 
 namespace {
 
@@ -434,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the row sums of this ticket are in once every worker warp has arrived at bar_db; its
       // record slot and <dS_z, H_{z+1}> are not reloaded before this warp's bar_rel arrival
       mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
+      M3_TRACE(it, 31);
       {
         const ChunkRec& rec = m.rec[ph];
         const float2 dgam = !q.last ? make_float2(m.dgam[ph].x, m.dgam[ph].y)
@@ -524,18 +528,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t id64 = idesc_bf16(128, 64, 0, 0), idq = idesc_bf16(128, 128, 1, 1);
         const uint32_t id128 = idesc_bf16(128, 128, 0, 1);
         mbar_wait(&m.bar_opa, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 21);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
           mma_run4<32, 32>(tmem + COL_DM, sdesc(sb + OFF_DY, 16, 1024),
                            sdesc(sb + OFF_X + hp * 1024u, 16, 2048), id64, hp == 0);
         mbar_wait(&m.bar_opc, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 22);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
           mma_run4<2048, 4096>(tmem + COL_Q, sdesc(sb + OFF_DYT, 8192, 1024),
                                sdesc(sb + OFF_C + hp * 1024u, 16384, 2048), idq, hp == 0);
         mbar_wait(&m.bar_ops1, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 23);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
@@ -545,6 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                              sdesc(sb + OFF_B + ka * 16384u + hp * 1024u, 16, 2048), id64, hp == 0 && ka == 0);
         mma_commit(&m.bar1);
         mbar_wait(&m.bar_oph, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 24);
         tc_fence_after_sync();
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
@@ -561,6 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // After epilogue 1 (dG', Mr written; G, dM read): dCa = dG' conj(B'), dXa = Mr^T dy,
         // dXb = conj(B') dS' into the columns of G and dM
         mbar_wait(&m.bar_ops2, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 25);
         tc_fence_after_sync();
         {
 #pragma unroll
@@ -582,6 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // after the carry (Q read): dBa = dG'^T conj(C') into the columns of Q
         mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 26);
         tc_fence_after_sync();
         {
           const uint32_t idba = idesc_bf16(128, 128, 1, 1);
@@ -593,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // dBb = x dS'x^T (MN) into the columns dCa used, once the workers have read them; its
         // commit also covers dBa
         mbar_wait(&m.bar_colfree, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 27);
         tc_fence_after_sync();
         {
           const uint32_t idbb = idesc_bf16(128, 128, 0, 1);
@@ -607,6 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // finished before arriving at bar_ops1 of this one); the next H_z into sH once the store
         // has read it
         mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 28);
         ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc, p.hp);
         if (nxt < p.total) {
           mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
@@ -619,12 +631,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&m.bar_dx, ph, p.err, kErrMmaWait);
         ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc, 0);
         mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
+        M3_TRACE(it, 29);
         ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc, p.hp);
         if (nxt < p.total) ctl_load_b(&tmB, smem, &m, qn, p.hp);
         bulk_wait_read_all();
         mbar_arrive(&m.bar_stfree);
         if (nxt < p.total)
           ctl_load_ds(smem, &m, p.ring, p.dgring, p.flags, p.err, p.nc, qn, (int)((it + 1) & 1));
+        M3_TRACE(it, 30);
         cur = nxt;
         qc = qn;
         ++it;
@@ -675,6 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // every warp's carry has read conj(H_z) there (bar2 can complete before that)
         mbar_wait(&m.bar_ops3, ph, p.err, kErrMmaWait);
         mbar_wait(&m.bar2, ph, p.err, kErrMmaWait);
+        if (warp == 0) M3_TRACE(it, 15);
         prefetch_l2();
         tc_fence_after_sync();
         {
@@ -690,9 +705,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         warp_arrive(&m.bar_dc, lane);
+        if (warp == 0) M3_TRACE(it, 16);
 
         // ---- epilogue 3: dx = dXa + dec_s dXb -> staging tile in sDGK
         mbar_wait(&m.bar3, ph, p.err, kErrMmaWait);
+        if (warp == 0) M3_TRACE(it, 17);
         tc_fence_after_sync();
         {  // 16x256b reads as in epilogue 1; each column pair leaves as one 8-byte store
           const int q4 = lane & 3, rr = lane >> 2;
@@ -716,8 +733,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         warp_arrive(&m.bar_dx, lane);
+        if (warp == 0) M3_TRACE(it, 18);
         // ---- epilogue 4: dB = conj(dBa + dec_s dBb) cis(theta_s) -> staging tiles in sDYT, sDGM
         mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
+        if (warp == 0) M3_TRACE(it, 19);
         tc_fence_after_sync();
         {
           float2 acc_a, acc_b;
@@ -732,6 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         warp_arrive(&m.bar_db, lane);
+        if (warp == 0) M3_TRACE(it, 20);
         ++it;
       }
       if (next >= p.total) break;
@@ -742,6 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       t0 = q.z * 64;
       const uint32_t ph = it & 1u;
       const ChunkRec& rec = m.rec[ph];
+      if (warp == 0) M3_TRACE(it, 0);
       float xv[8], gv[8];  // this thread's 8 values of x and of dy (row xs0)
       {
         const int tx = t0 + xs0;
@@ -755,6 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           load8(static_cast<const float*>(p.dy) + go, p.dys[3], p.dy_vec, tx < p.T, xp0, gv);
       }
       mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);  // C tile, decay record
+      if (warp == 0) M3_TRACE(it, 1);
 
       // ---- x, dy stacked over rows (K = p); e_l dy stacked over p (MN) once the previous
       // ticket's dx / dB stores have read sDGK / sDYT / sDGM
@@ -774,6 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      sb + OFF_DYT + (ml >> 6) * 8192u + swz(s, (ml & 63u) >> 3), w);
       }
       warp_arrive(&m.bar_opa, lane);  // dM may start
+      if (warp == 0) M3_TRACE(it, 2);
       // ---- raw tiles -> split operands, in place: C' = C cis(theta_l) and
       // conj(B') = conj(B conj(cis(theta_s))) stacked (16 lanes per row), conj(H_z) hi | lo from
       // the forward's thread-major state tile (float4 i of forward thread f at [i][f]; f holds row
@@ -782,6 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = 0; tile < 3; ++tile) {  // C (then Q may start), B (then G), H_z (then dCb)
         if (tile == 1) mbar_wait(&m.bar_tmb, ph, p.err, kErrTmaWait);
         if (tile == 2) mbar_wait(&m.bar_h, ph, p.err, kErrTmaWait);
+        if (warp == 0) M3_TRACE(it, 3 + 2 * tile);
         const uint32_t base = tile == 0 ? OFF_C : (tile == 1 ? OFF_B : OFF_H);
         const bool stacked = tile != 2;
         const float sg = tile == 0 ? 1.f : -1.f;
@@ -835,6 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tile == 0) warp_arrive(&m.bar_opc, lane);   // Q may start
         if (tile == 1) warp_arrive(&m.bar_ops1, lane);  // G may start
         if (tile == 2) warp_arrive(&m.bar_oph, lane);   // dCb may start
+        if (warp == 0) M3_TRACE(it, 4 + 2 * tile);
       }
 
       // ---- dS_z (fp32 in sDS, thread-major as the chunk z+1 ticket stored it: float4 i holds
@@ -842,6 +867,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // -> dS'x hi | lo (K-major rows p: k-atom grp/2, 16-byte chunk 4 (grp mod 2) + k, 4 bytes
       // per complex)
       mbar_wait(&m.bar_ds, ph, p.err, kErrTmaWait);
+      if (warp == 0) M3_TRACE(it, 9);
       float dsz[16];
       if (!q.last) {
 #pragma unroll
@@ -885,7 +911,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // ---- epilogue 1: Mr (over e dy, batch 1 done), dG' (two forms)
+      if (warp == 0) M3_TRACE(it, 10);
       mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
+      if (warp == 0) M3_TRACE(it, 11);
       tc_fence_after_sync();
       // 16x256b TMEM reads (hi / lo partial rows in one thread): rows 16 sub + 8 h + lane/4,
       // columns s = 16 grp + 8 k + 2 (lane%4), +1; each pair leaves as one 4-byte bf16x2 word
@@ -930,6 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       warp_arrive(&m.bar_ops2, lane);
+      if (warp == 0) M3_TRACE(it, 12);
       // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major, the layout above),
       // <dS_{z-1}, H_z>. Q in the 16x256b shape: rows p = 16 sub + 8 h + lane/4, complex
       // 16 grp + 4 k + lane%4 (k = 0..3), hi and lo partial rows added in registers.
@@ -987,8 +1016,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) m.dgp[ph][warp] = dg;
       }
       // (back-pressure for the hand-off warp: it has finished the ticket before this one)
+      if (warp == 0) M3_TRACE(it, 13);
       if (it > 0) mbar_wait(&m.bar_rel, (it - 1) & 1u, p.err, kErrMmaWait);
       warp_arrive(&m.bar_ops3, lane);
+      if (warp == 0) M3_TRACE(it, 14);
       // the next ticket: its x and dy are prefetched at the top of the loop, during the epilogues
       mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
       next = m.tick[(it + 1) & 1];

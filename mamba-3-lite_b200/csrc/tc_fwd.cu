@@ -26,9 +26,12 @@
 #include "m3ssd_common.cuh"
 #include "tc_common.cuh"
 #include "tc_path.h"
+#include "tc_trace.cuh"
 
 namespace m3ssd {
 namespace tc {
+
+M3_TRACE_DEFINE(m3ssd_trace_set_fwd)
 
 namespace {
 
@@ -221,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int z = q.z, bh = q.bh, j = q.j;
     const int b = bh / p.H, h = bh - b * p.H, t0 = z * 64;
     __syncthreads();  // previous ticket done: its MMAs completed, its y tile staged
+    if (warp == 0) M3_TRACE(iter, 0);
     int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
     if (ctrl) {
       if (iter > 0) {  // the previous ticket's y: two 32-column fp32 segments (one bf16) from sXT
@@ -236,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- TMA tiles of B and C land in the operand buffers; rotate and split them in place:
     // B first, then x and x~, so S~ = x~^T B'x runs on the tensor core while C is converted
     mbar_wait(&m.bar_tma, ph, p.err, kErrTmaWait);
+    if (warp == 0) M3_TRACE(iter, 1);
     // all raw values of one tile in registers (each thread: rows j/16, complex 4 (j%16) .. +3 for
     // j = tid + 256 it); written back in place after a barrier
     auto read_tile = [&](uint32_t base, float4 (&r4)[4][2]) {
@@ -296,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       read_tile(OFF_BX, rb);
       if (ctrl) bulk_wait_read_all();  // sXT (y staging) is rewritten below
       __syncthreads();
+      if (warp == 0) M3_TRACE(iter, 2);
       write_tile(1, rb);
       // x (hi, lo) and x~ = exp(rho_Gamma - rho_s) x, stacked over p
       const int s = tid >> 2, pg = tid & 3;
@@ -310,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       split_store16(xtb + swz(s, c4 + 0), xtb + swz(s, c4 + 2), xt);
       split_store16(xtb + swz(s, c4 + 1), xtb + swz(s, c4 + 3), xt + 8);
       read_tile(OFF_CX, rc);
+      if (warp == 0) M3_TRACE(iter, 3);
       // is H_z already published? (then its loads overlap the first MMAs.) Probed as late as
       // the probe's round trip still hides behind the rest of the transform: its value is
       // stored to shared memory at the end of the transform
@@ -317,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     fence_proxy_async_smem();
     __syncthreads();
+    if (warp == 0) M3_TRACE(iter, 4);
     if (tid == 0) {  // MMA batch 1a: S~^T = x~^T B'x (M128 N128)
       tc_fence_after_sync();
       const uint32_t idS = idesc_bf16(128, 128, 1, 1);
@@ -336,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_proxy_async_smem();
     __syncthreads();
     const bool h_early = m.h_ready != 0;
+    if (warp == 0) M3_TRACE(iter, 5);
     // not yet published at the probe: every thread looks again now (no barrier needed later: each
     // thread orders its own H loads after its own observation of the flag)
     uint32_t h_late = 1u;
@@ -354,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                       idG, (hl | j) != 0);
       mma_commit(&m.bar_mma1);
     }
+    if (warp == 0) M3_TRACE(iter, 6);
     float hz[32];
     if (j == 0) {  // a chain's entry state: zero, or h0 (row p = r, complex n = 32 wg + 16 part + c/2)
       if (p.h0 != nullptr) {
@@ -384,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- epilogue 1: Mr = exp(rho_l - rho_s) G (s <= l), split-bf16, stacked rows (over x~)
     float el_r;  // exp(rho_r), kept for the output (the record slot is refilled before it)
     mbar_wait(&m.bar_mma1, ph, p.err, kErrMmaWait);
+    if (warp == 0) M3_TRACE(iter, 7);
     tc_fence_after_sync();
     {
       float v[32];
@@ -406,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     sb + OFF_XT + swz(stack_row(r, 1), ch + 1), mr + 8);
     }
 
+    if (warp == 0) M3_TRACE(iter, 8);
     int nn = 0;
     if (ctrl) nn = (int)atomicAdd(p.counter, 1u);  // next ticket; stored at the state update
 
@@ -424,6 +436,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         hz[4 * i + 3] = v.w;
       }
     }
+    if (warp == 0) M3_TRACE(iter, 9);
     // conj(H_z) interleaved as a K-major B operand [k-atom][p][64 k] (hi | lo), over B'x
     {
       float w[32];
@@ -438,6 +451,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_proxy_async_smem();
     tc_fence_before_sync();
     __syncthreads();
+    if (warp == 0) M3_TRACE(iter, 10);
     if (tid == 0) {  // Y1 = Mr x, Y2 = Re(C' H_z) as C'x conj(H)x
       tc_fence_after_sync();
       const uint32_t idY1 = idesc_bf16(128, 64, 0, 1);
@@ -459,6 +473,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                       idY2, (hl | j) != 0);
       mma_commit(&m.bar_mma3);
     }
+    if (warp == 0) M3_TRACE(iter, 11);
 
     // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~, publish for chunk z+1
     {
@@ -509,15 +524,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_before_sync();
     __syncthreads();
     next = m.nxt;
+    if (warp == 0) M3_TRACE(iter, 12);
     // the barrier orders every thread's H stores before this gpu-scope release. Its fence costs
     // the control thread's warp ~1 us wherever it is placed (measured: here, after the output
     // epilogue, or with no loads of the warp in flight); here it also publishes H_{z+1} soonest.
     if (ctrl && j + 1 < (kChains ? p.seg : p.nc)) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+    if (ctrl) M3_TRACE(iter, 16);
 
     // ---- output y = Y1 + exp(rho_l) Y2 into the staging tile in sXT; the next ticket's B, C
     // tiles and record load as soon as the last MMA has read sCX / sBX
     mbar_wait(&m.bar_mma2, ph, p.err, kErrMmaWait);
     mbar_wait(&m.bar_mma3, ph, p.err, kErrMmaWait);
+    if (warp == 0) M3_TRACE(iter, 13);
     tc_fence_after_sync();
     if (ctrl && next < p.total) issue_tma(next);
     // x of the next ticket, issued after the waits (a wait that falls through to its out-of-line
@@ -560,6 +578,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       fence_proxy_async_smem();
     }
+    if (warp == 0) M3_TRACE(iter, 14);
     tc_fence_before_sync();
     ticket = next;
     ++iter;

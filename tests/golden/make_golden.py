@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this folder from the reference implementation itself.
 
-Run from the repository root in a container where the reference checkout is present:
+Run from the repository root in a container where the reference checkout is present, giving its
+root directory (or set M3SSD_REFERENCE to it):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 ``lm_tiny.npz``: a two-layer reference ``Mamba3Transformer`` (models/transformer.py) on CPU, its
 parameters, logits, loss and parameter gradients for one batch (see ``make_lm_fixture``).
@@ -171,7 +172,9 @@ def make_proj_fixtures(only):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("M3SSD_REFERENCE"),
+                    required="M3SSD_REFERENCE" not in os.environ,
+                    help="root of the reference checkout (default: $M3SSD_REFERENCE)")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
