@@ -165,16 +165,24 @@ M3SSD_API int m3ssd_launch_count(const m3ssd_problem* prob, int backward);
 /* Forward that allocates nothing, for callers that cannot allocate device memory when they call
  * the operator (a serving runtime that plans all device memory up front and forbids allocation
  * on the request path, or code inside another framework's step with no allocator at hand).
- * No counterpart in the reference. Same arguments and results as m3ssd_fwd, but
- * `workspace`/`workspace_bytes` are ignored (may be NULL/0): the scratch this forward needs
- * (status word, ticket counter, one hand-off flag per chunk) is a fixed device array inside the
- * library, 131,328 bytes, held on every GPU that loads the library until exit.
+ * No counterpart in the reference. Same arguments and results as m3ssd_fwd, except for the
+ * workspace: the scratch this forward needs (status word, ticket counter, one hand-off flag per
+ * chunk) is a fixed device array inside the library, 131,328 bytes, held on every GPU that loads
+ * the library until exit.
+ *   - `workspace` may be NULL (workspace_bytes ignored). If it is not NULL it must hold at least
+ *     4 bytes (M3SSD_ERR_WORKSPACE) at a 4-byte aligned address (M3SSD_ERR_ALIGN): after the
+ *     forward the call copies the device status word there (cudaMemcpyAsync on `stream`), so it
+ *     reads as m3ssd_fwd's status word at offset 0 of its workspace. With NULL no status is
+ *     reported.
  *   - Only the tensor-core forward: head_dim = state_dim = 64, real x, B/C with a contiguous
  *     state dimension and 16-byte aligned strides; otherwise M3SSD_ERR_SHAPE. y and states must
- *     be 16-byte aligned (M3SSD_ERR_ALIGN).
+ *     be 16-byte aligned (M3SSD_ERR_ALIGN). It always runs the one-pass form: for few long
+ *     sequences (where m3ssd_fwd splits each sequence into chains) it is several times slower
+ *     than m3ssd_fwd, with the same results.
  *   - batch * nheads * ceil(seqlen / 64) must be <= 32768, otherwise M3SSD_ERR_SCRATCH_LIMIT.
  *   - The first call on a device looks up the array's device address (with that device
- *     current); make that first call before any stream capture.
+ *     current), and again after the device's context changed (cudaDeviceReset); make that first
+ *     call before any stream capture.
  *   - Every call uses the same array and leaves its contents behind; each call clears what must
  *     start at zero before its kernel runs. Calls that overlap on the GPU (other streams, other
  *     host threads) race on the array: serialise them.

@@ -162,19 +162,43 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
+// per device: the array's device address and the context it was looked up in
 void* g_static_scratch_addr[kMaxDevices] = {};
+void* g_static_scratch_ctx[kMaxDevices] = {};
 
-// Device address of g_static_scratch on the current device, looked up once per device with that
-// device current (the name is only a host-side stand-in for the device array).
+// The current context of the calling thread, through the driver entry point the runtime exposes
+// (the library does not link libcuda). nullptr if it cannot be queried.
+void* current_context() {
+  using GetCtx = int (*)(void**);
+  static GetCtx fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<GetCtx>(ptr);
+    return static_cast<GetCtx>(nullptr);
+  }();
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
+// Device address of g_static_scratch on the current device, looked up with that device current
+// (the name is only a host-side stand-in for the device array). The lookup is cached per device
+// and redone when the device's context has changed (cudaDeviceReset reloads the module, which
+// can move the array).
 int static_scratch_address(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return M3SSD_ERR_DEVICE;
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_static_mu);
-  if (!g_static_scratch_addr[dev]) {
+  if (!g_static_scratch_addr[dev] || ctx == nullptr || ctx != g_static_scratch_ctx[dev]) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr)
       return M3SSD_ERR_DEVICE;
     g_static_scratch_addr[dev] = ptr;
+    // the lookup has made the device's primary context current if none was
+    g_static_scratch_ctx[dev] = current_context();
   }
   *out = g_static_scratch_addr[dev];
   return M3SSD_OK;
@@ -381,11 +405,20 @@ int m3ssd_fwd_static_scratch(const m3ssd_fwd_args* a, void* stream) {
     return M3SSD_ERR_SCRATCH_LIMIT;
   rc = check_device();
   if (rc) return rc;
+  // an optional caller buffer receives the device status word (4 bytes) after the forward
+  if (a->workspace != nullptr && a->workspace_bytes < 4) return M3SSD_ERR_WORKSPACE;
+  if (!aligned(a->workspace, 4)) return M3SSD_ERR_ALIGN;
   void* scratch = nullptr;
   rc = static_scratch_address(&scratch);
   if (rc) return rc;
-  // run_fwd clears the status word, ticket counter and flags it uses before its kernel runs
-  return m3ssd::tc::run_fwd(p, a->y, a->states, scratch, static_cast<cudaStream_t>(stream));
+  const auto st = static_cast<cudaStream_t>(stream);
+  // run_fwd clears the status word, ticket counter and flags it uses before its kernel runs; it
+  // always runs the one-pass forward (the chained form needs more scratch than the array holds)
+  rc = m3ssd::tc::run_fwd(p, a->y, a->states, scratch, st);
+  if (rc != M3SSD_OK || a->workspace == nullptr) return rc;
+  return cudaMemcpyAsync(a->workspace, scratch, 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess
+             ? M3SSD_OK
+             : M3SSD_ERR_LAUNCH;
 }
 
 int m3ssd_fwd_proj(const m3ssd_proj_fwd_args* a, void* stream) {
