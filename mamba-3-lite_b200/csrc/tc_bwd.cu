@@ -314,7 +314,8 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
                                               const float2* rotrow, bool conj_out,
                                               uint32_t seg01, uint32_t seg23, int sub, int grp,
                                               uint32_t xop, uint64_t* colfree, int lane,
-                                              float2& acc_a, float2& acc_b) {
+                                              float2& acc_a, float2& acc_b, uint32_t it,
+                                              int tslot) {
   const int q4 = lane & 3, rr = lane >> 2;
   const float cj = conj_out ? -1.f : 1.f;
 #pragma unroll
@@ -323,6 +324,7 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
     tmem_ld16x256_x4(ta + ((uint32_t)(16 * half) << 16), a);
     tmem_ld16x256_x4(tb + ((uint32_t)(16 * half) << 16), bb);
     tmem_ld_wait();
+    if ((threadIdx.x >> 5) == 0) M3_TRACE(it, tslot + 2 * half);
     if (half == 1 && colfree != nullptr) warp_arrive(colfree, lane);
     const uint32_t row = (uint32_t)(16 * sub + 8 * half + rr);
     const float w = wrow[row];
@@ -361,6 +363,7 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
       acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
     }
     if (half == 0) acc_a = acc; else acc_b = acc;
+    if ((threadIdx.x >> 5) == 0) M3_TRACE(it, tslot + 2 * half + 1);
   }
 }
 
@@ -698,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  tmem + lane_off + COL_DCB + 32u * grp, rec.el, rec.cis, false,
                                  sb + OFF_H, sb + OFF_H + 16384u, sub, grp,
                                  sb + OFF_C + ((uint32_t)grp >> 1) * 16384u, &m.bar_colfree, lane,
-                                 acc_a, acc_b);
+                                 acc_a, acc_b, it, 32);
           if ((lane & 3) == 0) {
             m.rc[ph][grp][16 * sub + (lane >> 2)] = acc_a;
             m.rc[ph][grp][16 * sub + 8 + (lane >> 2)] = acc_b;
@@ -744,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  tmem + lane_off + COL_DBB + 32u * grp, rec.dec, rec.cis, true,
                                  sb + OFF_DYT, sb + OFF_DGM, sub, grp,
                                  sb + OFF_B + ((uint32_t)grp >> 1) * 16384u, nullptr, lane, acc_a,
-                                 acc_b);
+                                 acc_b, it, 36);
           if ((lane & 3) == 0) {  // conj: dB' conj(B')
             m.rb[ph][grp][16 * sub + (lane >> 2)] = make_float2(acc_a.x, -acc_a.y);
             m.rb[ph][grp][16 * sub + 8 + (lane >> 2)] = make_float2(acc_b.x, -acc_b.y);
@@ -786,7 +789,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                      xv);
         split8_store(sb + OFF_DY + swz(stack8(s, 0), tid & 7),
                      sb + OFF_DY + swz(stack8(s, 1), tid & 7), gv);
+        if (warp == 0) M3_TRACE(it, 44);
         if (it > 0) mbar_wait(&m.bar_stfree, ph ^ 1u, p.err, kErrMmaWait);
+        if (warp == 0) M3_TRACE(it, 45);
         const float e = rec.el[s];
         float w[8];
 #pragma unroll
@@ -835,6 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         workers_sync();
+        if (warp == 0) M3_TRACE(it, 46 + (tile == 1));
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const int j = tid + kWorkers * i;
@@ -927,15 +933,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16x256_x2(tl + COL_G, g);
           tmem_ld16x256_x2(tl + COL_DM, dm);
           tmem_ld_wait();
+          if (warp == 0) M3_TRACE(it, 40 + 2 * h);
           const int row = 16 * sub + 8 * h + rr;
-          const float rl = rec.rho[row];
+          const float rl = rec.rho2[row];
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
             const int s0 = 16 * grp + 8 * k + 2 * q4;
             float mr2[2], dg2[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float L = (s0 + e <= row) ? expf(rl - rec.rho[s0 + e]) : 0.f;
+              const float L = (s0 + e <= row) ? exp2f(rl - rec.rho2[s0 + e]) : 0.f;
               mr2[e] = L * (g[4 * k + e] + g[4 * k + 2 + e]);
               dg2[e] = L * (dm[4 * k + e] + dm[4 * k + 2 + e]);
             }
@@ -955,6 +962,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 0u), kc) + off, dgh);
             st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 1u), kc) + off, dgl);
           }
+          if (warp == 0) M3_TRACE(it, 41 + 2 * h);
         }
       }
       warp_arrive(&m.bar_ops2, lane);
@@ -1204,13 +1212,11 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
   }
   const size_t keep = clear_status ? 0 : 4;  // an earlier pass of the same call reported here
   if (cudaMemsetAsync(base + keep, 0, L.ring - keep, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = sm_count();
+  if (sms <= 0) return M3SSD_ERR_DEVICE;
   auto kern = out.planar ? (G > 1 ? k_bwd_tc<true, true> : k_bwd_tc<true, false>)
                          : (G > 1 ? k_bwd_tc<false, true> : k_bwd_tc<false, false>);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-      cudaSuccess)
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kSmemBytes))
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
   if (dhT != nullptr && dgam == nullptr)

@@ -402,7 +402,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // and backward kernels. Position l of chunk z is t = 64 z + l; Sigma_l = rho_l + i theta_l is the
 // within-chunk inclusive cumsum of a = softplus(dt) A (a = 0 for t >= T), Gamma = Sigma_63.
 struct ChunkRec {
-  float rho[64];   // Re Sigma_l
+  float rho2[64];  // Re Sigma_l in log2 units (rho_l log2(e)): exp(rho_l - rho_s) = exp2(rho2_l - rho2_s)
   float el[64];    // exp(rho_l)
   float dec[64];   // exp(rho_Gamma - rho_l)
   float sp[64];    // softplus(dt_t) (0 past T)
@@ -425,6 +425,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // accesses: after acquiring data another CTA wrote with plain stores, before bulk-copying it
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// 16-byte asynchronous copy global -> shared (L2 only), or 16 zero bytes when `valid` is false
+// (nothing is read then). Completion is waited for with cp_async_wait_all() by the same thread.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 // barrier among the first `count` threads of the CTA (ids 1..15; 0 is __syncthreads)
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {

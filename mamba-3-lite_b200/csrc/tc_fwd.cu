@@ -22,6 +22,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <string.h>
+
+#include <mutex>
 
 #include "m3ssd_common.cuh"
 #include "tc_common.cuh"
@@ -353,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- MMA batch 1b: G = C'x B'x^T (M128 N64); the commit covers S~ too
     if (tid == 0) {
       tc_fence_after_sync();
+      M3_TRACE(iter, 17);
       const uint32_t idG = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
       for (int hl = 0; hl < 2; ++hl)
@@ -400,8 +404,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       float v[32];
       tmem_ld32(tmem + lane_off + COL_G + 32u * wg, v);
       tmem_ld_wait();
+      if (warp == 0) M3_TRACE(iter, 19);
       float mr[16];
-      const float rl = m.rec.rho[r];
+      const float rl = m.rec.rho2[r];
       el_r = m.rec.el[r];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -409,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
         const float gsum = (part ? v[16 + c] : v[c]) + recv;
         const int s = 32 * wg + 16 * part + c;
-        mr[c] = (s <= r) ? expf(rl - m.rec.rho[s]) * gsum : 0.f;
+        mr[c] = (s <= r) ? exp2f(rl - m.rec.rho2[s]) * gsum : 0.f;
       }
       const uint32_t ch = 4u * wg + 2u * part;
       split_store16(sb + OFF_XT + swz(stack_row(r, 0), ch), sb + OFF_XT + swz(stack_row(r, 1), ch), mr);
@@ -454,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0) M3_TRACE(iter, 10);
     if (tid == 0) {  // Y1 = Mr x, Y2 = Re(C' H_z) as C'x conj(H)x
       tc_fence_after_sync();
+      M3_TRACE(iter, 18);
       const uint32_t idY1 = idesc_bf16(128, 64, 0, 1);
 #pragma unroll
       for (int hl = 0; hl < 2; ++hl)
@@ -463,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                       sdesc(sb + (hl ? OFF_XL : OFF_XH) + j * 2048u, 8192, 1024), idY1,
                       (hl | j) != 0);
       mma_commit(&m.bar_mma2);
+      M3_TRACE(iter, 20);
       const uint32_t idY2 = idesc_bf16(128, 64, 0, 0);
 #pragma unroll
       for (int hl = 0; hl < 2; ++hl)
@@ -631,9 +638,102 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-static bool encode_bc_map_impl(CUtensorMap* map, const void* ptr, const Problem& p, const long long st[4]) {
+// Host-side caches of what every call would otherwise redo: encoded tensor maps (a map depends only
+// on its address, shape, strides, box and modes, not on the memory's contents or lifetime), the SM
+// count and the dynamic shared memory attribute of each kernel, per device. One mutex guards all;
+// each lookup is a short linear scan.
+namespace {
+struct MapKey {
+  CUtensorMapDataType dtype;
+  CUtensorMapSwizzle swizzle;
+  CUtensorMapL2promotion l2;
+  const void* ptr;
+  cuuint64_t dims[4];
+  cuuint64_t strides[3];
+  cuuint32_t box[4];
+};
+struct MapEntry {
+  bool used;
+  MapKey key;
+  CUtensorMap map;
+};
+constexpr int kMapCache = 64;
+constexpr int kMaxDev = 64;
+std::mutex g_cache_mu;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+int g_sms[kMaxDev] = {};
+struct AttrEntry {
+  const void* func;
+  int dev;
+  int bytes;
+};
+AttrEntry g_attrs[64];
+int g_nattrs = 0;
+
+// cuTensorMapEncodeTiled of a 4-D map (element strides 1, no interleave, no out-of-bounds NaN
+// fill), served from the cache when the same map was encoded before
+bool encode4(CUtensorMap* map, CUtensorMapDataType dtype, const void* ptr,
+             const cuuint64_t dims[4], const cuuint64_t strides[3], const cuuint32_t box[4],
+             CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2) {
+  MapKey k;
+  memset(&k, 0, sizeof(k));  // padding takes part in the comparison
+  k.dtype = dtype;
+  k.swizzle = swizzle;
+  k.l2 = l2;
+  k.ptr = ptr;
+  memcpy(k.dims, dims, sizeof(k.dims));
+  memcpy(k.strides, strides, sizeof(k.strides));
+  memcpy(k.box, box, sizeof(k.box));
+  std::lock_guard<std::mutex> lock(g_cache_mu);
+  for (int i = 0; i < kMapCache; ++i)
+    if (g_maps[i].used && memcmp(&g_maps[i].key, &k, sizeof(k)) == 0) {
+      *map = g_maps[i].map;
+      return true;
+    }
   const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   if (!encode) return false;
+  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  const CUresult rc = encode(map, dtype, 4, const_cast<void*>(ptr), dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) return false;
+  MapEntry& e = g_maps[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  e.used = true;
+  e.key = k;
+  e.map = *map;
+  return true;
+}
+}  // namespace
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  std::lock_guard<std::mutex> lock(g_cache_mu);
+  if (g_sms[dev] == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return 0;
+    g_sms[dev] = sms;
+  }
+  return g_sms[dev];
+}
+
+bool ensure_smem_attr(const void* func, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(g_cache_mu);
+  for (int i = 0; i < g_nattrs; ++i)
+    if (g_attrs[i].func == func && g_attrs[i].dev == dev && g_attrs[i].bytes >= bytes) return true;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return false;
+  if (g_nattrs < 64) g_attrs[g_nattrs++] = AttrEntry{func, dev, bytes};
+  return true;
+}
+
+static bool encode_bc_map_impl(CUtensorMap* map, const void* ptr, const Problem& p, const long long st[4]) {
   // interleaved: (B, T, H, 2N floats), box 64 steps x 2N floats of one head.
   // planar: (B, T, 2H, N floats) where row h is Re of head h and row H + h its Im (Im follows
   // Re by H*N floats in the in_proj layout), box 64 steps x N floats.
@@ -644,12 +744,8 @@ static bool encode_bc_map_impl(CUtensorMap* map, const void* ptr, const Problem&
   cuuint64_t strides[3] = {(cuuint64_t)st[2] * esz, (cuuint64_t)st[1] * esz,
                            (cuuint64_t)st[0] * esz};
   cuuint32_t box[4] = {pl ? 64u : 128u, 1u, 64u, 1u};
-  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
-  const CUresult rc = encode(
-      map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), dims, strides, box, es,
-      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return rc == CUDA_SUCCESS;
+  return encode4(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ptr, dims, strides, box,
+                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
 bool encode_bc_tensor_map(CUtensorMap* map, const void* ptr, const Problem& p,
@@ -663,32 +759,24 @@ bool encode_out_tensor_map(CUtensorMap* map, void* ptr, const Problem& p, int ro
 }
 
 bool encode_out_map_bf16(CUtensorMap* map, void* ptr, const Problem& p) {
-  const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
-  if (!encode || (reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
   cuuint64_t dims[4] = {64u, (cuuint64_t)p.H, (cuuint64_t)p.T, (cuuint64_t)p.Bsz};
   cuuint64_t strides[3] = {128u, 128u * (cuuint64_t)p.H, 128u * (cuuint64_t)p.H * (cuuint64_t)p.T};
   cuuint32_t box[4] = {64u, 1u, 64u, 1u};
-  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
-  const CUresult rc = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, ptr, dims, strides, box, es,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return rc == CUDA_SUCCESS;
+  return encode4(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ptr, dims, strides, box,
+                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
 }
 
 bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int row_floats,
                             int rows, long long s_row, long long s_t, long long s_b) {
-  const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
-  if (!encode || (reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
   if (s_row <= 0 || s_t <= 0 || s_b <= 0 || s_row % 4 || s_t % 4 || s_b % 4) return false;
   cuuint64_t dims[4] = {(cuuint64_t)row_floats, (cuuint64_t)rows, (cuuint64_t)p.T,
                         (cuuint64_t)p.Bsz};
   cuuint64_t strides[3] = {(cuuint64_t)s_row * 4u, (cuuint64_t)s_t * 4u, (cuuint64_t)s_b * 4u};
   cuuint32_t box[4] = {32u, 1u, 64u, 1u};
-  cuuint32_t es[4] = {1u, 1u, 1u, 1u};
-  const CUresult rc = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, es,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return rc == CUDA_SUCCESS;
+  return encode4(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ptr, dims, strides, box,
+                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
 }
 
 bool fwd_supported(const Problem& p) {
@@ -746,13 +834,11 @@ int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, 
     const int rc = run_chunk_prep(p, recs, st);
     if (rc != M3SSD_OK) return rc;
   }
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = sm_count();
+  if (sms <= 0) return M3SSD_ERR_DEVICE;
   auto kern = p.bc_planar ? (G > 1 ? k_fwd_tc<true, true> : k_fwd_tc<true, false>)
                           : (G > 1 ? k_fwd_tc<false, true> : k_fwd_tc<false, false>);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-      cudaSuccess)
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kSmemBytes))
     return M3SSD_ERR_LAUNCH;
   const int grid = fp.total < 2 * sms ? fp.total : 2 * sms;
   kern<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmY, fp);

@@ -453,8 +453,8 @@ int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], con
       reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
   const CarryPassArgs ca = carry_pass_args(p, dy, dys, recs, G);
   if (carry_tiled_ok(p, dy, dys)) {
-    if (cudaFuncSetAttribute(k_chain_bwd_pass1_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kCarryTiledSmem) != cudaSuccess)
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(k_chain_bwd_pass1_tiled),
+                          (int)kCarryTiledSmem))
       return M3SSD_ERR_LAUNCH;
     k_chain_bwd_pass1_tiled<<<p.Bsz * p.H * G, 256, kCarryTiledSmem, st>>>(ca, P);
   } else {

@@ -47,6 +47,11 @@ bool encode_out_map_bf16(CUtensorMap* map, void* ptr, const Problem& p);
 bool encode_out_map_strided(CUtensorMap* map, void* ptr, const Problem& p, int row_floats,
                             int rows, long long s_row, long long s_t, long long s_b);
 
+// SM count of the current device (0 if it cannot be queried), cached per device
+int sm_count();
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes) once per kernel and device
+bool ensure_smem_attr(const void* func, int bytes);
+
 // head_dim = state_dim = 64, real x, B/C with contiguous state dim and 16-byte aligned strides
 bool fwd_supported(const Problem& p);
 size_t fwd_workspace_bytes(const Problem& p);

@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(128) k_chunk_prep(const float2* __restrict__ A
   ChunkRec* r = out + rec;
   float sn, cs;
   sincosf(a.y, &sn, &cs);
-  r->rho[l] = a.x;
+  r->rho2[l] = a.x * 1.4426950408889634f;  // log2(e)
   r->el[l] = expf(a.x);
   r->dec[l] = expf(gam[half].x - a.x);
   r->sp[l] = sp;

@@ -12,7 +12,7 @@
 
 namespace m3ssd {
 namespace tc {
-constexpr int kTraceCtas = 16, kTraceIters = 64, kTraceSlots = 32;
+constexpr int kTraceCtas = 16, kTraceIters = 64, kTraceSlots = 48;
 }  // namespace tc
 }  // namespace m3ssd
 
