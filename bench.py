@@ -624,6 +624,38 @@ def run_proj_workload(args):
     return 0
 
 
+def run_trace_workload(args):
+    """Per-phase timeline of k_fwd_tc and k_bwd_tc at the block shape, from the measurement build
+    (build.py --trace): median microseconds after a chunk ticket's start for every phase boundary.
+    Timings of a trace build run slower than the default library's; read the shares."""
+    import torch
+    import m3ssd
+    from m3ssd import trace
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m3ssd.load()
+    B, T, H, D, N = args.batch, SHAPE["T"], SHAPE["H"], SHAPE["D"], SHAPE["N"]
+    d = make_inputs(dev, 1000, B, T, H, D, N)
+
+    def step():
+        xs = [d[k].detach().requires_grad_(True) for k in ("x", "A", "B_t", "C_t", "dt")]
+        y = m3ssd.ssd_complex_chunkwise(*xs, chunk_size=CHUNK)
+        y.backward(d["dy"])
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    fwd, bwd = trace.capture(step, dev, warmup=args.warmup)
+    clocks = sampler.stop()
+    mhz = clocks.get("sm_mhz") or 1965.0
+    line = {"workload": f"phase trace, B{B} L{T} H{H} D{D} N{N}, trace build",
+            "clocks": clocks,
+            "k_fwd_tc": trace.summarize(fwd, trace.FWD_PHASES, mhz),
+            "k_bwd_tc": trace.summarize(bwd, trace.BWD_PHASES, mhz)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -645,11 +677,12 @@ def main():
                     help="micro-batch per GPU of the whole-model step")
     ap.add_argument("--no-secondary", action="store_true",
                     help="default workload: skip the long / sharded / model keys")
-    ap.add_argument("--workload", choices=["op", "proj", "long", "model"], default="op",
+    ap.add_argument("--workload", choices=["op", "proj", "long", "model", "trace"], default="op",
                     help="op: the operator on unpacked inputs (default); proj: the block's SSD "
                          "input path from its in_proj output, fused vs composed; long: one "
                          "GPU's share of B4 L16384 H16 (few long sequences); model: the whole "
-                         "28-layer model's data-parallel train step")
+                         "28-layer model's data-parallel train step; trace: per-phase "
+                         "timeline of the tensor-core kernels (needs build.py --trace)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -661,6 +694,8 @@ def main():
         return run_long_workload(args)
     if args.workload == "model":
         return run_model_workload(args)
+    if args.workload == "trace":
+        return run_trace_workload(args)
 
     import torch
     import torch.distributed as dist
@@ -858,6 +893,37 @@ def main():
                     "unit": UNIT, "heads_per_gpu": r["heads_per_gpu"],
                     "roofline_frac_per_gpu": r["frac_per_gpu"]}
         guarded("sharded", sharded_key)
+
+        def complex_key():
+            # complex x (the reference tests' input type) at the block shape, same GPU
+            dc = make_inputs(dev, 5000 + rank, B, T, H, D, N)
+            xc = torch.complex(dc["x"], torch.randn_like(dc["x"]))
+
+            def cstep():
+                xs = [xc.detach().requires_grad_(True)] + [
+                    dc[k].detach().requires_grad_(True) for k in ("A", "B_t", "C_t", "dt")]
+                y = m3ssd.ssd_complex_chunkwise(*xs, chunk_size=CHUNK, precision=args.precision)
+                y.backward(dc["dy"])
+
+            for _ in range(3):
+                cstep()
+            torch.cuda.synchronize()
+            c0 = torch.cuda.Event(enable_timing=True)
+            c1 = torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            for _ in range(10):
+                cstep()
+            c1.record(stream)
+            torch.cuda.synchronize()
+            (cms,) = mdist.max_over_ranks([c0.elapsed_time(c1) / 10], device=dev)
+            del dc, xc
+            return {"what": "complex64 x (as in the reference's tests), fwd+bwd at the block "
+                            "shape: two passes of the real-x tensor-core kernels",
+                    "path": m3ssd.implementation((B, T, H, D), N, CHUNK, complex_x=True,
+                                                 precision=args.precision)[0],
+                    "ms_per_step": cms, "value": world * B * T / (cms / 1e3) / 1e6,
+                    "unit": UNIT, "ratio_to_real_x_step": cms / (ms / args.steps)}
+        guarded("complex_x", complex_key)
 
         def model_key():
             r = measure_model(args, dev, rank, world, args.model_layers, 5, 3, 2, clocks=False)

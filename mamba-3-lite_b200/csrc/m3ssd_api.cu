@@ -52,11 +52,17 @@ int check_problem(const m3ssd_problem* pr) {
 
 // Problems the tensor-core path can take (by shape and precision) are blocked at 64 positions
 // whichever path runs, so `states` written by either forward path is read correctly by either
-// backward path. The result does not depend on the blocking.
+// backward path. The result does not depend on the blocking. Complex x runs as two real-x passes
+// (tc_complex.cu).
 bool tc_shape(const m3ssd_problem* pr) {
   const uint32_t prec = pr->flags & M3SSD_PREC_MASK;
-  return pr->headdim == 64 && pr->dstate == 64 && !(pr->flags & M3SSD_X_COMPLEX) &&
-         prec != M3SSD_PREC_FP32;
+  return pr->headdim == 64 && pr->dstate == 64 && prec != M3SSD_PREC_FP32;
+}
+
+// whether the tensor-core kernels take this problem's operands (B / C through TMA); complex x is
+// judged on the real-x view of its passes
+bool tc_supported(const Problem& p) {
+  return m3ssd::tc::fwd_supported(p.x_complex ? m3ssd::tc::real_part_view(p, 0) : p);
 }
 
 Problem make_problem(const m3ssd_problem* pr) {
@@ -82,7 +88,9 @@ Problem make_problem(const m3ssd_problem* pr) {
 // adds the chained-pass buffers when the shape runs as several chains per sequence.
 size_t bwd_ws(const m3ssd_problem* pr, const Problem& p) {
   size_t a = m3ssd::simt::bwd_workspace_bytes(p), b = m3ssd::tc::bwd_workspace_bytes(p);
-  if (tc_shape(pr)) {
+  if (tc_shape(pr) && p.x_complex) {
+    b = m3ssd::tc::complex_bwd_workspace_bytes(p);
+  } else if (tc_shape(pr)) {
     const int G = m3ssd::tc::chains_for(p, true);
     if (G > 1) b = m3ssd::tc::bwd_chains_workspace_bytes(p, G);
   }
@@ -229,7 +237,7 @@ int proj_problem(const m3ssd_problem* pr, const float* proj, const int64_t ps[2]
                  Problem* out) {
   int rc = check_problem(pr);
   if (rc) return rc;
-  if (!tc_shape(pr)) return M3SSD_ERR_SHAPE;
+  if (!tc_shape(pr) || (pr->flags & M3SSD_X_COMPLEX)) return M3SSD_ERR_SHAPE;
   if (!proj || !A) return M3SSD_ERR_NULL;
   if (ps[0] <= 0 || ps[1] <= 0) return M3SSD_ERR_SHAPE;
   const ProjCols c = proj_cols(*pr);
@@ -290,7 +298,9 @@ size_t m3ssd_states_bytes(const m3ssd_problem* prob) {
   if (check_problem(prob) != M3SSD_OK) return 0;
   const Problem p = make_problem(prob);
   const size_t a = m3ssd::simt::states_bytes(p);
-  const size_t b = tc_shape(prob) ? m3ssd::tc::states_bytes(p) : 0;
+  const size_t b = !tc_shape(prob) ? 0
+                   : p.x_complex   ? m3ssd::tc::complex_states_bytes(p)
+                                   : m3ssd::tc::states_bytes(p);
   return a > b ? a : b;
 }
 
@@ -317,6 +327,10 @@ const char* m3ssd_bwd_path(const m3ssd_problem* prob) {
 int m3ssd_launch_count(const m3ssd_problem* prob, int backward) {
   if (check_problem(prob) != M3SSD_OK) return 0;
   if (!tc_shape(prob)) return backward ? m3ssd::simt::kBwdLaunches : m3ssd::simt::kFwdLaunches;
+  // complex x: two passes of the real-x kernels (the forward's records once), and the backward's
+  // dx interleave
+  if (prob->flags & M3SSD_X_COMPLEX)
+    return backward ? 2 * m3ssd::tc::kBwdLaunches + 1 : 2 * m3ssd::tc::kFwdLaunches - 1;
   // the chained forms: forward two passes (the records once) plus the segment chain; backward the
   // carry pass, the segment chain, the segments' end-state terms and the tensor-core pass
   const bool chained = m3ssd::tc::chains_for(make_problem(prob), backward != 0) > 1;
@@ -339,9 +353,12 @@ int m3ssd_fwd(const m3ssd_fwd_args* a, void* stream) {
   if (!aligned(a->workspace, 256)) return M3SSD_ERR_ALIGN;
   rc = check_device();
   if (rc) return rc;
-  if (tc_shape(&a->prob) && m3ssd::tc::fwd_supported(p)) {
+  if (tc_shape(&a->prob) && tc_supported(p)) {
     // y leaves the tensor-core forward through TMA stores
     if (!aligned(a->y, 16)) return M3SSD_ERR_ALIGN;
+    if (p.x_complex)
+      return m3ssd::tc::run_fwd_complex(p, a->y, a->states, a->workspace,
+                                        static_cast<cudaStream_t>(stream));
     return tc_fwd(p, a->y, a->states, a->workspace, stream, nullptr, nullptr);
   }
   if (p.y_bf16) return M3SSD_ERR_SHAPE;  // B / C strides the tensor-core path cannot take
@@ -373,9 +390,14 @@ int m3ssd_bwd(const m3ssd_bwd_args* a, void* stream) {
   for (int i = 0; i < 4; ++i) dys[i] = a->dy_strides[i];
   // the tensor-core backward reads the forward's private state layout and writes dx, dB, dC
   // with TMA stores: 16-byte aligned outputs
-  if (tc_shape(&a->prob) && m3ssd::tc::bwd_supported(p)) {
+  if (tc_shape(&a->prob) && tc_supported(p)) {
     if (!aligned(a->dx, 16) || !aligned(a->dB, 16) || !aligned(a->dC, 16))
       return M3SSD_ERR_ALIGN;
+    if (p.x_complex)
+      return m3ssd::tc::run_bwd_complex(
+          p, a->dy, dys, a->states, static_cast<float2*>(a->dx), static_cast<float2*>(a->dA),
+          static_cast<float2*>(a->dB), static_cast<float2*>(a->dC), a->ddt, a->workspace,
+          static_cast<cudaStream_t>(stream));
     const m3ssd::tc::BwdOut out = m3ssd::tc::contiguous_bwd_out(
         p, static_cast<float*>(a->dx), static_cast<float2*>(a->dA), static_cast<float2*>(a->dB),
         static_cast<float2*>(a->dC), a->ddt);
@@ -472,7 +494,9 @@ int m3ssd_fwd_state(const m3ssd_fwd_args* a, const void* h0, void* hT, void* str
   if (!a) return M3SSD_ERR_NULL;
   int rc = check_problem(&a->prob);
   if (rc) return rc;
-  if (!tc_shape(&a->prob) || a->prob.seqlen % m3ssd::tc::kChunk) return M3SSD_ERR_SHAPE;
+  if (!tc_shape(&a->prob) || (a->prob.flags & M3SSD_X_COMPLEX) ||
+      a->prob.seqlen % m3ssd::tc::kChunk)
+    return M3SSD_ERR_SHAPE;
   Problem p = make_problem(&a->prob);
   rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
                    a->dt_strides);
@@ -494,7 +518,9 @@ int m3ssd_bwd_state(const m3ssd_bwd_args* a, const void* hT, const void* dhT, vo
   if (!a) return M3SSD_ERR_NULL;
   int rc = check_problem(&a->prob);
   if (rc) return rc;
-  if (!tc_shape(&a->prob) || a->prob.seqlen % m3ssd::tc::kChunk) return M3SSD_ERR_SHAPE;
+  if (!tc_shape(&a->prob) || (a->prob.flags & M3SSD_X_COMPLEX) ||
+      a->prob.seqlen % m3ssd::tc::kChunk)
+    return M3SSD_ERR_SHAPE;
   Problem p = make_problem(&a->prob);
   rc = fill_inputs(p, a->x, a->x_strides, a->A, a->B, a->b_strides, a->C, a->c_strides, a->dt,
                    a->dt_strides);

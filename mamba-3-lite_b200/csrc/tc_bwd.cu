@@ -118,6 +118,11 @@ struct BwdParams {
   float2* dh0;
   const float2* dgam_last;
   int G, seg;  // chains per sequence and chunks per chain (see TicketPos)
+  // the complex-x second pass (see run_bwd_complex): C is multiplied by crot as it is read (dC then
+  // takes conj(crot) of its gradient), and dB, dC, ddt and the dA partials are added to what the
+  // first pass left (accum)
+  float2 crot;
+  int accum;
 };
 
 // (sequence, chunk) of a ticket: tickets run over sequences (then segments) fastest, chunks
@@ -214,11 +219,11 @@ static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const fl
 // (row h of the map) and 2, 3 the imaginary parts (row hp + h).
 static __device__ __noinline__ void ctl_store_tile(const CUtensorMap* map, uint8_t* smem,
                                                    uint32_t off01, uint32_t off23, int nseg,
-                                                   TicketPos q, int hp) {
+                                                   TicketPos q, int hp, bool accum) {
   for (int seg = 0; seg < nseg; ++seg)
-    tma_store_4d(map, smem + (seg < 2 ? off01 : off23) + (seg & 1) * 8192,
-                 hp > 0 ? 32 * (seg & 1) : 32 * seg, hp > 0 ? q.h + hp * (seg >> 1) : q.h,
-                 q.z * 64, q.b);
+    tma_put_4d(map, smem + (seg < 2 ? off01 : off23) + (seg & 1) * 8192,
+               hp > 0 ? 32 * (seg & 1) : 32 * seg, hp > 0 ? q.h + hp * (seg >> 1) : q.h,
+               q.z * 64, q.b, accum);
   bulk_commit_group();
 }
 
@@ -315,7 +320,7 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
                                               uint32_t seg01, uint32_t seg23, int sub, int grp,
                                               uint32_t xop, uint64_t* colfree, int lane,
                                               float2& acc_a, float2& acc_b, uint32_t it,
-                                              int tslot) {
+                                              int tslot, float2 extra) {
   const int q4 = lane & 3, rr = lane >> 2;
   const float cj = conj_out ? -1.f : 1.f;
 #pragma unroll
@@ -328,7 +333,7 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
     if (half == 1 && colfree != nullptr) warp_arrive(colfree, lane);
     const uint32_t row = (uint32_t)(16 * sub + 8 * half + rr);
     const float w = wrow[row];
-    const float2 rot = rotrow[row];
+    const float2 rot = cmul2(rotrow[row], extra);
     const float2 nr = make_float2(rot.x, -rot.y);
     const uint32_t xrow = stack8(row, 0u);  // its lo part is 8 stacked rows (1024 bytes) on
     float2 acc = make_float2(0.f, 0.f);
@@ -483,8 +488,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int l = lane + 32 * u, t = t0 + l;
           const float2 da = u ? s1 : s0;
           if (t < p.T) {
-            p.ddt[q.b * p.ddt_sb + (long long)t * p.ddt_st + q.h] =
-                (da.x * Ah.x + da.y * Ah.y) * rec.dsp[l];
+            float* dst = p.ddt + q.b * p.ddt_sb + (long long)t * p.ddt_st + q.h;
+            const float v = (da.x * Ah.x + da.y * Ah.y) * rec.dsp[l];
+            *dst = p.accum ? *dst + v : v;
             dap[u] = make_float2(da.x * rec.sp[l], da.y * rec.sp[l]);
           }
 #pragma unroll
@@ -622,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // has read it
         mbar_wait(&m.bar_dc, ph, p.err, kErrMmaWait);
         M3_TRACE(it, 28);
-        ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc, p.hp);
+        ctl_store_tile(&tmDC, smem, OFF_H, OFF_H + 16384u, 4, qc, p.hp, p.accum != 0);
         if (nxt < p.total) {
           mbar_wait(&m.bar4, ph, p.err, kErrMmaWait);
           ctl_load_c(&tmC, smem, &m, p.recs, p.nc, qn, (int)((it + 1) & 1), p.hp);
@@ -632,10 +638,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // dx from sDGK, dB from sDYT / sDGM; the next B tile (the epilogue of dB has read sB) and
         // the next dS (dBb has read sDS)
         mbar_wait(&m.bar_dx, ph, p.err, kErrMmaWait);
-        ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc, 0);
+        ctl_store_tile(&tmDX, smem, OFF_DGK, OFF_DGK, 2, qc, 0, false);
         mbar_wait(&m.bar_db, ph, p.err, kErrMmaWait);
         M3_TRACE(it, 29);
-        ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc, p.hp);
+        ctl_store_tile(&tmDB, smem, OFF_DYT, OFF_DGM, 4, qc, p.hp, p.accum != 0);
         if (nxt < p.total) ctl_load_b(&tmB, smem, &m, qn, p.hp);
         bulk_wait_read_all();
         mbar_arrive(&m.bar_stfree);
@@ -701,7 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  tmem + lane_off + COL_DCB + 32u * grp, rec.el, rec.cis, false,
                                  sb + OFF_H, sb + OFF_H + 16384u, sub, grp,
                                  sb + OFF_C + ((uint32_t)grp >> 1) * 16384u, &m.bar_colfree, lane,
-                                 acc_a, acc_b, it, 32);
+                                 acc_a, acc_b, it, 32, p.crot);
           if ((lane & 3) == 0) {
             m.rc[ph][grp][16 * sub + (lane >> 2)] = acc_a;
             m.rc[ph][grp][16 * sub + 8 + (lane >> 2)] = acc_b;
@@ -747,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  tmem + lane_off + COL_DBB + 32u * grp, rec.dec, rec.cis, true,
                                  sb + OFF_DYT, sb + OFF_DGM, sub, grp,
                                  sb + OFF_B + ((uint32_t)grp >> 1) * 16384u, nullptr, lane, acc_a,
-                                 acc_b, it, 36);
+                                 acc_b, it, 36, make_float2(1.f, 0.f));
           if ((lane & 3) == 0) {  // conj: dB' conj(B')
             m.rb[ph][grp][16 * sub + (lane >> 2)] = make_float2(acc_a.x, -acc_a.y);
             m.rb[ph][grp][16 * sub + 8 + (lane >> 2)] = make_float2(acc_b.x, -acc_b.y);
@@ -849,7 +855,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      : 16u * (((uint32_t)f >> 5) & 3u) + ((uint32_t)f & 15u);
           const uint32_t qq = stacked ? (uint32_t)j & 15u
                                       : 8u * ((uint32_t)f >> 7) + 4u * (((uint32_t)f >> 4) & 1u) + k;
-          const float2 cs = stacked ? rec.cis[l] : make_float2(1.f, 0.f);
+          const float2 cs = !stacked ? make_float2(1.f, 0.f)
+                            : tile == 0 ? cmul2(rec.cis[l], p.crot) : rec.cis[l];
           const float rv[8] = {r4[i][0].x, r4[i][0].y, r4[i][0].z, r4[i][0].w,
                                r4[i][1].x, r4[i][1].y, r4[i][1].z, r4[i][1].w};
           float v[8];
@@ -1041,7 +1048,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // dA[h] = sum over batch and chunks of the per-chunk partials: one CTA per head, fixed-order
 // strided partial sums and a fixed tree, so the result is deterministic.
 __global__ void __launch_bounds__(256) k_bwd_tc_dA(const float2* __restrict__ dapart, int Bsz,
-                                                   int H, int nc, float2* __restrict__ dA) {
+                                                   int H, int nc, float2* __restrict__ dA,
+                                                   int accum) {
   __shared__ float2 red[256];
   const int h = blockIdx.x;
   const int n = Bsz * nc;
@@ -1061,7 +1069,10 @@ __global__ void __launch_bounds__(256) k_bwd_tc_dA(const float2* __restrict__ da
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) dA[h] = red[0];
+  if (threadIdx.x == 0) {
+    const float2 prev = accum ? dA[h] : make_float2(0.f, 0.f);
+    dA[h] = make_float2(prev.x + red[0].x, prev.y + red[0].y);
+  }
 }
 
 // <dS_{nc-1}, conj(H_{nc})> of a sequence with a final-state gradient: the d Sigma term the last
@@ -1139,7 +1150,8 @@ BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, f
 
 int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
             const BwdOut& out, void* ws, cudaStream_t st, const void* hT, const void* dhT,
-            void* dh0, int G, const void* dgam, bool clear_status) {
+            void* dh0, int G, const void* dgam, bool clear_status, const void* recs_in,
+            float2 crot, bool accum) {
   const BwdLayout L = bwd_layout(p, G);
   BwdParams bp{};
   bp.Bsz = p.Bsz;
@@ -1173,7 +1185,12 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
     bp.cs[i] = p.cs[i];
   }
   bp.states = static_cast<const float*>(states);
-  bp.recs = reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
+  bp.recs = recs_in != nullptr
+                ? static_cast<const ChunkRec*>(recs_in)
+                : reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) +
+                                                    states_h_bytes(p));
+  bp.crot = crot;
+  bp.accum = accum ? 1 : 0;
   bp.ddt = out.ddt;
   // planar B / C in and planar dB / dC out go together (the in_proj entry points)
   if ((out.planar != 0) != (p.bc_planar != 0)) return M3SSD_ERR_SHAPE;
@@ -1223,7 +1240,7 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
     k_bwd_tc_dgam_last<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float2*>(hT),
                                                     bp.dhT, reinterpret_cast<float2*>(base + L.dglast));
   kern<<<grid, kThreads, kSmemBytes, st>>>(tmB, tmC, tmDX, tmDB, tmDC, bp);
-  k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, out.dA);
+  k_bwd_tc_dA<<<p.H, 256, 0, st>>>(bp.dapart, p.Bsz, p.H, bp.nc, out.dA, bp.accum);
   return cudaGetLastError() == cudaSuccess ? M3SSD_OK : M3SSD_ERR_LAUNCH;
 }
 

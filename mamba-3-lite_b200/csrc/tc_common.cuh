@@ -121,6 +121,23 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+// the same as a reduction: the tile is added (f32 add) to what global memory holds
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1, int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+// store (accumulate = false) or add (true) a tile
+__device__ __forceinline__ void tma_put_4d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                           int c2, int c3, bool accumulate) {
+  if (accumulate)
+    tma_reduce_add_4d(map, src, c0, c1, c2, c3);
+  else
+    tma_store_4d(map, src, c0, c1, c2, c3);
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -84,6 +84,11 @@ struct FwdParams {
   // segments: each sequence's chunks run as G chains of seg = nc / G chunks (G = 1: one chain).
   // A chain starts from h0 (per (sequence, segment), or zero) and its end state goes to hT.
   int G, seg;
+  // complex x runs as two real passes (x = xr + i xi: y = F(xr; C) + F(xi; i C)): the factor C is
+  // multiplied by as it is read (1, or i in the second pass), and whether y is added to what the
+  // first pass stored (TMA reduce-add) instead of stored
+  float2 crot;
+  int y_accum;
 };
 
 // (chunk, sequence, segment) of a ticket: chunk-within-segment major, so every chain's first
@@ -231,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     int next = 0;     // grabbed late in this ticket so the window of open tickets stays small
     if (ctrl) {
       if (iter > 0) {  // the previous ticket's y: two 32-column fp32 segments (one bf16) from sXT
-        tma_store_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb);
-        if (!p.y_bf16) tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
+        tma_put_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb, p.y_accum != 0);
+        if (!p.y_bf16) tma_put_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb, p.y_accum != 0);
         bulk_commit_group();
       }
       yb = b;
@@ -274,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int it = 0; it < 4; ++it) {
         const int j = tid + kThreads * it;
         const int l = j >> 4, q = j & 15;
-        const float2 cs = m.rec.cis[l];
+        const float2 cs = tile == 0 ? cmulf(m.rec.cis[l], p.crot) : m.rec.cis[l];
         const uint32_t ka = (uint32_t)q >> 3, ch = (uint32_t)q & 7u;
         const float rv[8] = {r4[it][0].x, r4[it][0].y, r4[it][0].z, r4[it][0].w,
                              r4[it][1].x, r4[it][1].y, r4[it][1].z, r4[it][1].w};
@@ -593,8 +598,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (ctrl) {
     if (iter > 0) {  // the last ticket's y
-      tma_store_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb);
-      if (!p.y_bf16) tma_store_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb);
+      tma_put_4d(&tmY, smem + OFF_XT, 0, yh, yt0, yb, p.y_accum != 0);
+      if (!p.y_bf16) tma_put_4d(&tmY, smem + OFF_XT + 8192, 32, yh, yt0, yb, p.y_accum != 0);
       bulk_commit_group();
     }
     bulk_wait_all();
@@ -794,7 +799,8 @@ size_t fwd_workspace_bytes(const Problem& p) {
 }
 
 int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, const void* h0,
-            void* hT, int G, bool prep, bool clear_status) {
+            void* hT, int G, bool prep, bool clear_status, const void* recs_in, float2 crot,
+            bool y_accum) {
   FwdParams fp{};
   fp.Bsz = p.Bsz;
   fp.T = p.T;
@@ -808,8 +814,13 @@ int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, 
                  ? 1
                  : 0;
   fp.states = static_cast<float*>(states);
-  ChunkRec* recs = reinterpret_cast<ChunkRec*>(static_cast<char*>(states) + states_h_bytes(p));
+  ChunkRec* recs = recs_in != nullptr
+                      ? static_cast<ChunkRec*>(const_cast<void*>(recs_in))
+                      : reinterpret_cast<ChunkRec*>(static_cast<char*>(states) + states_h_bytes(p));
   fp.recs = recs;
+  fp.crot = crot;
+  fp.y_accum = y_accum ? 1 : 0;
+  if (y_accum && p.y_bf16) return M3SSD_ERR_SHAPE;  // y accumulates in fp32 only
   uint32_t* w = static_cast<uint32_t*>(ws);
   fp.err = w;
   fp.counter = w + 1;

@@ -388,6 +388,7 @@ CarryPassArgs carry_pass_args(const Problem& p, const void* dy, const long long 
 // work-bound; B4 L16384 with 2 or 16 heads: chain-bound). The chained form runs two passes over
 // chains of nc / G chunks plus the segment chain. G = 1 unless chains are clearly faster.
 int chains_for(const Problem& p, bool backward) {
+  if (p.x_complex) return 1;  // complex x runs as two one-pass real passes (tc_complex.cu)
   const int nc = (p.T + 63) / 64;
   const double bh = (double)p.Bsz * p.H;
   const double ticket = backward ? 0.070 : 0.039, hop = backward ? 5.2 : 4.3;

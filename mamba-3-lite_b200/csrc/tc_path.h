@@ -60,9 +60,13 @@ size_t fwd_workspace_bytes(const Problem& p);
 // h0 / hT then hold one state per (sequence, segment) ((b * H + h) * G + segment). `prep` = false
 // reuses the chunk records a previous call left in `states`; `clear_status` = false keeps what an
 // earlier pass of the same call reported in the status word.
+// Complex x runs as two real passes (see run_fwd_complex); for those, `recs` gives the decay
+// records' location when they do not follow the H tiles of `states`, `crot` multiplies C as it is
+// read and `y_accum` adds y to what y holds instead of storing it.
 int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st,
             const void* h0 = nullptr, void* hT = nullptr, int G = 1, bool prep = true,
-            bool clear_status = true);
+            bool clear_status = true, const void* recs = nullptr, float2 crot = {1.f, 0.f},
+            bool y_accum = false);
 
 bool bwd_supported(const Problem& p);
 
@@ -90,10 +94,28 @@ BwdOut contiguous_bwd_out(const Problem& p, float* dx, float2* dA, float2* dB, f
 // count) every sequence runs as G independent chains (run_fwd): dhT / dh0 (and hT) then hold one
 // state per chain, and `dgam` (one complex per chain: <dhT, conj(end state)>, the chain's last
 // chunk's d Sigma term) may be passed ready-made instead of hT.
+// recs / crot as for run_fwd; `accum` adds dB, dC, ddt and dA to what they hold (the complex-x
+// second pass; dx is written as usual).
 int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void* states,
             const BwdOut& out, void* ws, cudaStream_t st, const void* hT = nullptr,
             const void* dhT = nullptr, void* dh0 = nullptr, int G = 1,
-            const void* dgam = nullptr, bool clear_status = true);
+            const void* dgam = nullptr, bool clear_status = true, const void* recs = nullptr,
+            float2 crot = {1.f, 0.f}, bool accum = false);
+
+// Complex x (x = xr + i xi) through the real-x kernels: the operator is linear in x, so
+// y = F(xr; A, B, C, dt) + F(xi; A, B, i C, dt). `states` holds both passes' H tiles and one set
+// of decay records (complex_states_bytes). The backward runs both passes' backwards (the second
+// one adding into dB, dC, ddt, dA, with dC taking conj(i) = -i of its C gradient) and
+// interleaves the two real parts of dx; its workspace adds two real dx buffers
+// (complex_bwd_workspace_bytes).
+size_t complex_states_bytes(const Problem& p);
+size_t complex_bwd_workspace_bytes(const Problem& p);
+int run_fwd_complex(const Problem& p, void* y, void* states, void* ws, cudaStream_t st);
+int run_bwd_complex(const Problem& p, const void* dy, const long long dys[4], const void* states,
+                    float2* dx, float2* dA, float2* dB, float2* dC, float* ddt, void* ws,
+                    cudaStream_t st);
+// the real-x view of part 0 (real) or 1 (imaginary) of a complex-x problem
+Problem real_part_view(const Problem& p, int part);
 
 // Long sequences with few of them: the hand-off chain from chunk to chunk (a few microseconds per
 // chunk) bounds the time, not the work. tc_long.cu then runs every sequence as G chains in two

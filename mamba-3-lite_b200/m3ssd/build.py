@@ -2,6 +2,7 @@
 
     python mamba-3-lite_b200/m3ssd/build.py            # build if sources are newer
     python mamba-3-lite_b200/m3ssd/build.py --force
+    python mamba-3-lite_b200/m3ssd/build.py --trace    # measurement build (m3ssd.trace)
 
 The shared library is written next to this file (``m3ssd/libm3ssd.so``) so it travels with the
 source tree; the CUDA runtime is linked statically so the library does not depend on which
@@ -24,6 +25,9 @@ INCLUDE = os.path.join(REPO, "include")
 BUILD_DIR = os.path.join(REPO, "_build")
 LIB_NAME = "libm3ssd.so"
 LIB_PATH = os.path.join(PKG, LIB_NAME)
+# measurement build: the same sources with -DM3SSD_TRACE (per-phase clock stamps of the
+# tensor-core kernels, read by m3ssd.trace); never loaded by the operator itself
+TRACE_LIB_PATH = os.path.join(PKG, "libm3ssd_trace.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
@@ -58,8 +62,8 @@ def needs_build():
     return _newest(sources() + headers() + [__file__]) > os.path.getmtime(LIB_PATH)
 
 
-def _compile(nvcc, src, extra):
-    obj = os.path.join(BUILD_DIR, os.path.basename(src) + ".o")
+def _compile(nvcc, src, extra, build_dir):
+    obj = os.path.join(build_dir, os.path.basename(src) + ".o")
     cmd = [nvcc, *NVCC_FLAGS, *extra, "-c", src, "-o", obj]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
@@ -67,25 +71,28 @@ def _compile(nvcc, src, extra):
     return obj, res.stderr
 
 
-def build(force=False, verbose=False, extra_flags=()):
-    if not force and not needs_build():
+def build(force=False, verbose=False, extra_flags=(), trace=False):
+    lib_path = TRACE_LIB_PATH if trace else LIB_PATH
+    if not force and not trace and not needs_build():
         return LIB_PATH
     nvcc = nvcc_path()
-    os.makedirs(BUILD_DIR, exist_ok=True)
+    build_dir = os.path.join(BUILD_DIR, "trace") if trace else BUILD_DIR
+    os.makedirs(build_dir, exist_ok=True)
+    flags = list(extra_flags) + (["-DM3SSD_TRACE"] if trace else [])
     srcs = sources()
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        outs = list(ex.map(lambda s: _compile(nvcc, s, list(extra_flags)), srcs))
+        outs = list(ex.map(lambda s: _compile(nvcc, s, flags, build_dir), srcs))
     if verbose:
         for _, err in outs:
             if err.strip():
                 print(err, file=sys.stderr)
-    tmp = LIB_PATH + ".tmp"
+    tmp = lib_path + ".tmp"
     cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *[o for o, _ in outs]]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":
@@ -93,7 +100,9 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true", help="print register/smem usage")
+    ap.add_argument("--trace", action="store_true",
+                    help="build the measurement library libm3ssd_trace.so (-DM3SSD_TRACE)")
     args = ap.parse_args()
     extra = ["-Xptxas", "-v"] if args.ptxas_v else []
     print(build(force=args.force or args.ptxas_v, verbose=args.verbose or args.ptxas_v,
-                extra_flags=extra))
+                extra_flags=extra, trace=args.trace))

@@ -35,6 +35,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import threading
 
 import torch
 
@@ -64,6 +65,27 @@ def _strides(t, n):
 
 def _stream_ptr(device):
     return torch.cuda.current_stream(device).cuda_stream
+
+
+# Scratch of a call (status word, ticket counter, hand-off flags and rings) is reused per
+# (device, current stream) up to this size: calls on one stream run in order, so they never use it
+# at the same time. Larger scratch, and scratch during stream capture, is allocated per call.
+_WS_CACHE_MAX = 64 << 20
+_ws_cache = {}
+_ws_lock = threading.Lock()
+
+
+def _workspace(dev, nbytes):
+    nbytes = max(int(nbytes), 256)
+    if nbytes > _WS_CACHE_MAX or torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            _ws_cache[key] = buf
+    return buf
 
 
 def _check_device_status(ws, what):
@@ -126,7 +148,7 @@ def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tens
     states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
                          device=dev)
     ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = _workspace(dev, ws_bytes)
     args = _lib.FwdArgs()
     args.prob = prob
     args.x, args.x_strides = x.data_ptr(), _lib.I64x4(*_strides(x, 4))
@@ -169,7 +191,7 @@ def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tenso
     dC = torch.empty(C_t.shape, dtype=torch.complex64, device=dev)
     ddt = torch.empty(dt.shape, dtype=torch.float32, device=dev)
     ws_bytes = int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = _workspace(dev, ws_bytes)
     args = _lib.BwdArgs()
     args.prob = prob
     args.x, args.x_strides = x.data_ptr(), _lib.I64x4(*_strides(x, 4))

@@ -27,8 +27,8 @@ import ctypes
 import torch
 
 from . import _lib
-from .ssd_complex import (_PREC, _check_device_status, _stream_ptr, _y_dtype,
-                          ssd_complex_chunkwise)
+from .ssd_complex import (_check_device_status, _PREC, ssd_complex_chunkwise, _stream_ptr,
+                          _workspace, _y_dtype)
 
 ctypes_ref = ctypes.byref
 
@@ -86,7 +86,7 @@ def ssd_proj_fwd(proj: torch.Tensor, A: torch.Tensor, H: int, D: int, N: int, ch
     states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
                          device=dev)
     ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = _workspace(dev, ws_bytes)
     args = _lib.ProjFwdArgs()
     args.prob = prob
     args.proj, args.proj_strides = proj.data_ptr(), _lib.I64x2(proj.stride(0), proj.stride(1))
@@ -123,7 +123,7 @@ def ssd_proj_bwd(dy: torch.Tensor, proj: torch.Tensor, A: torch.Tensor, states: 
     dproj = torch.empty(proj.shape, dtype=torch.float32, device=dev)
     dA = torch.empty(A.shape, dtype=torch.complex64, device=dev)
     ws_bytes = int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = _workspace(dev, ws_bytes)
     args = _lib.ProjBwdArgs()
     args.prob = prob
     args.proj, args.proj_strides = proj.data_ptr(), _lib.I64x2(proj.stride(0), proj.stride(1))

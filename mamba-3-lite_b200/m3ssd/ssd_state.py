@@ -27,8 +27,8 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .ssd_complex import (_PREC, _bf16_store_ok, _check_device_status, _check_inputs, _problem,
-                          _stream_ptr, _strides, _y_dtype)
+from .ssd_complex import (_bf16_store_ok, _check_device_status, _check_inputs, _PREC, _problem,
+                          _stream_ptr, _strides, _workspace, _y_dtype)
 
 ctypes_ref = ctypes.byref
 
@@ -63,7 +63,7 @@ def ssd_state_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torc
                          device=dev)
     hT = torch.empty(_state_shape(x, B_t), dtype=torch.complex64, device=dev)
     ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = _workspace(dev, ws_bytes)
     args = _lib.FwdArgs()
     _fill_common(args, x, A, B_t, C_t, dt, prob)
     args.y = y.data_ptr()
@@ -105,7 +105,7 @@ def ssd_state_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch
     ddt = torch.empty(dt.shape, dtype=torch.float32, device=dev)
     dh0 = torch.empty(_state_shape(x, B_t), dtype=torch.complex64, device=dev)
     ws_bytes = int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob)))
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = _workspace(dev, ws_bytes)
     args = _lib.BwdArgs()
     _fill_common(args, x, A, B_t, C_t, dt, prob)
     args.dy, args.dy_strides = dy.data_ptr(), _lib.I64x4(*_strides(dy, 4))

@@ -96,9 +96,11 @@ def test_long_few_sequences_run_as_chains(lib):
         p = prob(**kw)
         assert lib.m3ssd_launch_count(ctypes.byref(p), 0) == 4, kw
         assert lib.m3ssd_launch_count(ctypes.byref(p), 1) == 5, kw
-    # the fp32 path has no chained form
-    assert lib.m3ssd_launch_count(ctypes.byref(prob(batch=4, seqlen=16384, nheads=2, flags=0x1)),
+    # the fp32 path has no chained form, and complex x runs as two one-pass real passes
+    assert lib.m3ssd_launch_count(ctypes.byref(prob(batch=4, seqlen=16384, nheads=2, flags=0x11)),
                                   0) == lib.m3ssd_launch_count(ctypes.byref(prob(headdim=32)), 0)
+    assert lib.m3ssd_launch_count(ctypes.byref(prob(batch=4, seqlen=16384, nheads=2, flags=0x1)),
+                                  0) == 3
 
 
 def test_null_arguments_rejected_before_any_device_work(lib):
@@ -196,3 +198,32 @@ def test_cpu_tensors_raise_no_fallback():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(RuntimeError, match="not found"):
         _lib.load(str(tmp_path / "libm3ssd.so"))
+
+
+def test_complex_x_runs_as_two_tensor_core_passes(lib):
+    """Complex x at head_dim = state_dim = 64 takes the tensor-core path as two real-x passes:
+    states hold both passes' state tiles and one set of decay records, the forward launches the
+    records kernel once and the forward kernel twice, the backward two backward passes and the dx
+    interleave; precision fp32 keeps the CUDA-core path."""
+    real = prob(batch=2, seqlen=300, nheads=3)
+    cplx = prob(batch=2, seqlen=300, nheads=3, flags=_lib.M3SSD_X_COMPLEX)
+    assert lib.m3ssd_fwd_path(ctypes.byref(cplx)) == b"tcgen05-bf16x2"
+    chunks = 2 * 3 * 5
+    h_tiles = chunks * 64 * 128 * 4
+    recs = chunks * 1824
+    assert lib.m3ssd_states_bytes(ctypes.byref(real)) >= h_tiles + recs
+    assert lib.m3ssd_states_bytes(ctypes.byref(cplx)) >= 2 * h_tiles + recs
+    assert lib.m3ssd_launch_count(ctypes.byref(cplx), 0) == 3
+    assert lib.m3ssd_launch_count(ctypes.byref(cplx), 1) == 5
+    # its backward workspace holds the two real dx parts
+    dx_part = 2 * 300 * 3 * 64 * 4
+    assert lib.m3ssd_bwd_workspace_bytes(ctypes.byref(cplx)) >= 2 * dx_part
+    fp32 = prob(batch=2, seqlen=300, nheads=3, flags=_lib.M3SSD_X_COMPLEX | _lib.M3SSD_PREC_FP32)
+    assert lib.m3ssd_fwd_path(ctypes.byref(fp32)) == b"simt-fp32"
+    # the in_proj and state-carry entry points take real x only
+    a = _lib.ProjFwdArgs()
+    a.prob = cplx
+    assert lib.m3ssd_fwd_proj(ctypes.byref(a), None) == 2
+    f = _lib.FwdArgs()
+    f.prob = prob(batch=2, seqlen=256, nheads=3, flags=_lib.M3SSD_X_COMPLEX)
+    assert lib.m3ssd_fwd_state(ctypes.byref(f), None, None, None) == 2

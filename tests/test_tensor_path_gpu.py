@@ -26,8 +26,9 @@ def m3(cuda_device):
     return m3ssd
 
 
-def _inputs(dev, B, T, H, seed=0, dt_mode="raw", slow=False):
-    inp = cases.block_inputs(seed, B, T, H, 64, 64, dt_mode=dt_mode, slow_decay=slow)
+def _inputs(dev, B, T, H, seed=0, dt_mode="raw", slow=False, complex_x=False):
+    inp = cases.block_inputs(seed, B, T, H, 64, 64, dt_mode=dt_mode, slow_decay=slow,
+                             complex_x=complex_x)
     dy = cases.upstream_grad(seed, B, T, H, 64)
     t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in inp.items()}
     return t, torch.from_numpy(dy).to(dev)
@@ -56,7 +57,9 @@ def test_path_selection(m3):
     assert m3.implementation((16, 2048, 16, 64), 64)[0] == "tcgen05-bf16x2"
     assert m3.implementation((16, 2048, 16, 64), 64, precision="fp32")[0] == "simt-fp32"
     assert m3.implementation((2, 64, 2, 32), 64)[0] == "simt-fp32"
-    assert m3.implementation((2, 64, 2, 64), 64, complex_x=True)[0] == "simt-fp32"
+    # complex x: two passes of the real-x tensor-core kernels; fp32 precision stays on CUDA cores
+    assert m3.implementation((2, 64, 2, 64), 64, complex_x=True)[0] == "tcgen05-bf16x2"
+    assert m3.implementation((2, 64, 2, 64), 64, complex_x=True, precision="fp32")[0] == "simt-fp32"
 
 
 @pytest.mark.parametrize("B,T,H,dt_mode,slow", [
@@ -167,3 +170,67 @@ def test_deterministic(m3, cuda_device):
     args = [t[k] for k in KEYS]
     ys = [m3.ssd_complex_chunkwise(*args) for _ in range(3)]
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+
+
+# ---- complex x: y = F(xr; C) + F(xi; i C) through the real-x kernels, dx = dxr + i dxi
+
+@pytest.mark.parametrize("B,T,H,dt_mode,slow", [
+    (1, 64, 1, "raw", False), (2, 300, 3, "raw", False), (2, 256, 4, "literal", False),
+    (3, 1000, 5, "raw", True), (4, 2048, 16, "raw", False),
+])
+def test_complex_x_vs_fp64(m3, cuda_device, B, T, H, dt_mode, slow):
+    """Forward and all six gradients (dx complex) against the reference algorithm in complex128,
+    at the tensor-core tolerances."""
+    tol = TOL["tensor"]
+    t, dy = _inputs(cuda_device, B, T, H, seed=11, dt_mode=dt_mode, slow=slow, complex_x=True)
+    assert t["x"].dtype == torch.complex64
+    assert m3.implementation((B, T, H, 64), 64, complex_x=True) == ("tcgen05-bf16x2",) * 2
+    xs = [t[k].clone().requires_grad_(True) for k in KEYS]
+    y = m3.ssd_complex_chunkwise(*xs, precision="tensor")
+    (y * dy).sum().backward()
+    x64 = [_f64(t)[k].clone().requires_grad_(True) for k in KEYS]
+    y64 = ssd_chunkwise_torch(*x64, chunk_size=64, cdtype=torch.complex128)
+    (y64 * dy.double()).sum().backward()
+    assert torch.isfinite(y).all()
+    e, f = _rel(y, y64), _floored(y, y64)
+    print(f"complex x B{B} T{T} H{H} {dt_mode} slow={slow} y: normwise {e:.2e} floored {f:.2e}")
+    assert e < tol["y_normwise"] and f < tol["y_floored"]
+    for k, a, b in zip(GRAD_KEYS, xs, x64):
+        assert torch.isfinite(torch.view_as_real(a.grad) if a.grad.is_complex() else a.grad).all()
+        assert a.grad.dtype == (torch.complex64 if k in ("dx", "dA", "dB", "dC") else torch.float32)
+        e = _rel(a.grad, b.grad)
+        print(f"complex x B{B} T{T} H{H} {k}: normwise {e:.2e}")
+        assert e < tol["g_normwise"], (k, e)
+
+
+def test_complex_x_tensor_matches_fp32_path(m3, cuda_device):
+    """The two tensor-core passes against the CUDA-core complex-x path on the same inputs."""
+    t, dy = _inputs(cuda_device, 4, 777, 6, seed=12, complex_x=True)
+
+    def run(prec):
+        xs = [t[k].clone().requires_grad_(True) for k in KEYS]
+        y = m3.ssd_complex_chunkwise(*xs, precision=prec)
+        (y * dy).sum().backward()
+        return [y.detach()] + [v.grad for v in xs]
+
+    for k, a, b in zip(("y",) + GRAD_KEYS, run("tensor"), run("fp32")):
+        assert _rel(a, b) < (5e-5 if k == "y" else 1e-4), k
+
+
+def test_complex_x_real_part_only_equals_real_x(m3, cuda_device):
+    """A complex x with zero imaginary part gives the real-x result for y and every gradient."""
+    t, dy = _inputs(cuda_device, 2, 500, 3, seed=13)
+
+    def run(x):
+        xs = [x.clone().requires_grad_(True)] + [t[k].clone().requires_grad_(True)
+                                                 for k in KEYS[1:]]
+        y = m3.ssd_complex_chunkwise(*xs)
+        (y * dy).sum().backward()
+        return [y.detach()] + [v.grad for v in xs]
+
+    got = run(t["x"].to(torch.complex64))
+    ref = run(t["x"])
+    assert _rel(got[0], ref[0]) < 1e-6
+    assert _rel(got[1].real, ref[1]) < 1e-6  # dx real part
+    for a, b in zip(got[2:], ref[2:]):
+        assert _rel(a, b) < 1e-5
