@@ -24,7 +24,8 @@ Differences from the reference, all deliberate:
   "triton" or nothing); every value runs the CUDA kernels here.
 * ``precision`` (extra keyword) selects "auto" (default, same as "tensor"), "fp32" (CUDA cores,
   fp32 everywhere) or "tensor" (tcgen05 tensor-core tiles with split-bf16 operands and fp32
-  accumulation where the shape has them: head_dim = state_dim = 64, real x).
+  accumulation where the shape has them: head_dim = state_dim = 64; complex x runs as two
+  passes of the real-x kernels, y = F(Re x; C) + F(Im x; iC)).
 * ``y_dtype`` (extra keyword): torch.float32 (default, the reference's output) or torch.bfloat16,
   for the block whose next op (MIMO, models/mimo.py:27) runs in bf16 under autocast. The
   tensor-core kernels then round y to bf16 in their store and read its gradient as bf16, which
@@ -55,6 +56,26 @@ def _problem(x, B_t, chunk, flags):
     Bsz, T, H, D = x.shape
     N = B_t.shape[-1]
     return _lib.Problem(Bsz, T, H, D, N, int(chunk), int(flags), 0)
+
+
+_plans = {}
+
+
+def _plan(x, B_t, chunk, flags):
+    """Problem struct and buffer sizes of a call, validated once per (shape, chunk, flags)."""
+    key = (tuple(x.shape), B_t.shape[-1], int(chunk), int(flags))
+    plan = _plans.get(key)
+    if plan is None:
+        lib = _lib.load()
+        prob = _problem(x, B_t, chunk, flags)
+        _lib.check(lib.m3ssd_check_problem(ctypes_ref(prob)))
+        plan = (prob, int(lib.m3ssd_states_bytes(ctypes_ref(prob))),
+                int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob))),
+                int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob))))
+        if len(_plans) > 256:
+            _plans.clear()
+        _plans[key] = plan
+    return plan
 
 
 def _strides(t, n):
@@ -136,18 +157,13 @@ def _check_inputs(x, A, B_t, C_t, dt, chunk_size):
         raise ValueError(f"head_dim {D} / state_dim {N} exceeds the limit 256")
 
 
-@torch.library.custom_op("m3ssd::ssd_fwd", mutates_args=(), device_types="cuda")
-def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tensor,
-            dt: torch.Tensor, chunk: int, flags: int) -> tuple[torch.Tensor, torch.Tensor]:
+def _fwd_impl(x, A, B_t, C_t, dt, chunk, flags):
     lib = _lib.load()
     dev = x.device
     A = A.contiguous()
-    prob = _problem(x, B_t, chunk, flags)
-    _lib.check(lib.m3ssd_check_problem(ctypes_ref(prob)))
+    prob, states_bytes, ws_bytes, _ = _plan(x, B_t, chunk, flags)
     y = torch.empty(x.shape, dtype=_y_dtype(flags), device=dev)
-    states = torch.empty(int(lib.m3ssd_states_bytes(ctypes_ref(prob))), dtype=torch.uint8,
-                         device=dev)
-    ws_bytes = int(lib.m3ssd_fwd_workspace_bytes(ctypes_ref(prob)))
+    states = torch.empty(states_bytes, dtype=torch.uint8, device=dev)
     ws = _workspace(dev, ws_bytes)
     args = _lib.FwdArgs()
     args.prob = prob
@@ -165,6 +181,12 @@ def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tens
     return y, states
 
 
+@torch.library.custom_op("m3ssd::ssd_fwd", mutates_args=(), device_types="cuda")
+def ssd_fwd(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor, C_t: torch.Tensor,
+            dt: torch.Tensor, chunk: int, flags: int) -> tuple[torch.Tensor, torch.Tensor]:
+    return _fwd_impl(x, A, B_t, C_t, dt, chunk, flags)
+
+
 @ssd_fwd.register_fake
 def _(x, A, B_t, C_t, dt, chunk, flags):
     lib = _lib.load()
@@ -174,23 +196,18 @@ def _(x, A, B_t, C_t, dt, chunk, flags):
             torch.empty(nbytes, dtype=torch.uint8, device=x.device))
 
 
-@torch.library.custom_op("m3ssd::ssd_bwd", mutates_args=(), device_types="cuda")
-def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
-            C_t: torch.Tensor, dt: torch.Tensor, states: torch.Tensor, chunk: int,
-            flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
-                                 torch.Tensor]:
+def _bwd_impl(dy, x, A, B_t, C_t, dt, states, chunk, flags):
     lib = _lib.load()
     dev = x.device
     A = A.contiguous()
     if dy.dtype != _y_dtype(flags):
         dy = dy.to(_y_dtype(flags))
-    prob = _problem(x, B_t, chunk, flags)
+    prob, _, _, ws_bytes = _plan(x, B_t, chunk, flags)
     dx = torch.empty(x.shape, dtype=x.dtype, device=dev)
     dA = torch.empty(A.shape, dtype=torch.complex64, device=dev)
     dB = torch.empty(B_t.shape, dtype=torch.complex64, device=dev)
     dC = torch.empty(C_t.shape, dtype=torch.complex64, device=dev)
     ddt = torch.empty(dt.shape, dtype=torch.float32, device=dev)
-    ws_bytes = int(lib.m3ssd_bwd_workspace_bytes(ctypes_ref(prob)))
     ws = _workspace(dev, ws_bytes)
     args = _lib.BwdArgs()
     args.prob = prob
@@ -208,6 +225,14 @@ def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tenso
         _lib.check(lib.m3ssd_bwd(ctypes_ref(args), _stream_ptr(dev)))
     _check_device_status(ws, "backward")
     return dx, dA, dB, dC, ddt
+
+
+@torch.library.custom_op("m3ssd::ssd_bwd", mutates_args=(), device_types="cuda")
+def ssd_bwd(dy: torch.Tensor, x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
+            C_t: torch.Tensor, dt: torch.Tensor, states: torch.Tensor, chunk: int,
+            flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                 torch.Tensor]:
+    return _bwd_impl(dy, x, A, B_t, C_t, dt, states, chunk, flags)
 
 
 @ssd_bwd.register_fake
@@ -242,6 +267,25 @@ def _backward(ctx, dy, _dstates):
 ssd_fwd.register_autograd(_backward, setup_context=_setup_context)
 
 
+class _SsdFunction(torch.autograd.Function):
+    """The eager path: the same kernels as the m3ssd::ssd_fwd / ssd_bwd custom ops without the
+    op dispatch (the custom ops serve torch.compile, which traces them through register_fake)."""
+
+    @staticmethod
+    def forward(ctx, x, A, B_t, C_t, dt, chunk, flags):
+        y, states = _fwd_impl(x, A, B_t, C_t, dt, chunk, flags)
+        ctx.save_for_backward(x, A, B_t, C_t, dt, states)
+        ctx.chunk = chunk
+        ctx.flags = flags
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, A, B_t, C_t, dt, states = ctx.saved_tensors
+        dx, dA, dB, dC, ddt = _bwd_impl(dy, x, A, B_t, C_t, dt, states, ctx.chunk, ctx.flags)
+        return dx, dA, dB, dC, ddt, None, None
+
+
 def ssd_complex_chunkwise(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
                           C_t: torch.Tensor, dt: torch.Tensor, chunk_size: int = 64,
                           ssd_dispatch: str = "cuda", precision: str = "auto",
@@ -258,7 +302,10 @@ def ssd_complex_chunkwise(x: torch.Tensor, A: torch.Tensor, B_t: torch.Tensor,
     if bf16_in_kernel:
         flags |= _lib.M3SSD_Y_BF16
     with torch.autocast("cuda", enabled=False):
-        y, _ = ssd_fwd(x, A, B_t, C_t, dt, int(chunk_size), int(flags))
+        if torch.compiler.is_compiling():
+            y, _ = ssd_fwd(x, A, B_t, C_t, dt, int(chunk_size), int(flags))
+        else:
+            y = _SsdFunction.apply(x, A, B_t, C_t, dt, int(chunk_size), int(flags))
     return y.to(y_dtype) if y.dtype != y_dtype else y
 
 
