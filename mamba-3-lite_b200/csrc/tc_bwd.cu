@@ -18,7 +18,7 @@
 // carries e^{-Sigma_s}, and Gamma enters only through H_{z+1}. Nine contractions per chunk run on
 // tcgen05 (kind::f16) with split-bf16 operands stacked in groups of 8 rows (stack8) so each
 // shared buffer serves as a stacked A operand and as a plain B operand. dS_z is handed from the
-// CTA that processed chunk z+1 through a 4-slot ring in global memory (L2) with release flags.
+// CTA that processed chunk z+1 through one slot per chain in global memory (L2) with release flags.
 // Warps: 16 workers (operand transforms, epilogues, carry), one control warp (tickets, every TMA
 // and bulk copy, every MMA), one hand-off warp (the dS release and d Sigma -> ddt, dA partials).
 #include <cuda.h>
@@ -56,6 +56,11 @@ constexpr uint32_t kMiscBytes = 13312;
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBytes + 1024;
 constexpr uint32_t kLoadBytes = 64u * 128u * 4u + (uint32_t)sizeof(ChunkRec);  // C tile + record
 constexpr uint32_t kTmemCols = 512;
+// dS hand-off slots per chain. One is enough: the chunk z ticket's bulk load of dS_z has landed
+// (bar_ds) before its workers store dS_{z-1} over it, and only that ticket reads dS_z. A single
+// 32 KB slot per chain keeps the ring small enough to stay in L2 between its write and its read
+// (with four, the slots' lines were evicted and written back to DRAM: ~0.2 GB per block-shape call).
+constexpr int kRingSlots = 1;
 // TMEM columns: batch 1, batch 2, batch 3 (reusing batch-1 columns), dBb (reusing dCa)
 constexpr uint32_t COL_G = 0, COL_DM = 64, COL_Q = 128, COL_DCA = 256, COL_DCB = 384;
 constexpr uint32_t COL_DXA = 0, COL_DXB = 64, COL_DBA = 128, COL_DBB = 256;
@@ -210,9 +215,11 @@ static __device__ __noinline__ void ctl_load_ds(uint8_t* smem, Misc* m, const fl
   flag_wait(flags + (long long)q.bh * nc + q.z, err);
   fence_proxy_async_global();  // the ring was written with plain stores by another CTA
   mbar_arrive_expect_tx(&m->bar_ds, 32768u + 16u);
-  bulk_load(smem + OFF_DS, ring + ((long long)q.sg * 4 + (q.z & 3)) * 64 * 128, 32768u,
+  bulk_load(smem + OFF_DS, ring + ((long long)q.sg * kRingSlots + (q.z % kRingSlots)) * 64 * 128,
+            32768u,
             &m->bar_ds);
-  bulk_load(&m->dgam[slot], dgring + (long long)q.sg * 4 + (q.z & 3), 16u, &m->bar_ds);
+  bulk_load(&m->dgam[slot], dgring + (long long)q.sg * kRingSlots + (q.z % kRingSlots), 16u,
+            &m->bar_ds);
 }
 // TMA stores of a 64-row output tile from its 32-float staging segments (segments 0, 1 at off01,
 // 2, 3 at off23), one bulk group. hp > 0: planar complex tile, segments 0, 1 hold the real parts
@@ -436,7 +443,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           dg.x += m.dgp[ph][w].x;
           dg.y += m.dgp[ph][w].y;
         }
-        __stcg(p.dgring + (long long)q.sg * 4 + ((q.z - 1) & 3), make_float4(dg.x, dg.y, 0.f, 0.f));
+        __stcg(p.dgring + (long long)q.sg * kRingSlots + ((q.z - 1) % kRingSlots),
+               make_float4(dg.x, dg.y, 0.f, 0.f));
         // the workers' ring stores happened before their bar_ops3 arrivals
         fence_proxy_async_global();
         st_release_gpu(p.flags + (long long)q.bh * p.nc + q.z - 1, 1u);
@@ -986,7 +994,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float2 dg = make_float2(0.f, 0.f);
         if (!q.first) {
           const float2 g = rec.g;
-          float4* slot = reinterpret_cast<float4*>(p.ring + ((long long)q.sg * 4 + ((q.z - 1) & 3)) * 64 * 128);
+          float4* slot = reinterpret_cast<float4*>(
+              p.ring + ((long long)q.sg * kRingSlots + ((q.z - 1) % kRingSlots)) * 64 * 128);
           const uint32_t hb = sb + OFF_H + ((uint32_t)grp >> 1) * 8192u + 4u * q4;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -1122,8 +1131,8 @@ BwdLayout bwd_layout(const Problem& p, int G) {
   BwdLayout L;
   L.flags = 256;
   L.ring = al(L.flags + 4 * bh * nc);
-  L.dgring = al(L.ring + chains * 4 * 64 * 128 * sizeof(float));
-  L.dapart = al(L.dgring + chains * 4 * sizeof(float4));
+  L.dgring = al(L.ring + chains * kRingSlots * 64 * 128 * sizeof(float));
+  L.dapart = al(L.dgring + chains * kRingSlots * sizeof(float4));
   L.dglast = al(L.dapart + bh * nc * sizeof(float2));
   L.total = al(L.dglast + chains * sizeof(float2));
   return L;
