@@ -284,3 +284,35 @@ def test_autograd_plumbing_checkpoint_and_compile(m3, cuda_device):
     y2 = m3.ssd_complex_chunkwise(*xs2, chunk_size=32)
     (y2.sum() * 0.0).backward()
     assert all(v.grad is not None and torch.count_nonzero(v.grad) == 0 for v in xs2)
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_plain_per_element_error_vs_reference(m3, cuda_device, precision):
+    """The plain per-element relative error |got - ref| / |ref| of y (no floor), against the
+    reference's own output and against the exact recurrence, beside the reference's own plain
+    error against the exact recurrence, over every golden case whose reference output is finite
+    (the block-shape cases on their stored sample of entries). The fp32 path must be no less
+    accurate than the reference algorithm itself on that measure. The split-bf16 tensor path is
+    reported only: its relative error near y = 0 has no bound of that form (it is held to the
+    floored per-element bar and the normwise bars in the other tests)."""
+    rows = []
+    for name in cases.CASES:
+        inp, dy, chunk = cases.make_case(name)
+        g = dict(np.load(os.path.join(GOLDEN, name + ".npz")))
+        ref = np.asarray(g["y"], dtype=np.float64)
+        if not np.isfinite(ref).all():
+            continue
+        got = run_op(m3, inp, dy, chunk, precision, cuda_device, grads=False)["y"]
+        got = pick(g, name, "y", got).astype(np.float64)
+        exact = pick(g, name, "y", O.ssd_naive(**inp).real)
+        nz = (ref != 0) & (exact != 0)
+        plain = lambda a, b: float(np.max(np.abs(a[nz] - b[nz]) / np.abs(b[nz])))
+        rows.append((name, plain(got, ref), plain(got, exact), plain(ref, exact)))
+    assert rows
+    print(f"\n{precision}: case, plain rel. error vs reference, vs exact, reference vs exact")
+    for r in rows:
+        print(f"  {r[0]:14s} {r[1]:.2e} {r[2]:.2e} {r[3]:.2e}")
+    worst_ours = max(r[2] for r in rows)
+    worst_ref = max(r[3] for r in rows)
+    if precision == "fp32":
+        assert worst_ours <= worst_ref

@@ -135,9 +135,11 @@ def test_fused_matches_reference_block_fixture(m3, cuda_device):
         assert err < bar, (key, err)
 
 
-def test_fused_against_fp64_block_shape(m3, cuda_device):
-    """B4 L2048 H16: y, d(proj) and dA against the reference algorithm in complex128 on the GPU."""
-    B, T, H = 4, 2048, 16
+# B4 L2048 H16 runs in one pass; B2 L4090 H4 as chains with a ragged last chunk (the backward's
+# carry pass then reads planar C with its plain-load kernel)
+@pytest.mark.parametrize("B,T,H", [(4, 2048, 16), (2, 4090, 4)])
+def test_fused_against_fp64_block_shape(m3, cuda_device, B, T, H):
+    """y, d(proj) and dA against the reference algorithm in complex128 on the GPU."""
     proj, A, dy = _case(cuda_device, B, T, H, seed=11)
     y, gp, ga = _fused(m3, proj, A, dy, H)
     p64 = proj.double().requires_grad_(True)
@@ -160,8 +162,10 @@ def test_fused_against_fp64_block_shape(m3, cuda_device):
     assert rel(ga, a64.grad) < tol["g_normwise"]
 
 
-# T = 4096 (8 sequences of 64 chunks) runs as chains: the carry pass reads dy as bf16 there too
-@pytest.mark.parametrize("T,fused", [(2048, True), (200, True), (200, False), (4096, True)])
+# T = 4096 and 4090 (8 sequences of 64 chunks) run as chains: the carry pass reads dy as bf16 (and,
+# fused, C as planar tiles) with the plain-load carry kernel, 4090 with a ragged last chunk
+@pytest.mark.parametrize("T,fused", [(2048, True), (200, True), (200, False), (4096, True),
+                                     (4090, True), (4090, False)])
 def test_bf16_readout(m3, cuda_device, T, fused):
     """y_dtype=bfloat16: the kernels round y in their store and read dy as bf16. y is bit-equal to
     the fp32 result rounded, and the gradients equal those of the fp32 path fed the same (bf16)

@@ -234,3 +234,28 @@ def test_complex_x_real_part_only_equals_real_x(m3, cuda_device):
     assert _rel(got[1].real, ref[1]) < 1e-6  # dx real part
     for a, b in zip(got[2:], ref[2:]):
         assert _rel(a, b) < 1e-5
+
+
+def test_chained_ragged_bf16_dy_vs_fp64(m3, cuda_device):
+    """B2 L4090 H4 runs as chains with a ragged last chunk; with y in bf16 the backward's carry pass
+    reads dy as bf16 through its plain-load kernel. Gradients against the complex128 reference fed
+    the same (bf16-valued) upstream gradient."""
+    B, T, H = 2, 4090, 4
+    from m3ssd import _lib
+    import ctypes
+    prob = _lib.Problem(B, T, H, 64, 64, 64, _lib.M3SSD_Y_BF16, 0)
+    assert _lib.load().m3ssd_launch_count(ctypes.byref(prob), 1) > 2  # chained backward
+    tol = TOL["tensor"]
+    t, dy = _inputs(cuda_device, B, T, H, seed=14, slow=True)
+    dy16 = dy.to(torch.bfloat16)
+    xs = [t[k].clone().requires_grad_(True) for k in KEYS]
+    y = m3.ssd_complex_chunkwise(*xs, y_dtype=torch.bfloat16)
+    assert y.dtype == torch.bfloat16
+    y.backward(dy16)
+    x64 = [_f64(t)[k].clone().requires_grad_(True) for k in KEYS]
+    y64 = ssd_chunkwise_torch(*x64, chunk_size=64, cdtype=torch.complex128)
+    (y64 * dy16.double()).sum().backward()
+    for k, a, b in zip(GRAD_KEYS, xs, x64):
+        e = _rel(a.grad, b.grad)
+        print(f"chained ragged bf16 dy {k}: normwise {e:.2e}")
+        assert e < tol["g_normwise"], (k, e)
