@@ -458,36 +458,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                       sb + OFF_BX + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
                       w + 8 * jj);
     }
-    fence_proxy_async_smem();
-    tc_fence_before_sync();
-    __syncthreads();
-    if (warp == 0) M3_TRACE(iter, 10);
-    if (tid == 0) {  // Y1 = Mr x, Y2 = Re(C' H_z) as C'x conj(H)x
-      tc_fence_after_sync();
-      M3_TRACE(iter, 18);
-      const uint32_t idY1 = idesc_bf16(128, 64, 0, 1);
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_bf16_ss(tmem + COL_Y1, sdesc(sb + OFF_XT + j * 32u, 16, 1024),
-                      sdesc(sb + (hl ? OFF_XL : OFF_XH) + j * 2048u, 8192, 1024), idY1,
-                      (hl | j) != 0);
-      mma_commit(&m.bar_mma2);
-      M3_TRACE(iter, 20);
-      const uint32_t idY2 = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          mma_bf16_ss(tmem + COL_Y2, sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
-                      sdesc(sb + OFF_BX + hl * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024),
-                      idY2, (hl | j) != 0);
-      mma_commit(&m.bar_mma3);
-    }
-    if (warp == 0) M3_TRACE(iter, 11);
-
-    // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~, publish for chunk z+1
+    // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~ (S~ is done since the first
+    // MMA wait), before the barrier that starts Y1 and Y2: its gpu-scope release below then runs
+    // while the tensor core computes them instead of holding up the control warp's output
+    // epilogue
     {
       if (ctrl) m.nxt = nn;
       const float2 g = m.rec.g, ct = m.rec.ct;
@@ -533,13 +507,38 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
+    fence_proxy_async_smem();
     tc_fence_before_sync();
     __syncthreads();
     next = m.nxt;
+    if (warp == 0) M3_TRACE(iter, 10);
+    if (tid == 0) {  // Y1 = Mr x, Y2 = Re(C' H_z) as C'x conj(H)x
+      tc_fence_after_sync();
+      M3_TRACE(iter, 18);
+      const uint32_t idY1 = idesc_bf16(128, 64, 0, 1);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_ss(tmem + COL_Y1, sdesc(sb + OFF_XT + j * 32u, 16, 1024),
+                      sdesc(sb + (hl ? OFF_XL : OFF_XH) + j * 2048u, 8192, 1024), idY1,
+                      (hl | j) != 0);
+      mma_commit(&m.bar_mma2);
+      M3_TRACE(iter, 20);
+      const uint32_t idY2 = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          mma_bf16_ss(tmem + COL_Y2, sdesc(sb + OFF_CX + (j >> 2) * 16384u + (j & 3) * 32u, 16, 1024),
+                      sdesc(sb + OFF_BX + hl * 16384u + (j >> 2) * 8192u + (j & 3) * 32u, 16, 1024),
+                      idY2, (hl | j) != 0);
+      mma_commit(&m.bar_mma3);
+    }
+    if (warp == 0) M3_TRACE(iter, 11);
     if (warp == 0) M3_TRACE(iter, 12);
-    // the barrier orders every thread's H stores before this gpu-scope release. Its fence costs
-    // the control thread's warp ~1 us wherever it is placed (measured: here, after the output
-    // epilogue, or with no loads of the warp in flight); here it also publishes H_{z+1} soonest.
+    // the barrier orders every thread's H stores before this gpu-scope release (its fence holds
+    // the control thread's warp ~1 us; the Y MMAs run meanwhile)
     if (ctrl && j + 1 < (kChains ? p.seg : p.nc)) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
     if (ctrl) M3_TRACE(iter, 16);
 
