@@ -401,10 +401,10 @@ int chains_for(const Problem& p, bool backward) {
   int best_g = 1;
   for (int G = 2; G <= kMaxChains && nc / G >= 2; G *= 2) {
     if (nc % G != 0) break;  // a larger power of two does not divide nc either
-    // first pass (forward: the tensor-core pass; backward: the CUDA-core carry pass, ~35 ns of
-    // throughput per chunk, ~8 us per chunk along a chain), the tensor-core pass, the chains
-    const double first = backward ? fmax(bh * nc * 0.035, (double)(nc / G) * 8.0) + 3.0
-                                  : pass((double)(nc / G) * hop);
+    // first pass (tc_chain_state.cu: each chunk's two tiles, 48 KB, read at ~45% of HBM
+    // bandwidth, ~17 ns of throughput per chunk, ~4.5 us per chunk along a chain), the
+    // tensor-core pass, the chains
+    const double first = fmax(bh * nc * 0.017, (double)(nc / G) * 4.5) + 5.0;
     const double est = first + pass((double)(nc / G) * hop) + 10.0 + 0.5 * G;
     if (est < best) {
       best = est;
@@ -430,10 +430,20 @@ int run_fwd_chains(const Problem& p, void* y, void* states, void* ws, cudaStream
   char* base = static_cast<char*>(ws);
   float2* L = reinterpret_cast<float2*>(base + al256(fwd_workspace_bytes(p)));
   float2* S = L + (size_t)p.Bsz * p.H * G * kStateElems;
-  int rc = run_fwd(p, y, states, ws, st, nullptr, L, G, true, true);
-  if (rc != M3SSD_OK) return rc;
-  const ChunkRec* recs =
-      reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
+  ChunkRec* recs = reinterpret_cast<ChunkRec*>(static_cast<char*>(states) + states_h_bytes(p));
+  const long long* xs = p.xs;
+  if (chain_state_tc_ok(p, true, p.x, xs, 0)) {
+    // first pass as one GEMM per chain (tc_chain_state.cu), after the decay records
+    if (cudaMemsetAsync(ws, 0, 4, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
+    int rc = run_chunk_prep(p, recs, st);
+    if (rc != M3SSD_OK) return rc;
+    rc = run_chain_state(p, true, p.x, xs, 0, recs, G, L, static_cast<uint32_t*>(ws), st);
+    if (rc != M3SSD_OK) return rc;
+  } else {
+    // first pass as a tensor-core forward from zero entry states (its y is rewritten below)
+    const int rc = run_fwd(p, y, states, ws, st, nullptr, L, G, true, true);
+    if (rc != M3SSD_OK) return rc;
+  }
   k_chain_fwd<<<dim3(p.Bsz * p.H, kStateElems / 256), 256, 0, st>>>(
       recs, nc, G, static_cast<const float2*>(h0), L, S, static_cast<float2*>(hT));
   if (cudaGetLastError() != cudaSuccess) return M3SSD_ERR_LAUNCH;
@@ -453,7 +463,13 @@ int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], con
   const ChunkRec* recs =
       reinterpret_cast<const ChunkRec*>(static_cast<const char*>(states) + states_h_bytes(p));
   const CarryPassArgs ca = carry_pass_args(p, dy, dys, recs, G);
-  if (carry_tiled_ok(p, dy, dys)) {
+  // the first pass reports into the status word, which the tensor-core pass below then keeps
+  if (cudaMemsetAsync(ws, 0, 4, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
+  if (chain_state_tc_ok(p, false, dy, dys, p.y_bf16)) {
+    const int rc =
+        run_chain_state(p, false, dy, dys, p.y_bf16, recs, G, P, static_cast<uint32_t*>(ws), st);
+    if (rc != M3SSD_OK) return rc;
+  } else if (carry_tiled_ok(p, dy, dys)) {
     if (!ensure_smem_attr(reinterpret_cast<const void*>(k_chain_bwd_pass1_tiled),
                           (int)kCarryTiledSmem))
       return M3SSD_ERR_LAUNCH;
@@ -466,7 +482,7 @@ int run_bwd_chains(const Problem& p, const void* dy, const long long dys[4], con
   k_chain_dgam<<<p.Bsz * p.H * G, 256, 0, st>>>(static_cast<const float*>(states), nc, G, dE,
                                                 static_cast<const float2*>(hT), dgam);
   if (cudaGetLastError() != cudaSuccess) return M3SSD_ERR_LAUNCH;
-  return run_bwd(p, dy, dys, states, out, ws, st, nullptr, dE, nullptr, G, dgam, true);
+  return run_bwd(p, dy, dys, states, out, ws, st, nullptr, dE, nullptr, G, dgam, false);
 }
 
 }  // namespace tc

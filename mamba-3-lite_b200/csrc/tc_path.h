@@ -126,6 +126,15 @@ Problem real_part_view(const Problem& p, int part);
 int chains_for(const Problem& p, bool backward);
 size_t fwd_chains_workspace_bytes(const Problem& p, int G);
 size_t bwd_chains_workspace_bytes(const Problem& p, int G);
+// tc_chain_state.cu: the chained form's first passes on the tensor cores, one CTA per chain: the
+// end state of every chain from a zero entry state (forward: W = B, R = x) or its entry-state
+// gradient from a zero end-state gradient (backward: W = C, R = dy), written (n, p) per chain.
+// 16-byte rows of B / C (interleaved or planar) and of x / dy only (chain_state_tc_ok).
+bool chain_state_tc_ok(const Problem& p, bool forward, const void* r, const long long rs[4],
+                       int r_bf16);
+int run_chain_state(const Problem& p, bool forward, const void* r, const long long rs[4],
+                    int r_bf16, const ChunkRec* recs, int G, float2* out, uint32_t* err,
+                    cudaStream_t st);
 // the forward / backward with G chains per sequence; h0, hT, dhT, dh0 as for run_fwd / run_bwd
 // with G = 1 (one state per sequence, optional)
 int run_fwd_chains(const Problem& p, void* y, void* states, void* ws, cudaStream_t st,

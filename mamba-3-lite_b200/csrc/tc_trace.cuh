@@ -18,7 +18,7 @@ constexpr int kTraceCtas = 16, kTraceIters = 64, kTraceSlots = 48;
 
 #ifdef M3SSD_TRACE
 #define M3_TRACE_DEFINE(setter)                                                          \
-  static __device__ unsigned long long* g_m3_trace = nullptr;                            \
+  static __constant__ unsigned long long* g_m3_trace = nullptr;                          \
   extern "C" __attribute__((visibility("default"))) int setter(void* buf) {              \
     unsigned long long* p = static_cast<unsigned long long*>(buf);                       \
     return (int)cudaMemcpyToSymbol(g_m3_trace, &p, sizeof(p));                           \
