@@ -46,20 +46,33 @@ struct TileSmem {
 // one contiguous in global memory).
 template <bool A_KFAST, bool B_KFAST, class FA, class FB>
 __device__ __forceinline__ void tile_mma(float2 (&acc)[4], int K, FA fa, FB fb, TileSmem& sm) {
+  constexpr int kPer = TS * TS / NT;  // elements of each operand a thread stages per K step
   const int tid = threadIdx.x, tn = tid & 31, tm0 = tid >> 5;
+  // the next K step's operands are read into registers while the current one is multiplied
+  float2 ra[kPer], rb[kPer];
+  auto fetch = [&](int k0) {
+    const int kn = min(TS, K - k0);
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = tid + u * NT;
+      const int ka = A_KFAST ? (i % TS) : (i / TS), m = A_KFAST ? (i / TS) : (i % TS);
+      const int kb = B_KFAST ? (i % TS) : (i / TS), n = B_KFAST ? (i / TS) : (i % TS);
+      ra[u] = ka < kn ? fa(k0 + ka, m) : cz();
+      rb[u] = kb < kn ? fb(k0 + kb, n) : cz();
+    }
+  };
+  fetch(0);
   for (int k0 = 0; k0 < K; k0 += TS) {
     const int kn = min(TS, K - k0);
-    for (int i = tid; i < TS * TS; i += NT) {
-      const int k = A_KFAST ? (i % TS) : (i / TS);
-      const int m = A_KFAST ? (i / TS) : (i % TS);
-      sm.a[k][m] = (k < kn) ? fa(k0 + k, m) : cz();
-    }
-    for (int i = tid; i < TS * TS; i += NT) {
-      const int k = B_KFAST ? (i % TS) : (i / TS);
-      const int n = B_KFAST ? (i / TS) : (i % TS);
-      sm.b[k][n] = (k < kn) ? fb(k0 + k, n) : cz();
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = tid + u * NT;
+      sm.a[A_KFAST ? (i % TS) : (i / TS)][A_KFAST ? (i / TS) : (i % TS)] = ra[u];
+      sm.b[B_KFAST ? (i % TS) : (i / TS)][B_KFAST ? (i / TS) : (i % TS)] = rb[u];
     }
     __syncthreads();
+    if (k0 + TS < K) fetch(k0 + TS);
+#pragma unroll 4
     for (int k = 0; k < kn; ++k) {
       const float2 bv = sm.b[k][tn];
 #pragma unroll
@@ -79,6 +92,10 @@ __device__ __forceinline__ float2 warp_sum(float2 v) {
 }
 
 __host__ __device__ __forceinline__ int tiles(int n) { return (n + TS - 1) / TS; }
+
+// chunks per batch of loads in the two scans: a batch's loads are all issued before its stores,
+// so a thread waits on memory once per kScanBatch chunks instead of once per chunk
+constexpr int kScanBatch = 8;
 
 // ---------------------------------------------------------------------------------------------
 // within-chunk inclusive cumsum of a = softplus(dt) * A (models/ssd_complex.py:82, :89)
@@ -144,7 +161,8 @@ __global__ void __launch_bounds__(NT) k_fwd_state(Problem p, const float2* __res
 // Overwrites S_z with H_z (the state entering chunk z), equal to the decay_chunk einsum at
 // models/ssd_complex.py:98-111.
 // ---------------------------------------------------------------------------------------------
-__global__ void k_fwd_scan(Problem p, const float2* __restrict__ acs, float2* __restrict__ states) {
+__global__ void __launch_bounds__(256) k_fwd_scan(Problem p, const float2* __restrict__ acs,
+                                                  float2* __restrict__ states) {
   const int bh = blockIdx.y;
   const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= (long long)p.N * p.D) return;
@@ -152,11 +170,22 @@ __global__ void k_fwd_scan(Problem p, const float2* __restrict__ acs, float2* __
   float2* st = states + (long long)bh * p.nc * nd + e;
   const float2* ac = acs + (long long)bh * p.Tp() + (p.C - 1);
   float2 hcur = cz();
-  for (int z = 0; z < p.nc; ++z) {
-    const float2 s = st[z * nd];
-    st[z * nd] = hcur;
-    const float2 g = cexp(ac[(long long)z * p.C]);
-    hcur = cadd(cmul(g, hcur), s);
+  for (int z0 = 0; z0 < p.nc; z0 += kScanBatch) {
+    float2 s[kScanBatch], g[kScanBatch];
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      const int z = z0 + u;
+      s[u] = z < p.nc ? st[z * nd] : cz();
+      g[u] = z < p.nc ? ac[(long long)z * p.C] : cz();
+    }
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      const int z = z0 + u;
+      if (z < p.nc) {
+        st[z * nd] = hcur;
+        hcur = cadd(cmul(cexp(g[u]), hcur), s[u]);
+      }
+    }
   }
 }
 
@@ -277,8 +306,8 @@ __global__ void __launch_bounds__(256) k_bwd_scan(Problem p, const float2* __res
                                                   const float2* __restrict__ states,
                                                   float2* __restrict__ dsbuf,
                                                   float2* __restrict__ gpart) {
-  __shared__ float2 red[256];
-  const int bh = blockIdx.y;
+  __shared__ float2 red[kScanBatch][8];  // per chunk of a batch, one partial per warp (8 warps)
+  const int bh = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long nd = (long long)p.N * p.D;
   const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = e < nd;
@@ -286,23 +315,36 @@ __global__ void __launch_bounds__(256) k_bwd_scan(Problem p, const float2* __res
   float2* ds = dsbuf + (long long)bh * p.nc * nd + (valid ? e : 0);
   const float2* hz = states + (long long)bh * p.nc * nd + (valid ? e : 0);
   float2 dS = cz();
-  for (int z = p.nc - 1; z >= 0; --z) {
-    const float2 gz = cexp(ac[(long long)z * p.C]);
-    float2 q = cz(), hv = cz();
-    if (valid) {
-      q = ds[z * nd];
-      hv = hz[z * nd];
-      ds[z * nd] = dS;
+  for (int z1 = p.nc - 1; z1 >= 0; z1 -= kScanBatch) {  // chunks z1, z1 - 1, ..., z1 - 7
+    float2 q[kScanBatch], hv[kScanBatch], gz[kScanBatch];
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      const int z = z1 - u;
+      q[u] = (valid && z >= 0) ? ds[z * nd] : cz();
+      hv[u] = (valid && z >= 0) ? hz[z * nd] : cz();
+      gz[u] = z >= 0 ? ac[(long long)z * p.C] : cz();
     }
-    red[threadIdx.x] = cmul(dS, cconj(cmul(gz, hv)));
-    __syncthreads();
-    for (int o = 128; o > 0; o >>= 1) {
-      if (threadIdx.x < o) red[threadIdx.x] = cadd(red[threadIdx.x], red[threadIdx.x + o]);
-      __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      const int z = z1 - u;
+      float2 part = cz();
+      if (z >= 0) {
+        const float2 g = cexp(gz[u]);
+        if (valid) ds[z * nd] = dS;
+        part = cmul(dS, cconj(cmul(g, hv[u])));
+        dS = cadd(q[u], cmul(cconj(g), dS));
+      }
+      part = warp_sum(part);
+      if (lane == 0) red[u][warp] = part;
     }
-    if (threadIdx.x == 0) gpart[((long long)bh * p.nc + z) * gridDim.x + blockIdx.x] = red[0];
     __syncthreads();
-    dS = cadd(q, cmul(cconj(gz), dS));
+    if (threadIdx.x < kScanBatch && z1 - (int)threadIdx.x >= 0) {
+      float2 v = cz();
+#pragma unroll
+      for (int w = 0; w < 8; ++w) v = cadd(v, red[threadIdx.x][w]);
+      gpart[((long long)bh * p.nc + (z1 - (int)threadIdx.x)) * gridDim.x + blockIdx.x] = v;
+    }
+    __syncthreads();
   }
 }
 
