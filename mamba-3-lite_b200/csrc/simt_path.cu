@@ -40,11 +40,33 @@ struct TileSmem {
   float2 b[TS][TS + 1];  // [k][n]
 };
 
+// What a tile product needs of each term a * b: kFull the complex product; kBReal and kAReal a
+// product whose b (a) is real; kRe only the real part; kReBReal only the real part with b real.
+// Each drops the multiplications by a known zero or by a part nobody reads, in the same fused
+// order as cfma, so a result that is computed equals cfma's bit for bit.
+enum : int { kFull, kBReal, kAReal, kRe, kReBReal };
+template <int KIND>
+__device__ __forceinline__ void kfma(float2& acc, float2 a, float2 b) {
+  if constexpr (KIND == kFull) {
+    cfma(acc, a, b);
+  } else if constexpr (KIND == kBReal) {
+    acc.x = fmaf(a.x, b.x, acc.x);
+    acc.y = fmaf(a.y, b.x, acc.y);
+  } else if constexpr (KIND == kAReal) {
+    acc.x = fmaf(a.x, b.x, acc.x);
+    acc.y = fmaf(a.x, b.y, acc.y);
+  } else if constexpr (KIND == kRe) {
+    acc.x = fmaf(a.x, b.x, fmaf(-a.y, b.y, acc.x));
+  } else {
+    acc.x = fmaf(a.x, b.x, acc.x);
+  }
+}
+
 // acc[i] accumulates output (row tm0 + 8 i, col tn) with tn = tid % 32, tm0 = tid / 32, for
-// a TS x TS output tile: out[m][n] += sum_k fa(k, m) * fb(k, n). fa/fb return 0 outside the
-// problem. *_KFAST selects which index varies fastest across threads while staging (pick the
-// one contiguous in global memory).
-template <bool A_KFAST, bool B_KFAST, class FA, class FB>
+// a TS x TS output tile: out[m][n] += sum_k fa(k, m) * fb(k, n) (the parts KIND asks for).
+// fa/fb return 0 outside the problem. *_KFAST selects which index varies fastest across threads
+// while staging (pick the one contiguous in global memory).
+template <int KIND, bool A_KFAST, bool B_KFAST, class FA, class FB>
 __device__ __forceinline__ void tile_mma(float2 (&acc)[4], int K, FA fa, FB fb, TileSmem& sm) {
   constexpr int kPer = TS * TS / NT;  // elements of each operand a thread stages per K step
   const int tid = threadIdx.x, tn = tid & 31, tm0 = tid >> 5;
@@ -76,7 +98,7 @@ __device__ __forceinline__ void tile_mma(float2 (&acc)[4], int K, FA fa, FB fb, 
     for (int k = 0; k < kn; ++k) {
       const float2 bv = sm.b[k][tn];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) cfma(acc[i], sm.a[k][tm0 + 8 * i], bv);
+      for (int i = 0; i < 4; ++i) kfma<KIND>(acc[i], sm.a[k][tm0 + 8 * i], bv);
     }
     __syncthreads();
   }
@@ -125,6 +147,7 @@ __global__ void k_chunk_cumsum(Problem p, float2* __restrict__ acs) {
 // forward stage 1: per-chunk state S_z[n,p] = sum_s e^{Gamma - Sigma_s} B[s,n] x[s,p]
 // (models/ssd_complex.py:54 with decay_states from :90)
 // ---------------------------------------------------------------------------------------------
+template <bool XC>  // x complex
 __global__ void __launch_bounds__(NT) k_fwd_state(Problem p, const float2* __restrict__ acs,
                                                   float2* __restrict__ states) {
   __shared__ TileSmem sm;
@@ -146,7 +169,7 @@ __global__ void __launch_bounds__(NT) k_fwd_state(Problem p, const float2* __res
     const int d = p0 + j;
     return d < p.D ? ld_x(p, b, t0 + s, h, d) : cz();
   };
-  tile_mma<false, false>(acc, p.C, fa, fb, sm);
+  tile_mma<XC ? kFull : kBReal, false, false>(acc, p.C, fa, fb, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
   float2* st = states + ((long long)bh * p.nc + z) * p.N * p.D;
 #pragma unroll
@@ -194,6 +217,7 @@ __global__ void __launch_bounds__(256) k_fwd_scan(Problem p, const float2* __res
 //                               + e^{Sigma_l} sum_n C[l,n] H_z[n,p] )
 // (models/ssd_complex.py:53 and :115-119)
 // ---------------------------------------------------------------------------------------------
+template <bool XC>  // x complex; only Re(y) is formed
 __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restrict__ acs,
                                                 const float2* __restrict__ states,
                                                 float* __restrict__ y) {
@@ -218,7 +242,7 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
       const int s = s0 + j;
       return (s < p.C && n < p.N) ? ld_B(p, b, t0 + s, h, n) : cz();
     };
-    tile_mma<true, true>(accG, p.N, fa, fb, sm);
+    tile_mma<kFull, true, true>(accG, p.N, fa, fb, sm);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int l = l0 + tm0 + 8 * i, s = s0 + tn;
@@ -232,7 +256,7 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
       const int s = s0 + k, d = p0 + j;
       return (s < p.C && d < p.D) ? ld_x(p, b, t0 + s, h, d) : cz();
     };
-    tile_mma<true, false>(accY, min(TS, p.C - s0), fa2, fb2, sm);
+    tile_mma<XC ? kRe : kReBReal, true, false>(accY, min(TS, p.C - s0), fa2, fb2, sm);
   }
   if (threadIdx.x < TS) {
     const int l = l0 + threadIdx.x;
@@ -248,7 +272,7 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
     const int d = p0 + j;
     return (n < p.N && d < p.D) ? hz[(long long)d * p.N + n] : cz();
   };
-  tile_mma<true, false>(accY, p.N, fa3, fb3, sm);
+  tile_mma<kRe, true, false>(accY, p.N, fa3, fb3, sm);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int l = l0 + tm0 + 8 * i, d = p0 + tn, t = t0 + l;
@@ -289,7 +313,7 @@ __global__ void __launch_bounds__(NT) k_bwd_q(Problem p, Grad g, const float2* _
     const int d = p0 + j;
     return d < p.D ? make_float2(ld_dy(p, g, b, t0 + l, h, d), 0.f) : cz();
   };
-  tile_mma<false, false>(acc, p.C, fa, fb, sm);
+  tile_mma<kBReal, false, false>(acc, p.C, fa, fb, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
   float2* q = dsbuf + ((long long)bh * p.nc + z) * p.N * p.D;
 #pragma unroll
@@ -360,6 +384,7 @@ struct BwdBufs {
 };
 
 // Per (chunk, l-tile, s-tile): M, dM, dG, W and the row/column sums of W.
+template <bool XC>  // x complex
 __global__ void __launch_bounds__(NT) k_bwd_mm(Problem p, Grad g, const float2* __restrict__ acs,
                                                BwdBufs w) {
   __shared__ TileSmem sm;
@@ -383,7 +408,7 @@ __global__ void __launch_bounds__(NT) k_bwd_mm(Problem p, Grad g, const float2* 
       const int s = s0 + j;
       return (s < p.C && n < p.N) ? ld_B(p, b, t0 + s, h, n) : cz();
     };
-    tile_mma<true, true>(accG, p.N, fa, fb, sm);
+    tile_mma<kFull, true, true>(accG, p.N, fa, fb, sm);
     auto fa2 = [&](int d, int m) -> float2 {
       const int l = l0 + m;
       return (l < p.C && d < p.D) ? make_float2(ld_dy(p, g, b, t0 + l, h, d), 0.f) : cz();
@@ -392,7 +417,7 @@ __global__ void __launch_bounds__(NT) k_bwd_mm(Problem p, Grad g, const float2* 
       const int s = s0 + j;
       return (s < p.C && d < p.D) ? cconj(ld_x(p, b, t0 + s, h, d)) : cz();
     };
-    tile_mma<true, true>(accM, p.D, fa2, fb2, sm);
+    tile_mma<XC ? kAReal : kReBReal, true, true>(accM, p.D, fa2, fb2, sm);  // dy real
   }
   float2 colsum = cz();
 #pragma unroll
@@ -447,7 +472,7 @@ __global__ void __launch_bounds__(NT) k_bwd_dc(Problem p, Grad g, const float2* 
     const int n = n0 + j;
     return n < p.N ? cconj(ld_B(p, b, t0 + s, h, n)) : cz();
   };
-  tile_mma<true, false>(acc1, p.C, fa, fb, sm);
+  tile_mma<kFull, true, false>(acc1, p.C, fa, fb, sm);
   auto fa2 = [&](int d, int m) -> float2 {
     const int l = l0 + m;
     return l < p.C ? make_float2(ld_dy(p, g, b, t0 + l, h, d), 0.f) : cz();
@@ -456,7 +481,7 @@ __global__ void __launch_bounds__(NT) k_bwd_dc(Problem p, Grad g, const float2* 
     const int n = n0 + j;
     return n < p.N ? cconj(hz[(long long)d * p.N + n]) : cz();
   };
-  tile_mma<true, true>(acc2, p.D, fa2, fb2, sm);
+  tile_mma<kAReal, true, true>(acc2, p.D, fa2, fb2, sm);  // dy real
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -475,6 +500,7 @@ __global__ void __launch_bounds__(NT) k_bwd_dc(Problem p, Grad g, const float2* 
 }
 
 // dB[s,n] = sum_l dG[l,s] conj(C[l,n]) + conj(e^{Gamma-Sigma_s}) sum_p dS[n,p] conj(x[s,p])
+template <bool XC>  // x complex
 __global__ void __launch_bounds__(NT) k_bwd_db(Problem p, const float2* __restrict__ acs,
                                                const float2* __restrict__ dsbuf, BwdBufs w,
                                                float2* __restrict__ dB) {
@@ -497,7 +523,7 @@ __global__ void __launch_bounds__(NT) k_bwd_db(Problem p, const float2* __restri
     const int n = n0 + j;
     return n < p.N ? cconj(ld_C(p, b, t0 + l, h, n)) : cz();
   };
-  tile_mma<false, false>(acc1, p.C, fa, fb, sm);
+  tile_mma<kFull, false, false>(acc1, p.C, fa, fb, sm);
   auto fa2 = [&](int d, int m) -> float2 {
     const int s = s0 + m;
     return s < p.C ? cconj(ld_x(p, b, t0 + s, h, d)) : cz();
@@ -506,7 +532,7 @@ __global__ void __launch_bounds__(NT) k_bwd_db(Problem p, const float2* __restri
     const int n = n0 + j;
     return n < p.N ? dsz[(long long)d * p.N + n] : cz();
   };
-  tile_mma<true, true>(acc2, p.D, fa2, fb2, sm);
+  tile_mma<XC ? kFull : kAReal, true, true>(acc2, p.D, fa2, fb2, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -524,6 +550,7 @@ __global__ void __launch_bounds__(NT) k_bwd_db(Problem p, const float2* __restri
 }
 
 // dx[s,p] = sum_l conj(M[l,s]) dy[l,p] + sum_n conj(e^{Gamma-Sigma_s} B[s,n]) dS[n,p]
+template <bool XC>  // x complex (for a real x only Re(dx) is formed)
 __global__ void __launch_bounds__(NT) k_bwd_dx(Problem p, Grad g, const float2* __restrict__ acs,
                                                const float2* __restrict__ dsbuf, BwdBufs w,
                                                void* __restrict__ dx) {
@@ -550,7 +577,7 @@ __global__ void __launch_bounds__(NT) k_bwd_dx(Problem p, Grad g, const float2* 
     const int d = p0 + j;
     return d < p.D ? make_float2(ld_dy(p, g, b, t0 + l, h, d), 0.f) : cz();
   };
-  tile_mma<false, false>(acc, p.C, fa, fb, sm);
+  tile_mma<XC ? kBReal : kReBReal, false, false>(acc, p.C, fa, fb, sm);  // dy real
   auto fa2 = [&](int n, int m) -> float2 {
     const int s = s0 + m;
     return (s < p.C && n < p.N) ? cconj(cmul(es[m], ld_B(p, b, t0 + s, h, n))) : cz();
@@ -559,14 +586,14 @@ __global__ void __launch_bounds__(NT) k_bwd_dx(Problem p, Grad g, const float2* 
     const int d = p0 + j;
     return (n < p.N && d < p.D) ? dsz[(long long)d * p.N + n] : cz();
   };
-  tile_mma<true, false>(acc, p.N, fa2, fb2, sm);
+  tile_mma<XC ? kFull : kRe, true, false>(acc, p.N, fa2, fb2, sm);
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int s = s0 + tm0 + 8 * i, d = p0 + tn, t = t0 + s;
     if (s < p.C && d < p.D && t < p.T) {
       const long long o = (((long long)b * p.T + t) * p.H + h) * p.D + d;
-      if (p.x_complex) reinterpret_cast<float2*>(dx)[o] = acc[i];
+      if (XC) reinterpret_cast<float2*>(dx)[o] = acc[i];
       else reinterpret_cast<float*>(dx)[o] = acc[i].x;
     }
   }
@@ -676,11 +703,11 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   if (cudaMemsetAsync(ws, 0, kStatusBytes, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   k_chunk_cumsum<<<(unsigned)((nbhz + 127) / 128), 128, 0, st>>>(p, acs);
   const dim3 g_np((unsigned)(tiles(p.N) * tiles(p.D)), (unsigned)p.nc, (unsigned)(p.Bsz * p.H));
-  k_fwd_state<<<g_np, NT, 0, st>>>(p, acs, S);
+  (p.x_complex ? k_fwd_state<true> : k_fwd_state<false>)<<<g_np, NT, 0, st>>>(p, acs, S);
   const dim3 g_scan((unsigned)scan_blocks_for(p), (unsigned)(p.Bsz * p.H));
   k_fwd_scan<<<g_scan, 256, 0, st>>>(p, acs, S);
   const dim3 g_lp((unsigned)(tiles(p.C) * tiles(p.D)), (unsigned)p.nc, (unsigned)(p.Bsz * p.H));
-  k_fwd_out<<<g_lp, NT, 0, st>>>(p, acs, S, y);
+  (p.x_complex ? k_fwd_out<true> : k_fwd_out<false>)<<<g_lp, NT, 0, st>>>(p, acs, S, y);
   return launch_ok();
 }
 
@@ -710,10 +737,10 @@ int run_bwd(const Problem& p, const float* dy, const long long dys[4], const voi
   k_bwd_q<<<dim3((unsigned)(tiles(p.N) * tiles(p.D)), nc, bh), NT, 0, st>>>(p, g, acs, dsbuf);
   const int sb = scan_blocks_for(p);
   k_bwd_scan<<<dim3((unsigned)sb, bh), 256, 0, st>>>(p, acs, S, dsbuf, w.gpart);
-  k_bwd_mm<<<dim3((unsigned)(tiles(p.C) * tiles(p.C)), nc, bh), NT, 0, st>>>(p, g, acs, w);
+  (p.x_complex ? k_bwd_mm<true> : k_bwd_mm<false>)<<<dim3((unsigned)(tiles(p.C) * tiles(p.C)), nc, bh), NT, 0, st>>>(p, g, acs, w);
   k_bwd_dc<<<dim3((unsigned)(tiles(p.C) * tiles(p.N)), nc, bh), NT, 0, st>>>(p, g, acs, S, w, dC);
-  k_bwd_db<<<dim3((unsigned)(tiles(p.C) * tiles(p.N)), nc, bh), NT, 0, st>>>(p, acs, dsbuf, w, dB);
-  k_bwd_dx<<<dim3((unsigned)(tiles(p.C) * tiles(p.D)), nc, bh), NT, 0, st>>>(p, g, acs, dsbuf, w, dx);
+  (p.x_complex ? k_bwd_db<true> : k_bwd_db<false>)<<<dim3((unsigned)(tiles(p.C) * tiles(p.N)), nc, bh), NT, 0, st>>>(p, acs, dsbuf, w, dB);
+  (p.x_complex ? k_bwd_dx<true> : k_bwd_dx<false>)<<<dim3((unsigned)(tiles(p.C) * tiles(p.D)), nc, bh), NT, 0, st>>>(p, g, acs, dsbuf, w, dx);
   k_bwd_da<<<(unsigned)((nbhz + 127) / 128), 128, 0, st>>>(p, acs, w, sb, ddt);
   k_bwd_dA<<<(unsigned)((p.H + 127) / 128), 128, 0, st>>>(p, w.dapart, dA);
   return launch_ok();
