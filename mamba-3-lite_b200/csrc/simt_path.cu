@@ -217,6 +217,9 @@ __global__ void __launch_bounds__(256) k_fwd_scan(Problem p, const float2* __res
 //                               + e^{Sigma_l} sum_n C[l,n] H_z[n,p] )
 // (models/ssd_complex.py:53 and :115-119)
 // ---------------------------------------------------------------------------------------------
+// One CTA per (l tile, group of kOutTiles p tiles, chunk): each G tile is formed once for the
+// whole group.
+constexpr int kOutTiles = 2;
 template <bool XC>  // x complex; only Re(y) is formed
 __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restrict__ acs,
                                                 const float2* __restrict__ states,
@@ -224,13 +227,18 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
   __shared__ TileSmem sm;
   __shared__ float2 mt[TS][TS + 1];
   __shared__ float2 el[TS];
-  const int tP = tiles(p.D);
-  const int l0 = (blockIdx.x / tP) * TS, p0 = (blockIdx.x % tP) * TS;
+  const int tP = tiles(p.D), gP = (tP + kOutTiles - 1) / kOutTiles;
+  const int l0 = (blockIdx.x / gP) * TS, pt0 = (blockIdx.x % gP) * kOutTiles;
+  const int np = min(kOutTiles, tP - pt0);  // p tiles of this CTA (uniform over the block)
   const int z = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh % p.H;
   const int t0 = z * p.C;
   const float2* ac = acs + (long long)bh * p.Tp() + t0;
   const int tn = threadIdx.x & 31, tm0 = threadIdx.x >> 5;
-  float2 accY[4] = {cz(), cz(), cz(), cz()};
+  float2 accY[kOutTiles][4];
+#pragma unroll
+  for (int pt = 0; pt < kOutTiles; ++pt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) accY[pt][i] = cz();
   const int l_end = min(l0 + TS, p.C);
   for (int s0 = 0; s0 < l_end; s0 += TS) {
     float2 accG[4] = {cz(), cz(), cz(), cz()};
@@ -252,11 +260,16 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
     }
     __syncthreads();
     auto fa2 = [&](int k, int m) -> float2 { return mt[m][k]; };
-    auto fb2 = [&](int k, int j) -> float2 {
-      const int s = s0 + k, d = p0 + j;
-      return (s < p.C && d < p.D) ? ld_x(p, b, t0 + s, h, d) : cz();
-    };
-    tile_mma<XC ? kRe : kReBReal, true, false>(accY, min(TS, p.C - s0), fa2, fb2, sm);
+#pragma unroll
+    for (int pt = 0; pt < kOutTiles; ++pt) {
+      if (pt >= np) break;
+      const int p0 = (pt0 + pt) * TS;
+      auto fb2 = [&](int k, int j) -> float2 {
+        const int s = s0 + k, d = p0 + j;
+        return (s < p.C && d < p.D) ? ld_x(p, b, t0 + s, h, d) : cz();
+      };
+      tile_mma<XC ? kRe : kReBReal, true, false>(accY[pt], min(TS, p.C - s0), fa2, fb2, sm);
+    }
   }
   if (threadIdx.x < TS) {
     const int l = l0 + threadIdx.x;
@@ -268,16 +281,21 @@ __global__ void __launch_bounds__(NT) k_fwd_out(Problem p, const float2* __restr
     const int l = l0 + m;
     return (l < p.C && n < p.N) ? cmul(el[m], ld_C(p, b, t0 + l, h, n)) : cz();
   };
-  auto fb3 = [&](int n, int j) -> float2 {
-    const int d = p0 + j;
-    return (n < p.N && d < p.D) ? hz[(long long)d * p.N + n] : cz();
-  };
-  tile_mma<kRe, true, false>(accY, p.N, fa3, fb3, sm);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int l = l0 + tm0 + 8 * i, d = p0 + tn, t = t0 + l;
-    if (l < p.C && t < p.T && d < p.D)
-      y[(((long long)b * p.T + t) * p.H + h) * p.D + d] = accY[i].x;
+  for (int pt = 0; pt < kOutTiles; ++pt) {
+    if (pt >= np) break;
+    const int p0 = (pt0 + pt) * TS;
+    auto fb3 = [&](int n, int j) -> float2 {
+      const int d = p0 + j;
+      return (n < p.N && d < p.D) ? hz[(long long)d * p.N + n] : cz();
+    };
+    tile_mma<kRe, true, false>(accY[pt], p.N, fa3, fb3, sm);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int l = l0 + tm0 + 8 * i, d = p0 + tn, t = t0 + l;
+      if (l < p.C && t < p.T && d < p.D)
+        y[(((long long)b * p.T + t) * p.H + h) * p.D + d] = accY[pt][i].x;
+    }
   }
 }
 
@@ -706,7 +724,8 @@ int run_fwd(const Problem& p, float* y, void* states, void* ws, cudaStream_t st)
   (p.x_complex ? k_fwd_state<true> : k_fwd_state<false>)<<<g_np, NT, 0, st>>>(p, acs, S);
   const dim3 g_scan((unsigned)scan_blocks_for(p), (unsigned)(p.Bsz * p.H));
   k_fwd_scan<<<g_scan, 256, 0, st>>>(p, acs, S);
-  const dim3 g_lp((unsigned)(tiles(p.C) * tiles(p.D)), (unsigned)p.nc, (unsigned)(p.Bsz * p.H));
+  const dim3 g_lp((unsigned)(tiles(p.C) * ((tiles(p.D) + kOutTiles - 1) / kOutTiles)),
+                  (unsigned)p.nc, (unsigned)(p.Bsz * p.H));
   (p.x_complex ? k_fwd_out<true> : k_fwd_out<false>)<<<g_lp, NT, 0, st>>>(p, acs, S, y);
   return launch_ok();
 }
