@@ -490,7 +490,8 @@ __global__ void __launch_bounds__(NT) k_bwd_dc(Problem p, Grad g, const float2* 
     const int n = n0 + j;
     return n < p.N ? cconj(ld_B(p, b, t0 + s, h, n)) : cz();
   };
-  tile_mma<kFull, true, false>(acc1, p.C, fa, fb, sm);
+  // dG[l][s] is zero for s > l: s stops at this tile's last row
+  tile_mma<kFull, true, false>(acc1, min(p.C, l0 + TS), fa, fb, sm);
   auto fa2 = [&](int d, int m) -> float2 {
     const int l = l0 + m;
     return l < p.C ? make_float2(ld_dy(p, g, b, t0 + l, h, d), 0.f) : cz();
@@ -533,15 +534,16 @@ __global__ void __launch_bounds__(NT) k_bwd_db(Problem p, const float2* __restri
   const float2* dsz = dsbuf + cc * p.N * p.D;
   float2 acc1[4] = {cz(), cz(), cz(), cz()};
   float2 acc2[4] = {cz(), cz(), cz(), cz()};
-  auto fa = [&](int l, int m) -> float2 {
+  // dG[l][s] is zero for l < s: l starts at this tile's first row (l = s0 + k)
+  auto fa = [&](int k, int m) -> float2 {
     const int s = s0 + m;
-    return s < p.C ? w.dgbuf[(cc * p.C + l) * p.C + s] : cz();
+    return s < p.C ? w.dgbuf[(cc * p.C + s0 + k) * p.C + s] : cz();
   };
-  auto fb = [&](int l, int j) -> float2 {
+  auto fb = [&](int k, int j) -> float2 {
     const int n = n0 + j;
-    return n < p.N ? cconj(ld_C(p, b, t0 + l, h, n)) : cz();
+    return n < p.N ? cconj(ld_C(p, b, t0 + s0 + k, h, n)) : cz();
   };
-  tile_mma<kFull, false, false>(acc1, p.C, fa, fb, sm);
+  tile_mma<kFull, false, false>(acc1, p.C - s0, fa, fb, sm);
   auto fa2 = [&](int d, int m) -> float2 {
     const int s = s0 + m;
     return s < p.C ? cconj(ld_x(p, b, t0 + s, h, d)) : cz();
@@ -587,15 +589,16 @@ __global__ void __launch_bounds__(NT) k_bwd_dx(Problem p, Grad g, const float2* 
   }
   __syncthreads();
   float2 acc[4] = {cz(), cz(), cz(), cz()};
-  auto fa = [&](int l, int m) -> float2 {
+  // M[l][s] is zero for l < s: l starts at this tile's first row (l = s0 + k)
+  auto fa = [&](int k, int m) -> float2 {
     const int s = s0 + m;
-    return s < p.C ? cconj(w.mbuf[(cc * p.C + l) * p.C + s]) : cz();
+    return s < p.C ? cconj(w.mbuf[(cc * p.C + s0 + k) * p.C + s]) : cz();
   };
-  auto fb = [&](int l, int j) -> float2 {
+  auto fb = [&](int k, int j) -> float2 {
     const int d = p0 + j;
-    return d < p.D ? make_float2(ld_dy(p, g, b, t0 + l, h, d), 0.f) : cz();
+    return d < p.D ? make_float2(ld_dy(p, g, b, t0 + s0 + k, h, d), 0.f) : cz();
   };
-  tile_mma<XC ? kBReal : kReBReal, false, false>(acc, p.C, fa, fb, sm);  // dy real
+  tile_mma<XC ? kBReal : kReBReal, false, false>(acc, p.C - s0, fa, fb, sm);  // dy real
   auto fa2 = [&](int n, int m) -> float2 {
     const int s = s0 + m;
     return (s < p.C && n < p.N) ? cconj(cmul(es[m], ld_B(p, b, t0 + s, h, n))) : cz();
