@@ -383,7 +383,10 @@ __device__ __forceinline__ void combine_rows2(uint32_t ta, uint32_t tb, const fl
 
 // kPlanar: B and C arrive, and dB and dC leave, as separate real and imaginary tiles (the in_proj
 // column layout); everything else is shared
-template <bool kPlanar, bool kChains>
+// kCarryFirst: the workers form the carry (and so release dS_{z-1} to the next chunk's ticket)
+// before epilogue 1 instead of after it: for problems with few independent chains, whose time is
+// the chain of chunk-to-chunk hand-offs rather than the tickets' throughput
+template <bool kPlanar, bool kChains, bool kCarryFirst>
 __global__ void __launch_bounds__(kThreads, 1)
     k_bwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDB,
@@ -936,114 +939,125 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&m.bar1, ph, p.err, kErrMmaWait);
       if (warp == 0) M3_TRACE(it, 11);
       tc_fence_after_sync();
-      // 16x256b TMEM reads (hi / lo partial rows in one thread): rows 16 sub + 8 h + lane/4,
-      // columns s = 16 grp + 8 k + 2 (lane%4), +1; each pair leaves as one 4-byte bf16x2 word
-      // per split half and destination
-      {
-        const int q4 = lane & 3, rr = lane >> 2;
+      auto epilogue1 = [&]() {
+        // 16x256b TMEM reads (hi / lo partial rows in one thread): rows 16 sub + 8 h + lane/4,
+        // columns s = 16 grp + 8 k + 2 (lane%4), +1; each pair leaves as one 4-byte bf16x2 word
+        // per split half and destination
+        {
+          const int q4 = lane & 3, rr = lane >> 2;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float g[8], dm[8];
-          const uint32_t tl = tmem + lane_off + ((uint32_t)(16 * h) << 16) + 16u * grp;
-          tmem_ld16x256_x2(tl + COL_G, g);
-          tmem_ld16x256_x2(tl + COL_DM, dm);
+          for (int h = 0; h < 2; ++h) {
+            float g[8], dm[8];
+            const uint32_t tl = tmem + lane_off + ((uint32_t)(16 * h) << 16) + 16u * grp;
+            tmem_ld16x256_x2(tl + COL_G, g);
+            tmem_ld16x256_x2(tl + COL_DM, dm);
+            tmem_ld_wait();
+            if (warp == 0) M3_TRACE(it, 40 + 2 * h);
+            const int row = 16 * sub + 8 * h + rr;
+            const float rl = rec.rho2[row];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int s0 = 16 * grp + 8 * k + 2 * q4;
+              float mr2[2], dg2[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float L = (s0 + e <= row) ? exp2f(rl - rec.rho2[s0 + e]) : 0.f;
+                mr2[e] = L * (g[4 * k + e] + g[4 * k + 2 + e]);
+                dg2[e] = L * (dm[4 * k + e] + dm[4 * k + 2 + e]);
+              }
+              uint32_t mrh, mrl, dgh, dgl;
+              split2(mr2[0], mr2[1], mrh, mrl);
+              split2(dg2[0], dg2[1], dgh, dgl);
+              // MN-major (stacked s): k-atom s0/32, chunks 2 ((s0/8) mod 4) (hi) and +1 (lo)
+              const uint32_t ch = 2u * (((uint32_t)s0 >> 3) & 3u), off = 4u * (uint32_t)q4;
+              const uint32_t mnh = ((uint32_t)s0 >> 5) * 8192u + swz((uint32_t)row, ch) + off;
+              const uint32_t mnl = ((uint32_t)s0 >> 5) * 8192u + swz((uint32_t)row, ch + 1u) + off;
+              st_shared_u32(sb + OFF_DYT + mnh, mrh);
+              st_shared_u32(sb + OFF_DYT + mnl, mrl);
+              st_shared_u32(sb + OFF_DGM + mnh, dgh);
+              st_shared_u32(sb + OFF_DGM + mnl, dgl);
+              // K-major (stacked rows): chunk s0/8
+              const uint32_t kc = (uint32_t)s0 >> 3;
+              st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 0u), kc) + off, dgh);
+              st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 1u), kc) + off, dgl);
+            }
+            if (warp == 0) M3_TRACE(it, 41 + 2 * h);
+          }
+        }
+        warp_arrive(&m.bar_ops2, lane);
+        if (warp == 0) M3_TRACE(it, 12);
+      };
+      auto carry = [&]() {
+        // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major, the layout above),
+        // <dS_{z-1}, H_z>. Q in the 16x256b shape: rows p = 16 sub + 8 h + lane/4, complex
+        // 16 grp + 4 k + lane%4 (k = 0..3), hi and lo partial rows added in registers.
+        {
+          const uint32_t q4 = (uint32_t)lane & 3u, rr = (uint32_t)lane >> 2;
+          float qa[16], qb[16];
+          tmem_ld16x256_x4(tmem + lane_off + COL_Q + 32u * grp, qa);
+          tmem_ld16x256_x4(tmem + lane_off + (16u << 16) + COL_Q + 32u * grp, qb);
           tmem_ld_wait();
-          if (warp == 0) M3_TRACE(it, 40 + 2 * h);
-          const int row = 16 * sub + 8 * h + rr;
-          const float rl = rec.rho2[row];
+          float2 dg = make_float2(0.f, 0.f);
+          if (!q.first) {
+            const float2 g = rec.g;
+            float4* slot = reinterpret_cast<float4*>(
+                p.ring + ((long long)q.sg * kRingSlots + ((q.z - 1) % kRingSlots)) * 64 * 128);
+            const uint32_t hb = sb + OFF_H + ((uint32_t)grp >> 1) * 8192u + 4u * q4;
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int s0 = 16 * grp + 8 * k + 2 * q4;
-            float mr2[2], dg2[2];
+            for (int i = 0; i < 4; ++i) {
+              const float* qv = (i >> 1) ? qb : qa;
+              const uint32_t prow = 16u * (uint32_t)sub + 8u * ((uint32_t)i >> 1) + rr;
+              float o[4];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float L = (s0 + e <= row) ? exp2f(rl - rec.rho2[s0 + e]) : 0.f;
-              mr2[e] = L * (g[4 * k + e] + g[4 * k + 2 + e]);
-              dg2[e] = L * (dm[4 * k + e] + dm[4 * k + 2 + e]);
+              for (int u = 0; u < 2; ++u) {
+                const int k = 2 * (i & 1) + u, c = 4 * i + 2 * u;
+                const float qre = qv[4 * k] + qv[4 * k + 2], qim = qv[4 * k + 1] + qv[4 * k + 3];
+                o[2 * u] = qre + g.x * dsz[c] + g.y * dsz[c + 1];
+                o[2 * u + 1] = -qim + g.x * dsz[c + 1] - g.y * dsz[c];
+                const uint32_t off = swz(prow, 4u * ((uint32_t)grp & 1u) + (uint32_t)k);
+                const float2 h = unsplit2(ld_shared_u32(hb + off), ld_shared_u32(hb + 16384u + off));
+                dg.x += o[2 * u] * h.x - o[2 * u + 1] * h.y;
+                dg.y += o[2 * u] * h.y + o[2 * u + 1] * h.x;
+              }
+              __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
             }
-            uint32_t mrh, mrl, dgh, dgl;
-            split2(mr2[0], mr2[1], mrh, mrl);
-            split2(dg2[0], dg2[1], dgh, dgl);
-            // MN-major (stacked s): k-atom s0/32, chunks 2 ((s0/8) mod 4) (hi) and +1 (lo)
-            const uint32_t ch = 2u * (((uint32_t)s0 >> 3) & 3u), off = 4u * (uint32_t)q4;
-            const uint32_t mnh = ((uint32_t)s0 >> 5) * 8192u + swz((uint32_t)row, ch) + off;
-            const uint32_t mnl = ((uint32_t)s0 >> 5) * 8192u + swz((uint32_t)row, ch + 1u) + off;
-            st_shared_u32(sb + OFF_DYT + mnh, mrh);
-            st_shared_u32(sb + OFF_DYT + mnl, mrl);
-            st_shared_u32(sb + OFF_DGM + mnh, dgh);
-            st_shared_u32(sb + OFF_DGM + mnl, dgl);
-            // K-major (stacked rows): chunk s0/8
-            const uint32_t kc = (uint32_t)s0 >> 3;
-            st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 0u), kc) + off, dgh);
-            st_shared_u32(sb + OFF_DGK + swz(stack8((uint32_t)row, 1u), kc) + off, dgl);
+          } else if (p.dh0 != nullptr) {  // a chain's first chunk: dS_{z-1} is its entry state's gradient
+            const float2 g = rec.g;
+            float2* dst = p.dh0 + (long long)q.sg * 64 * 64 + 16 * sub + rr;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float* qv = (i >> 1) ? qb : qa;
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int k = 2 * (i & 1) + u, c = 4 * i + 2 * u;
+                const float qre = qv[4 * k] + qv[4 * k + 2], qim = qv[4 * k + 1] + qv[4 * k + 3];
+                const int n = 16 * grp + 4 * k + (int)q4;
+                __stcg(dst + n * 64 + 8 * (i >> 1),
+                       make_float2(qre + g.x * dsz[c] + g.y * dsz[c + 1],
+                                   -qim + g.x * dsz[c + 1] - g.y * dsz[c]));
+              }
+            }
           }
-          if (warp == 0) M3_TRACE(it, 41 + 2 * h);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
+            dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
+          }
+          if (lane == 0) m.dgp[ph][warp] = dg;
         }
+        // (back-pressure for the hand-off warp: it has finished the ticket before this one)
+        if (warp == 0) M3_TRACE(it, 13);
+        if (it > 0) mbar_wait(&m.bar_rel, (it - 1) & 1u, p.err, kErrMmaWait);
+        warp_arrive(&m.bar_ops3, lane);
+        if (warp == 0) M3_TRACE(it, 14);
+      };
+      if constexpr (kCarryFirst) {
+        carry();
+        epilogue1();
+      } else {
+        epilogue1();
+        carry();
       }
-      warp_arrive(&m.bar_ops2, lane);
-      if (warp == 0) M3_TRACE(it, 12);
-      // ---- carry: dS_{z-1} = Q + conj(e^Gamma) dS_z -> ring (thread-major, the layout above),
-      // <dS_{z-1}, H_z>. Q in the 16x256b shape: rows p = 16 sub + 8 h + lane/4, complex
-      // 16 grp + 4 k + lane%4 (k = 0..3), hi and lo partial rows added in registers.
-      {
-        const uint32_t q4 = (uint32_t)lane & 3u, rr = (uint32_t)lane >> 2;
-        float qa[16], qb[16];
-        tmem_ld16x256_x4(tmem + lane_off + COL_Q + 32u * grp, qa);
-        tmem_ld16x256_x4(tmem + lane_off + (16u << 16) + COL_Q + 32u * grp, qb);
-        tmem_ld_wait();
-        float2 dg = make_float2(0.f, 0.f);
-        if (!q.first) {
-          const float2 g = rec.g;
-          float4* slot = reinterpret_cast<float4*>(
-              p.ring + ((long long)q.sg * kRingSlots + ((q.z - 1) % kRingSlots)) * 64 * 128);
-          const uint32_t hb = sb + OFF_H + ((uint32_t)grp >> 1) * 8192u + 4u * q4;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float* qv = (i >> 1) ? qb : qa;
-            const uint32_t prow = 16u * (uint32_t)sub + 8u * ((uint32_t)i >> 1) + rr;
-            float o[4];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int k = 2 * (i & 1) + u, c = 4 * i + 2 * u;
-              const float qre = qv[4 * k] + qv[4 * k + 2], qim = qv[4 * k + 1] + qv[4 * k + 3];
-              o[2 * u] = qre + g.x * dsz[c] + g.y * dsz[c + 1];
-              o[2 * u + 1] = -qim + g.x * dsz[c + 1] - g.y * dsz[c];
-              const uint32_t off = swz(prow, 4u * ((uint32_t)grp & 1u) + (uint32_t)k);
-              const float2 h = unsplit2(ld_shared_u32(hb + off), ld_shared_u32(hb + 16384u + off));
-              dg.x += o[2 * u] * h.x - o[2 * u + 1] * h.y;
-              dg.y += o[2 * u] * h.y + o[2 * u + 1] * h.x;
-            }
-            __stcg(slot + i * kWorkers + tid, make_float4(o[0], o[1], o[2], o[3]));
-          }
-        } else if (p.dh0 != nullptr) {  // a chain's first chunk: dS_{z-1} is its entry state's gradient
-          const float2 g = rec.g;
-          float2* dst = p.dh0 + (long long)q.sg * 64 * 64 + 16 * sub + rr;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float* qv = (i >> 1) ? qb : qa;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int k = 2 * (i & 1) + u, c = 4 * i + 2 * u;
-              const float qre = qv[4 * k] + qv[4 * k + 2], qim = qv[4 * k + 1] + qv[4 * k + 3];
-              const int n = 16 * grp + 4 * k + (int)q4;
-              __stcg(dst + n * 64 + 8 * (i >> 1),
-                     make_float2(qre + g.x * dsz[c] + g.y * dsz[c + 1],
-                                 -qim + g.x * dsz[c + 1] - g.y * dsz[c]));
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          dg.x += __shfl_xor_sync(0xffffffffu, dg.x, o);
-          dg.y += __shfl_xor_sync(0xffffffffu, dg.y, o);
-        }
-        if (lane == 0) m.dgp[ph][warp] = dg;
-      }
-      // (back-pressure for the hand-off warp: it has finished the ticket before this one)
-      if (warp == 0) M3_TRACE(it, 13);
-      if (it > 0) mbar_wait(&m.bar_rel, (it - 1) & 1u, p.err, kErrMmaWait);
-      warp_arrive(&m.bar_ops3, lane);
-      if (warp == 0) M3_TRACE(it, 14);
       // the next ticket: its x and dy are prefetched at the top of the loop, during the epilogues
       mbar_wait(&m.bar_ctl, ph ^ 1u, p.err, kErrMmaWait);
       next = m.tick[(it + 1) & 1];
@@ -1240,8 +1254,14 @@ int run_bwd(const Problem& p, const void* dy, const long long dys[4], const void
   if (cudaMemsetAsync(base + keep, 0, L.ring - keep, st) != cudaSuccess) return M3SSD_ERR_LAUNCH;
   const int sms = sm_count();
   if (sms <= 0) return M3SSD_ERR_DEVICE;
-  auto kern = out.planar ? (G > 1 ? k_bwd_tc<true, true> : k_bwd_tc<true, false>)
-                         : (G > 1 ? k_bwd_tc<false, true> : k_bwd_tc<false, false>);
+  // few independent chains (sequences x chains per sequence): the chunk-to-chunk hand-offs, ~5.2 us
+  // each, take longer than the tickets' throughput (~70 ns each), so the carry goes first
+  const bool carry_first = (double)p.Bsz * p.H * G * 0.070 < 5.2;
+  auto kern = carry_first
+                  ? (out.planar ? (G > 1 ? k_bwd_tc<true, true, true> : k_bwd_tc<true, false, true>)
+                                : (G > 1 ? k_bwd_tc<false, true, true> : k_bwd_tc<false, false, true>))
+                  : (out.planar ? (G > 1 ? k_bwd_tc<true, true, false> : k_bwd_tc<true, false, false>)
+                                : (G > 1 ? k_bwd_tc<false, true, false> : k_bwd_tc<false, false, false>));
   if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kSmemBytes))
     return M3SSD_ERR_LAUNCH;
   const int grid = bp.total < sms ? bp.total : sms;
