@@ -70,7 +70,10 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs. nvidia-smi
+    reports every 100 ms, after a start-up that can take longer than a short timed region, so
+    `hold` keeps the GPU busy with untimed steps until it has reported: before the region (the
+    clock under load, read as the region starts) and after it (one more report)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -81,6 +84,7 @@ class ClockSampler:
         self.proc = None
         self.lines = []
         self.thread = None
+        self.first = None  # index of the first report under load (set by the first hold)
 
     def start(self):
         try:
@@ -98,6 +102,21 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def hold(self, step, new=1, timeout_s=5.0, batch=8):
+        """Runs untimed `step()`s (in synchronized batches, so the queue stays short) until
+        nvidia-smi has reported `new` more times, or `timeout_s` has passed."""
+        import torch
+        if self.proc is None:
+            return
+        if self.first is None:
+            self.first = len(self.lines)
+        target = len(self.lines) + new
+        t_end = time.time() + timeout_s
+        while len(self.lines) < target and time.time() < t_end:
+            for _ in range(batch):
+                step()
+            torch.cuda.synchronize()
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -108,9 +127,9 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sms, maxs, reasons = [], [], set()
+        sms, maxs, watts, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.first or 0:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -119,12 +138,17 @@ class ClockSampler:
                 maxs.append(float(parts[2]))
             except ValueError:
                 continue
+            try:
+                watts.append(float(parts[3]))
+            except ValueError:
+                pass
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sms) if sms else None,
                 "sm_max_mhz": max(maxs) if maxs else None,
-                "reasons": sorted(reasons), "samples": len(sms)}
+                "reasons": sorted(reasons), "samples": len(sms),
+                "power_w": statistics.median(watts) if watts else None}
 
 
 def make_inputs(dev, seed, B, T, H, D, N, pin=False, slow_decay=False):
@@ -226,6 +250,9 @@ def measure_long(args, dev, rank, world, shard, steps, warmup, clocks=True):
     if LONG["H"] % shard:
         raise ValueError(f"{shard} GPUs do not divide {LONG['H']} heads")
     B, T, H, D, N = LONG["B"], LONG["T"], LONG["H"] // shard, SHAPE["D"], SHAPE["N"]
+    sampler = ClockSampler(dev.index or 0) if clocks else None
+    if sampler:
+        sampler.start()  # starts up while the inputs are made
     d = make_inputs(dev, 3000 + rank, B, T, H, D, N, slow_decay=True)
     prob = _lib.Problem(B, T, H, D, N, CHUNK, 0, 0)
     launches = (lib.m3ssd_launch_count(ctypes.byref(prob), 0),
@@ -250,10 +277,8 @@ def measure_long(args, dev, rank, world, shard, steps, warmup, clocks=True):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    sampler = ClockSampler(dev.index or 0) if clocks else None
     if sampler:
-        sampler.start()
-        time.sleep(0.3)
+        sampler.hold(step, new=2)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -266,6 +291,8 @@ def measure_long(args, dev, rank, world, shard, steps, warmup, clocks=True):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    if sampler:
+        sampler.hold(step)
     clk = sampler.stop() if sampler else None
     os.environ["M3SSD_CHECK"] = "1"
     step()
@@ -576,11 +603,12 @@ def run_proj_workload(args):
 
     sampler = ClockSampler(0)
     sampler.start()
-    time.sleep(0.3)
+    sampler.hold(fused, new=2)
     ms_fused = timed(fused)
     ms_composed = timed(composed)
     ms_fused16 = timed(fused_bf16)
     ms_composed16 = timed(composed_bf16)
+    sampler.hold(fused)
     clocks = sampler.stop()
     os.environ["M3SSD_CHECK"] = "1"
     same = bool(torch.equal(fused(), composed()))
@@ -645,7 +673,9 @@ def run_trace_workload(args):
 
     sampler = ClockSampler(0)
     sampler.start()
+    sampler.hold(step, new=2)
     fwd, bwd = trace.capture(step, dev, warmup=args.warmup)
+    sampler.hold(step)
     clocks = sampler.stop()
     mhz = clocks.get("sm_mhz") or 1965.0
     line = {"workload": f"phase trace, B{B} L{T} H{H} D{D} N{N}, trace build",
@@ -707,6 +737,9 @@ def main():
     from m3ssd import dist as mdist
     if world > 1:
         mdist.init_process_group("nccl", timeout_s=120.0, device=dev)
+    # nvidia-smi starts while the inputs are made; only its reports from the first hold on count
+    sampler = ClockSampler(local)
+    sampler.start()
     m3ssd.load()
     B, T, H, D, N = (SHAPE[k] for k in ("B", "T", "H", "D", "N"))
     B = args.batch
@@ -743,9 +776,7 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
+    sampler.hold(step, new=2)  # nvidia-smi has reported twice under load
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -758,6 +789,7 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    sampler.hold(step)  # and once more after the region
     clocks = sampler.stop()
     ms = t_start.elapsed_time(t_end)
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
