@@ -160,7 +160,10 @@ __device__ __forceinline__ void split_store16(uint32_t hi_addr, uint32_t lo_addr
 
 // kPlanar: B and C tiles arrive as separate real and imaginary 64 x 64 fp32 tiles (the in_proj
 // column layout) instead of one interleaved 64 x 128 tile; everything after the transform is shared
-template <bool kPlanar, bool kChains>
+// kStateFirst: H_{z+1} is formed and released as soon as S~ and H_z are in, before epilogue 1,
+// behind a block barrier of its own (the control warp's release fence then delays its epilogue):
+// for problems with few independent chains, whose time is the chain of chunk-to-chunk hand-offs
+template <bool kPlanar, bool kChains, bool kStateFirst>
 __global__ void __launch_bounds__(kThreads, 2)
     k_fwd_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmY, const FwdParams p) {
@@ -400,11 +403,86 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
 
+    auto load_hz = [&]() {
+      // ---- H_z from the predecessor chunk (bounded wait on its release flag if not yet seen)
+      if (j > 0 && !h_early) {
+        if (h_late == 0u) flag_wait_relaxed(p.flags + (long long)bh * p.nc + z, p.err);
+        fence_acquire_gpu();
+        const float4* src =
+            reinterpret_cast<const float4*>(p.states + ((long long)bh * p.nc + z) * 64 * 128) + tid;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = __ldcg(src + i * kThreads);
+          hz[4 * i] = v.x;
+          hz[4 * i + 1] = v.y;
+          hz[4 * i + 2] = v.z;
+          hz[4 * i + 3] = v.w;
+        }
+      }
+    };
+    auto state_update = [&]() {
+      // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~ (S~ is done since the first
+      // MMA wait). In the default order it runs before the barrier that starts Y1 and Y2: its
+      // gpu-scope release then runs while the tensor core computes them instead of holding up
+      // the control warp's output epilogue
+      {
+        const float2 g = m.rec.g, ct = m.rec.ct;
+        float4* tile0 = reinterpret_cast<float4*>(p.states + (long long)bh * p.nc * 64 * 128) + tid;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float s0[16], s1[16];
+          tmem_ld16(tmem + lane_off + COL_S + 64u * wg + 16u * hh, s0);
+          tmem_ld16(tmem + lane_off + COL_S + 64u * wg + 32u + 16u * hh, s1);
+          tmem_ld_wait();
+          float hn[16];
+#pragma unroll
+          for (int c = 0; c < 16; c += 2) {
+            const float sa = part ? s0[c] : s1[c];
+            const float sbv = part ? s0[c + 1] : s1[c + 1];
+            const float ra = __shfl_xor_sync(0xffffffffu, sa, 16);
+            const float rbv = __shfl_xor_sync(0xffffffffu, sbv, 16);
+            const float sr = (part ? s1[c] : s0[c]) + ra;
+            const float si = -((part ? s1[c + 1] : s0[c + 1]) + rbv);  // B'x is conjugated
+            const int k = 16 * hh + c;
+            const float2 hv = cmulf(g, make_float2(hz[k], hz[k + 1]));
+            const float2 sv = cmulf(ct, make_float2(sr, si));
+            hn[c] = hv.x + sv.x;
+            hn[c + 1] = hv.y + sv.y;
+          }
+          if (j == 0) {  // a chain's first chunk stores its own entry state tile (the backward reads it)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              __stcg(tile0 + (long long)z * 64 * 32 + (4 * hh + i) * kThreads,
+                     make_float4(hz[16 * hh + 4 * i], hz[16 * hh + 4 * i + 1],
+                                 hz[16 * hh + 4 * i + 2], hz[16 * hh + 4 * i + 3]));
+          }
+          if (j + 1 < (kChains ? p.seg : p.nc)) {
+            float4* dst = tile0 + (long long)(z + 1) * 64 * 32;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              __stcg(dst + (4 * hh + i) * kThreads,
+                     make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
+          } else if (p.hT != nullptr) {  // the chain's end state, transposed to (n, p)
+            float2* dst = p.hT + ((long long)q.sg * 64 + 32 * wg + 16 * part + 8 * hh) * 64 + r;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) __stcg(dst + c * 64, make_float2(hn[2 * c], hn[2 * c + 1]));
+          }
+        }
+      }
+    };
     // ---- epilogue 1: Mr = exp(rho_l - rho_s) G (s <= l), split-bf16, stacked rows (over x~)
     float el_r;  // exp(rho_r), kept for the output (the record slot is refilled before it)
     mbar_wait(&m.bar_mma1, ph, p.err, kErrMmaWait);
     if (warp == 0) M3_TRACE(iter, 7);
     tc_fence_after_sync();
+    if constexpr (kStateFirst) {  // H_{z+1} out to the next chunk's ticket first
+      load_hz();
+      state_update();
+      tc_fence_before_sync();
+      __syncthreads();
+      if (ctrl && j + 1 < (kChains ? p.seg : p.nc))
+        st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+    }
     {
       float v[32];
       tmem_ld32(tmem + lane_off + COL_G + 32u * wg, v);
@@ -431,21 +509,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     int nn = 0;
     if (ctrl) nn = (int)atomicAdd(p.counter, 1u);  // next ticket; stored at the state update
 
-    // ---- H_z from the predecessor chunk (bounded wait on its release flag if not yet seen)
-    if (j > 0 && !h_early) {
-      if (h_late == 0u) flag_wait_relaxed(p.flags + (long long)bh * p.nc + z, p.err);
-      fence_acquire_gpu();
-      const float4* src =
-          reinterpret_cast<const float4*>(p.states + ((long long)bh * p.nc + z) * 64 * 128) + tid;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(src + i * kThreads);
-        hz[4 * i] = v.x;
-        hz[4 * i + 1] = v.y;
-        hz[4 * i + 2] = v.z;
-        hz[4 * i + 3] = v.w;
-      }
-    }
+    if constexpr (!kStateFirst) load_hz();
     if (warp == 0) M3_TRACE(iter, 9);
     // conj(H_z) interleaved as a K-major B operand [k-atom][p][64 k] (hi | lo), over B'x
     {
@@ -458,55 +522,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                       sb + OFF_BX + 16384u + (uint32_t)wg * 8192u + swz(r, 4 * part + jj),
                       w + 8 * jj);
     }
-    // ---- state update H_{z+1} = e^Gamma H_z + cis(theta_Gamma) S~ (S~ is done since the first
-    // MMA wait), before the barrier that starts Y1 and Y2: its gpu-scope release below then runs
-    // while the tensor core computes them instead of holding up the control warp's output
-    // epilogue
-    {
-      if (ctrl) m.nxt = nn;
-      const float2 g = m.rec.g, ct = m.rec.ct;
-      float4* tile0 = reinterpret_cast<float4*>(p.states + (long long)bh * p.nc * 64 * 128) + tid;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float s0[16], s1[16];
-        tmem_ld16(tmem + lane_off + COL_S + 64u * wg + 16u * hh, s0);
-        tmem_ld16(tmem + lane_off + COL_S + 64u * wg + 32u + 16u * hh, s1);
-        tmem_ld_wait();
-        float hn[16];
-#pragma unroll
-        for (int c = 0; c < 16; c += 2) {
-          const float sa = part ? s0[c] : s1[c];
-          const float sbv = part ? s0[c + 1] : s1[c + 1];
-          const float ra = __shfl_xor_sync(0xffffffffu, sa, 16);
-          const float rbv = __shfl_xor_sync(0xffffffffu, sbv, 16);
-          const float sr = (part ? s1[c] : s0[c]) + ra;
-          const float si = -((part ? s1[c + 1] : s0[c + 1]) + rbv);  // B'x is conjugated
-          const int k = 16 * hh + c;
-          const float2 hv = cmulf(g, make_float2(hz[k], hz[k + 1]));
-          const float2 sv = cmulf(ct, make_float2(sr, si));
-          hn[c] = hv.x + sv.x;
-          hn[c + 1] = hv.y + sv.y;
-        }
-        if (j == 0) {  // a chain's first chunk stores its own entry state tile (the backward reads it)
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            __stcg(tile0 + (long long)z * 64 * 32 + (4 * hh + i) * kThreads,
-                   make_float4(hz[16 * hh + 4 * i], hz[16 * hh + 4 * i + 1],
-                               hz[16 * hh + 4 * i + 2], hz[16 * hh + 4 * i + 3]));
-        }
-        if (j + 1 < (kChains ? p.seg : p.nc)) {
-          float4* dst = tile0 + (long long)(z + 1) * 64 * 32;
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            __stcg(dst + (4 * hh + i) * kThreads,
-                   make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]));
-        } else if (p.hT != nullptr) {  // the chain's end state, transposed to (n, p)
-          float2* dst = p.hT + ((long long)q.sg * 64 + 32 * wg + 16 * part + 8 * hh) * 64 + r;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) __stcg(dst + c * 64, make_float2(hn[2 * c], hn[2 * c + 1]));
-        }
-      }
-    }
+    if (ctrl) m.nxt = nn;
+    if constexpr (!kStateFirst) state_update();
     fence_proxy_async_smem();
     tc_fence_before_sync();
     __syncthreads();
@@ -539,7 +556,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0) M3_TRACE(iter, 12);
     // the barrier orders every thread's H stores before this gpu-scope release (its fence holds
     // the control thread's warp ~1 us; the Y MMAs run meanwhile)
-    if (ctrl && j + 1 < (kChains ? p.seg : p.nc)) st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
+    if (!kStateFirst && ctrl && j + 1 < (kChains ? p.seg : p.nc))
+      st_release_gpu(p.flags + (long long)bh * p.nc + z + 1, 1u);
     if (ctrl) M3_TRACE(iter, 16);
 
     // ---- output y = Y1 + exp(rho_l) Y2 into the staging tile in sXT; the next ticket's B, C
@@ -846,8 +864,14 @@ int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, 
   }
   const int sms = sm_count();
   if (sms <= 0) return M3SSD_ERR_DEVICE;
-  auto kern = p.bc_planar ? (G > 1 ? k_fwd_tc<true, true> : k_fwd_tc<true, false>)
-                          : (G > 1 ? k_fwd_tc<false, true> : k_fwd_tc<false, false>);
+  // few independent chains (sequences x chains per sequence): the chunk-to-chunk hand-offs, ~4.3 us
+  // each, take longer than the tickets' throughput (~39 ns each), so the state goes first
+  const bool state_first = (double)p.Bsz * p.H * G * 0.039 < 4.3;
+  auto kern = state_first
+                  ? (p.bc_planar ? (G > 1 ? k_fwd_tc<true, true, true> : k_fwd_tc<true, false, true>)
+                                 : (G > 1 ? k_fwd_tc<false, true, true> : k_fwd_tc<false, false, true>))
+                  : (p.bc_planar ? (G > 1 ? k_fwd_tc<true, true, false> : k_fwd_tc<true, false, false>)
+                                 : (G > 1 ? k_fwd_tc<false, true, false> : k_fwd_tc<false, false, false>));
   if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kSmemBytes))
     return M3SSD_ERR_LAUNCH;
   const int grid = fp.total < 2 * sms ? fp.total : 2 * sms;
