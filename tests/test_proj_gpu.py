@@ -65,6 +65,7 @@ def _composed(m3, proj, A, dy, H, chunk=64):
     (1, 64, 4, 128),     # chunk 128 (the kernels block at 64; the result does not depend on it)
     (2, 1000, 8, 64),
     (1, 4096, 2, 64),    # few long sequences: both directions run as chains (planar C in the carry pass)
+    (8, 256, 16, 64),    # 128 sequences: the default kernel order (fewer run the latency-bound variants)
 ])
 def test_fused_equals_composition_bitwise(m3, cuda_device, B, T, H, chunk):
     proj, A, dy = _case(cuda_device, B, T, H, seed=B * 1000 + T)
