@@ -60,7 +60,7 @@ bool tc_shape(const m3ssd_problem* pr) {
 }
 
 // whether the tensor-core kernels take this problem's operands (B / C through TMA); complex x is
-// judged on the real-x view of its passes
+// checked on the real-x view of its passes
 bool tc_supported(const Problem& p) {
   return m3ssd::tc::fwd_supported(p.x_complex ? m3ssd::tc::real_part_view(p, 0) : p);
 }
