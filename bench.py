@@ -70,23 +70,41 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs. nvidia-smi
-    reports every 100 ms, after a start-up that can take longer than a short timed region, so
-    `hold` keeps the GPU busy with untimed steps until it has reported: before the region (the
-    clock under load, read as the region starts) and after it (one more report)."""
+    """Samples the SM clock, throttle reasons and power of one GPU around the timed region.
+
+    Through NVML (nvidia_ml_py) a background thread reads them every 2 ms, and `begin` / `end`
+    mark the region, so the samples fall inside it (a 20-step region is ~18 ms). Without NVML,
+    nvidia-smi reports every 100 ms after a start-up that can outlast a short region, so `hold`
+    keeps the GPU busy with untimed steps until it has reported before and after the region."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
         self.thread = None
-        self.first = None  # index of the first report under load (set by the first hold)
+        self.first = None  # (nvidia-smi) index of the first report under load
+        self.nvml = None
+        self.samples = []  # (NVML) (time, sm MHz, reason bits, W)
+        self.window = [None, None]
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+            self.halt = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
@@ -98,13 +116,31 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def _poll(self):
+        nv = self.nvml
+        while not self.halt.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                watts = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((time.perf_counter(), float(sm), int(bits), watts))
+            except Exception:
+                pass
+            self.halt.wait(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def begin(self):
+        self.window[0] = time.perf_counter()
+
+    def end(self):
+        self.window[1] = time.perf_counter()
+
     def hold(self, step, new=1, timeout_s=5.0, batch=8):
-        """Runs untimed `step()`s (in synchronized batches, so the queue stays short) until
-        nvidia-smi has reported `new` more times, or `timeout_s` has passed."""
+        """(nvidia-smi only) Runs untimed `step()`s, in synchronized batches so the queue stays
+        short, until nvidia-smi has reported `new` more times or `timeout_s` has passed."""
         import torch
         if self.proc is None:
             return
@@ -118,6 +154,8 @@ class ClockSampler:
             torch.cuda.synchronize()
 
     def stop(self):
+        if self.nvml is not None:
+            return self._stop_nvml()
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -128,7 +166,6 @@ class ClockSampler:
         if self.thread:
             self.thread.join(timeout=2)
         sms, maxs, watts, reasons = [], [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines[self.first or 0:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
@@ -142,13 +179,37 @@ class ClockSampler:
                 watts.append(float(parts[3]))
             except ValueError:
                 pass
-            for nm, v in zip(names, parts[5:9]):
+            for nm, v in zip(self.REASONS, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sms) if sms else None,
                 "sm_max_mhz": max(maxs) if maxs else None,
                 "reasons": sorted(reasons), "samples": len(sms),
-                "power_w": statistics.median(watts) if watts else None}
+                "power_w": statistics.median(watts) if watts else None,
+                "source": "nvidia-smi, reports next to the timed region"}
+
+    def _stop_nvml(self):
+        nv = self.nvml
+        self.halt.set()
+        self.thread.join(timeout=2)
+        t0, t1 = self.window
+        inside = [x for x in self.samples
+                  if (t0 is None or x[0] >= t0) and (t1 is None or x[0] <= t1)]
+        rows = inside or self.samples[-5:]
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted({nm for nm, b in bits.items() for x in rows if x[2] & b})
+        try:
+            nv.nvmlShutdown()
+        except Exception:
+            pass
+        return {"sm_mhz": statistics.median(x[1] for x in rows) if rows else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(rows),
+                "power_w": statistics.median(x[3] for x in rows) if rows else None,
+                "source": "NVML every 2 ms, " + ("inside the timed region" if inside
+                                                 else "last samples before the region ended")}
 
 
 def make_inputs(dev, seed, B, T, H, D, N, pin=False, slow_decay=False):
@@ -284,11 +345,15 @@ def measure_long(args, dev, rank, world, shard, steps, warmup, clocks=True):
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.begin()
     t0.record(stream)
     for _ in range(steps):
         step(timed=True)
     t1.record(stream)
     torch.cuda.synchronize()
+    if sampler:
+        sampler.end()
     if world > 1:
         dist.barrier()
     if sampler:
@@ -421,8 +486,11 @@ def measure_model(args, dev, rank, world, layers, steps, warmup, e2e_steps, cloc
     sampler = ClockSampler(dev.index or 0) if clocks else None
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        time.sleep(0.3)  # nvidia-smi's first report (the region is ~1 s)
+        sampler.begin()
     ms, loss = timed(steps, False)
+    if sampler:
+        sampler.end()
     clk = sampler.stop() if sampler else None
     e2e_ms, _ = timed(max(1, e2e_steps), True)
     ms, e2e_ms = mdist.max_over_ranks([ms, e2e_ms], device=dev)
@@ -604,10 +672,12 @@ def run_proj_workload(args):
     sampler = ClockSampler(0)
     sampler.start()
     sampler.hold(fused, new=2)
+    sampler.begin()
     ms_fused = timed(fused)
     ms_composed = timed(composed)
     ms_fused16 = timed(fused_bf16)
     ms_composed16 = timed(composed_bf16)
+    sampler.end()
     sampler.hold(fused)
     clocks = sampler.stop()
     os.environ["M3SSD_CHECK"] = "1"
@@ -674,7 +744,9 @@ def run_trace_workload(args):
     sampler = ClockSampler(0)
     sampler.start()
     sampler.hold(step, new=2)
+    sampler.begin()
     fwd, bwd = trace.capture(step, dev, warmup=args.warmup)
+    sampler.end()
     sampler.hold(step)
     clocks = sampler.stop()
     mhz = clocks.get("sm_mhz") or 1965.0
@@ -776,20 +848,22 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    sampler.hold(step, new=2)  # nvidia-smi has reported twice under load
+    sampler.hold(step, new=2)  # (nvidia-smi only) it has reported twice under load
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    sampler.begin()
     t_start.record(stream)
     for _ in range(args.steps):
         step(timed=True)
     t_end.record(stream)
     torch.cuda.synchronize()
+    sampler.end()
     if world > 1:
         dist.barrier()
-    sampler.hold(step)  # and once more after the region
+    sampler.hold(step)  # (nvidia-smi only) and once more after the region
     clocks = sampler.stop()
     ms = t_start.elapsed_time(t_end)
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
