@@ -259,3 +259,23 @@ def test_chained_ragged_bf16_dy_vs_fp64(m3, cuda_device):
         e = _rel(a.grad, b.grad)
         print(f"chained ragged bf16 dy {k}: normwise {e:.2e}")
         assert e < tol["g_normwise"], (k, e)
+
+
+def test_sequence_alone_equals_its_slice_of_a_large_batch(m3, cuda_device):
+    """Sequences are independent, so the first sequence of a batch of 32 (128 sequences: the
+    kernels' default order) and the same sequence alone (4 sequences: the order for few chains,
+    the forward's state first and the backward's carry first) get the same y, dx, dB, dC and ddt,
+    bit for bit (dA sums over the batch)."""
+    t, dy = _inputs(cuda_device, 32, 256, 4, seed=21)
+
+    def run(sl):
+        xs = [t[k][sl].detach().clone().requires_grad_(True) if k != "A" else
+              t[k].detach().clone().requires_grad_(True) for k in KEYS]
+        y = m3.ssd_complex_chunkwise(*xs, chunk_size=64)
+        y.backward(dy[sl])
+        return [y.detach()] + [xs[i].grad for i in (0, 2, 3, 4)]
+
+    full = run(slice(0, 32))
+    one = run(slice(0, 1))
+    for name, a, b in zip(("y", "dx", "dB", "dC", "ddt"), one, full):
+        assert torch.equal(a, b[0:1]), name
