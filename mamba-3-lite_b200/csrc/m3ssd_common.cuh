@@ -47,6 +47,9 @@ __device__ __forceinline__ float softplus_grad_f(float v) {
 struct Problem {
   int Bsz, T, H, D, N, C, nc;  // nc = ceil(T / C)
   int x_complex;
+  // x is one part (real or imaginary) of complex values, strides counting floats (the view a
+  // complex-x pass takes): the floats between its elements belong to the same complex tensor
+  int x_pair;
   const void* x;   long long xs[4];
   const float2* A;
   const float2* Bm; long long bs[4];

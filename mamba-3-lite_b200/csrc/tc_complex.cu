@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256) k_interleave_dx(const float4* __restrict_
 Problem real_part_view(const Problem& p, int part) {
   Problem q = p;
   q.x_complex = 0;
+  q.x_pair = 1;
   q.x = static_cast<const float*>(p.x) + part;
   for (int i = 0; i < 4; ++i) q.xs[i] = 2 * p.xs[i];  // complex strides in floats
   return q;

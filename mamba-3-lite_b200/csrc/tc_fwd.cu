@@ -70,6 +70,9 @@ struct FwdParams {
   int Bsz, T, H, nc, total;
   const float* x;
   long long xs[4];
+  // 1: 16 consecutive values of a row by four 128-bit loads. 2 or 3: x is the real (2) or the
+  // imaginary (3) part of complex values (strides of 2 floats): eight 128-bit loads of the complex
+  // pairs, keeping that part
   int x_vec;
   const ChunkRec* recs;
   float* states;
@@ -121,7 +124,7 @@ __device__ __forceinline__ void load_x16(const FwdParams& p, int b, int t, int h
     return;
   }
   const float* base = p.x + b * p.xs[0] + (long long)t * p.xs[1] + h * p.xs[2];
-  if (p.x_vec) {
+  if (p.x_vec == 1) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float4 v = ldg_nc_v4(base + p0 + 4 * i);
@@ -129,6 +132,15 @@ __device__ __forceinline__ void load_x16(const FwdParams& p, int b, int t, int h
       xv[4 * i + 1] = v.y;
       xv[4 * i + 2] = v.z;
       xv[4 * i + 3] = v.w;
+    }
+  } else if (p.x_vec >= 2) {
+    const int part = p.x_vec - 2;
+    const float* pairs = base - part + 2 * p0;  // the complex values p0 .. p0 + 15
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = ldg_nc_v4(pairs + 4 * i);
+      xv[2 * i] = part ? v.y : v.x;
+      xv[2 * i + 1] = part ? v.w : v.z;
     }
   } else {
 #pragma unroll
@@ -826,9 +838,11 @@ int run_fwd(const Problem& p, void* y, void* states, void* ws, cudaStream_t st, 
   fp.total = p.Bsz * p.H * fp.nc;
   fp.x = static_cast<const float*>(p.x);
   for (int i = 0; i < 4; ++i) fp.xs[i] = p.xs[i];
-  fp.x_vec = (p.xs[3] == 1 && p.xs[0] % 4 == 0 && p.xs[1] % 4 == 0 && p.xs[2] % 4 == 0 &&
-              reinterpret_cast<uintptr_t>(p.x) % 16 == 0)
-                 ? 1
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x);
+  const bool rows16 = p.xs[0] % 4 == 0 && p.xs[1] % 4 == 0 && p.xs[2] % 4 == 0;
+  fp.x_vec = (p.xs[3] == 1 && rows16 && xa % 16 == 0) ? 1
+             : (p.x_pair && p.xs[3] == 2 && rows16 && (xa & ~uintptr_t(4)) % 16 == 0)
+                 ? 2 + (int)((xa >> 2) & 1)
                  : 0;
   fp.states = static_cast<float*>(states);
   ChunkRec* recs = recs_in != nullptr
