@@ -765,7 +765,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", default="auto")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    # the pipeline fills and drains once per timed region (the last step's device -> host copy,
+    # ~15 ms at the block shape, runs alone): 20 steps keep that to a few percent of the region
+    ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg")
     ap.add_argument("--batch", type=int, default=SHAPE["B"],
