@@ -82,8 +82,9 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, enabled=True):
         self.gpu = gpu_index
+        self.enabled = enabled
         self.proc = None
         self.lines = []
         self.thread = None
@@ -93,6 +94,8 @@ class ClockSampler:
         self.window = [None, None]
 
     def start(self):
+        if not self.enabled:
+            return
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -154,6 +157,8 @@ class ClockSampler:
             torch.cuda.synchronize()
 
     def stop(self):
+        if not self.enabled:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         if self.nvml is not None:
             return self._stop_nvml()
         if self.proc is None:
@@ -311,7 +316,7 @@ def measure_long(args, dev, rank, world, shard, steps, warmup, clocks=True):
     if LONG["H"] % shard:
         raise ValueError(f"{shard} GPUs do not divide {LONG['H']} heads")
     B, T, H, D, N = LONG["B"], LONG["T"], LONG["H"] // shard, SHAPE["D"], SHAPE["N"]
-    sampler = ClockSampler(dev.index or 0) if clocks else None
+    sampler = ClockSampler(dev.index or 0) if clocks and rank == 0 else None
     if sampler:
         sampler.start()  # starts up while the inputs are made
     d = make_inputs(dev, 3000 + rank, B, T, H, D, N, slow_decay=True)
@@ -483,7 +488,7 @@ def measure_model(args, dev, rank, world, layers, steps, warmup, e2e_steps, cloc
     for _ in range(warmup):
         lm.train_step(net, opt, tokens, targets)
     torch.cuda.synchronize()
-    sampler = ClockSampler(dev.index or 0) if clocks else None
+    sampler = ClockSampler(dev.index or 0) if clocks and rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)  # nvidia-smi's first report (the region is ~1 s)
@@ -812,7 +817,9 @@ def main():
     if world > 1:
         mdist.init_process_group("nccl", timeout_s=120.0, device=dev)
     # nvidia-smi starts while the inputs are made; only its reports from the first hold on count
-    sampler = ClockSampler(local)
+    # rank 0 alone samples (its line reports its GPU's clocks): eight processes polling NVML every
+    # 2 ms slowed the 8-GPU step by ~15%
+    sampler = ClockSampler(local, enabled=rank == 0)
     sampler.start()
     m3ssd.load()
     B, T, H, D, N = (SHAPE[k] for k in ("B", "T", "H", "D", "N"))
